@@ -1,0 +1,428 @@
+"""Benchmark of the B200 FP8 linear hot path (one JSON line on rank 0).
+
+Workload (N=1 and per rank at N>1): BASELINE config 1, the merged QKV FP8
+projection of one H3-style block — X bf16 [32760, 4096] (N(0,1) with 0.1 %
+x20 outliers), W_qkv e4m3 [12288, 4096] (N(0,0.02), per-output-row scales),
+bias bf16 [12288], output Q, K, V bf16 [32760, 32, 128].  One step = the
+per-token e4m3 quantisation of X plus the tcgen05 GEMM whose epilogue applies
+row x column scales and bias and writes the three planes.
+
+Timing: W warm-up steps, then K steps, each bracketed by CUDA events on the
+launching stream with a 256 MB buffer written between steps to flush L2
+(outside the events); a barrier + synchronize brackets the whole timed
+region; multi-GPU value uses the max over ranks.  Tokens are independent, so
+at N GPUs every rank runs its own full workload with replicated weights
+(weak scaling, no collective on the data path).
+
+``e2e`` runs the same step through the public drop-in API
+(``RowFP8Execution("w8a8").qkv_linear``) with the input copied from pinned
+host memory and Q, K, V copied back to pinned host memory inside the timed
+region.
+
+``--impl reference`` times the reference's own CPU path for this layer
+(``RowFP8Execution("weight-only").linear``: dequantise to bf16, then
+``F.linear`` on the host cores) through the oracle's restatement, on a
+bounded row sample of the same workload.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import platform
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+import torch
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+M, K, N_QKV, HEADS = 32760, 4096, 12288, 32
+FLOP_PER_STEP = 2.0 * M * N_QKV * K
+METRIC = "FP8/NVFP4 linear TFLOP/s/GPU & % of tcgen05 peak; DiT-block linear ms at 1-8 GPU"
+WORKLOAD = "c1 merged QKV FP8: X bf16 [32760,4096] -> e4m3 per-token, W e4m3 [12288,4096], bias, Q/K/V [32760,32,128]"
+NOMINAL_FP8_TFLOPS = 4500.0
+L2_FLUSH_BYTES = 256 << 20
+
+
+def measured_peaks() -> dict:
+    path = ROOT / "MEASURED_PEAKS.json"
+    if path.exists():
+        return json.loads(path.read_text())
+    return {}
+
+
+def profile_traffic() -> float | None:
+    """Per-launch DRAM bytes of the GEMM from the committed ncu summary, if present."""
+    path = ROOT / "profiles" / "fp8_gemm_qkv_c1.txt"
+    if not path.exists():
+        return None
+    for line in path.read_text().splitlines():
+        if line.startswith("traffic_bytes_per_launch:"):
+            return float(line.split(":", 1)[1])
+    return None
+
+
+class ClockSampler:
+    """Samples SM clocks and throttle reasons with nvidia-smi during the timed region."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.QUERY}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        self.lines = []
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                out, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                out, _ = self.proc.communicate()
+            self.lines = [line for line in out.splitlines() if line.strip()]
+
+    def summary(self) -> dict:
+        clocks, max_clock, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in getattr(self, "lines", []):
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                clocks.append(float(parts[1]))
+                max_clock = float(parts[2])
+            except ValueError:
+                continue
+            for name, flag in zip(names, parts[5:9]):
+                if flag.lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(clocks) if clocks else None, "sm_max_mhz": max_clock,
+                "reasons": sorted(reasons), "samples": len(clocks)}
+
+
+def synthetic_workload(device: torch.device, rank: int):
+    """Seeded inputs of BASELINE config 1 (seeds X 1001, W 2010, bias 3001; offset by rank)."""
+    gen = torch.Generator().manual_seed(1001 + 97 * rank)
+    x = torch.randn(M, K, generator=gen)
+    count = round(0.001 * M * K)
+    idx = torch.randperm(M * K, generator=torch.Generator().manual_seed(1002 + 97 * rank))[:count]
+    x.view(-1)[idx] *= 20
+    x = x.to(torch.bfloat16)
+    w = (torch.randn(N_QKV, K, generator=torch.Generator().manual_seed(2010)) * 0.02)
+    w = w.to(torch.bfloat16).to(device)
+    # per-output-row e4m3 weight quantisation on the device with the library's
+    # own quantiser (pad_to=1): identical to the activation formula per row
+    from vflash_b200.kernels import quantize_fp8_rows
+
+    w_codes, w_scales = quantize_fp8_rows(w, pad_to=1)
+    bias = (torch.randn(N_QKV, generator=torch.Generator().manual_seed(3001)) * 0.01).to(torch.bfloat16)
+    return x, w_codes, w_scales, bias.to(device)
+
+
+def run_gpu(args) -> None:
+    from vflash_b200 import _lib
+    from vflash_b200.kernels import Epilogue, fp8_gemm, quantize_fp8_rows
+    from vflash_b200.native.h3_fp8_linear import RowFP8Execution
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    distributed = world > 1
+    if distributed:
+        import datetime
+
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local_rank)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local_rank))
+    device = torch.device("cuda", local_rank)
+    torch.cuda.set_device(device)
+
+    def barrier():
+        if distributed:
+            torch.distributed.barrier()
+        torch.cuda.synchronize(device)
+
+    x_host, w_codes, w_scales, bias = synthetic_workload(device, rank)
+    x = x_host.to(device)
+    flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=device)
+    stream = torch.cuda.current_stream(device)
+
+    def step(ev):
+        ev[0].record(stream)
+        codes, scales = quantize_fp8_rows(x)
+        ev[1].record(stream)
+        fp8_gemm(codes, scales, M, w_codes, w_scales, Epilogue(bias=bias, planes=3))
+        ev[2].record(stream)
+
+    for _ in range(args.warmup):
+        step([torch.cuda.Event(enable_timing=True) for _ in range(3)])
+    barrier()
+    events = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(args.steps)]
+    with ClockSampler(local_rank) as clocks:
+        barrier()
+        wall0 = time.perf_counter()
+        for i in range(args.steps):
+            flush.fill_(float(i))
+            step(events[i])
+        barrier()
+        wall = time.perf_counter() - wall0
+    step_ms = [e[0].elapsed_time(e[2]) for e in events]
+    quant_ms = [e[0].elapsed_time(e[1]) for e in events]
+    gemm_ms = [e[1].elapsed_time(e[2]) for e in events]
+    total_ms = sum(step_ms)
+    if distributed:
+        t = torch.tensor([total_ms], device=device)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        total_ms = t.item()
+    status = _lib.device_status(clear=True)
+
+    # ---- e2e through the public API with host buffers -----------------------
+    execution = RowFP8Execution("w8a8", activation_quantizer="triton")
+    x_pinned = x_host.pin_memory()
+    x_dev = torch.empty_like(x)
+    outs_host = [torch.empty((M, HEADS, K // HEADS), dtype=torch.bfloat16).pin_memory() for _ in range(3)]
+    w_e2e = w_codes
+
+    def e2e_step():
+        x_dev.copy_(x_pinned, non_blocking=True)
+        q, k, v = execution.qkv_linear(x_dev, w_e2e, w_scales, bias)
+        for host, plane in zip(outs_host, (q, k, v)):
+            host.copy_(plane.view(M, HEADS, K // HEADS), non_blocking=True)
+
+    for _ in range(max(1, args.warmup)):
+        e2e_step()
+    barrier()
+    e2e_steps = max(3, min(args.steps, 10))
+    s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s0.record(stream)
+    for _ in range(e2e_steps):
+        e2e_step()
+    s1.record(stream)
+    barrier()
+    e2e_ms = s0.elapsed_time(s1)
+    if distributed:
+        t = torch.tensor([e2e_ms], device=device)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        e2e_ms = t.item()
+
+    library = None
+    if rank == 0 and not args.no_library_probe:
+        library = library_fp8_probe(device)
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_baseline(x_host, w_codes.cpu(), w_scales.cpu(), bias.cpu(), args.cpu_seconds)
+
+    if distributed:
+        barrier()
+        torch.distributed.destroy_process_group()
+    if rank != 0:
+        return
+    peaks = measured_peaks()
+    if "bf16_tflops" in peaks:
+        peak = 2.0 * float(peaks["bf16_tflops"])
+        peak_src = "2 x measured cuBLAS bf16 burst (MEASURED_PEAKS.json bf16_tflops) = dense fp8 equivalent"
+    else:
+        peak = 2.0 * 1590.0
+        peak_src = "2 x fallback bf16 1.59 PFLOP/s"
+    gemm_mean = statistics.mean(gemm_ms)
+    achieved = FLOP_PER_STEP / (gemm_mean * 1e-3) / 1e12
+    value = world * args.steps * FLOP_PER_STEP / (total_ms * 1e-3) / 1e12
+    e2e_value = world * e2e_steps * FLOP_PER_STEP / (e2e_ms * 1e-3) / 1e12
+    quant_mean = statistics.mean(quant_ms)
+    quant_bytes = M * K * 2 + M * K + 32768 * 4
+    hbm = float(peaks.get("hbm_gbs", 6650.0))
+    line = {
+        "metric": METRIC,
+        "value": round(value, 2),
+        "unit": "TFLOP/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(statistics.mean(step_ms), 4),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "e4m3 x e4m3 -> fp32 acc -> bf16",
+        "data": "synthetic (seeded N(0,1) activations with 0.1% x20 outliers; N(0,0.02) weights, per-row e4m3)",
+        "config": {"workload": WORKLOAD, "M": M, "N": N_QKV, "K": K, "bias": True,
+                   "l2": "flushed between steps (256 MB buffer written outside the timed events)",
+                   "parallelism": f"token-sharded dp{world} (weights replicated)",
+                   "step": "fp8 quantiser + tcgen05 GEMM with QKV-plane epilogue"},
+        "roofline": {"bound": "tensor", "achieved": round(achieved, 1), "peak": round(peak, 1),
+                     "unit": "TFLOP/s", "frac": round(achieved / peak, 4), "traffic": profile_traffic(),
+                     "kernel": "fp8_gemm_kernel<STORE> (QKV planes)", "peak_source": peak_src,
+                     "frac_of_nominal_4500": round(achieved / NOMINAL_FP8_TFLOPS, 4),
+                     "gemm_ms": round(gemm_mean, 4)},
+        "quantiser": {"ms": round(quant_mean, 4), "gb_per_s": round(quant_bytes / (quant_mean * 1e-3) / 1e9, 1),
+                      "frac_of_measured_hbm": round(quant_bytes / (quant_mean * 1e-3) / 1e9 / hbm, 4)},
+        "e2e": {"value": round(e2e_value, 2), "unit": "TFLOP/s",
+                "h2d_bytes_per_step": M * K * 2, "d2h_bytes_per_step": 3 * M * (N_QKV // 3) * 2,
+                "api": "RowFP8Execution('w8a8').qkv_linear, pinned host in/out",
+                "ms_per_step": round(e2e_ms / e2e_steps, 3)},
+        "gpu_launches": 2 * args.steps,
+        "clocks": clocks.summary(),
+        "wall_s_timed_region": round(wall, 3),
+        "device_status": status,
+    }
+    if library is not None:
+        line["library_fp8_tflops"] = library
+    if cpu is not None:
+        line["cpu_baseline"] = cpu
+    print(json.dumps(line), flush=True)
+
+
+def library_fp8_probe(device) -> dict:
+    """cuBLASLt FP8 GEMM throughput (torch._scaled_mm, tensorwise) on this box, for context."""
+    try:
+        n = 8192
+        a = torch.randn(n, n, device=device).to(torch.float8_e4m3fn)
+        b = torch.randn(n, n, device=device).to(torch.float8_e4m3fn).t()
+        one = torch.ones((), device=device)
+        for _ in range(3):
+            torch._scaled_mm(a, b, scale_a=one, scale_b=one, out_dtype=torch.bfloat16)
+        torch.cuda.synchronize(device)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        reps = 20
+        e0.record()
+        for _ in range(reps):
+            torch._scaled_mm(a, b, scale_a=one, scale_b=one, out_dtype=torch.bfloat16)
+        e1.record()
+        torch.cuda.synchronize(device)
+        ms = e0.elapsed_time(e1) / reps
+        return {"tflops": round(2 * n**3 / (ms * 1e-3) / 1e12, 1), "shape": "8192^3 tensorwise"}
+    except Exception as exc:  # pragma: no cover - diagnostic only
+        return {"error": str(exc)[:200]}
+
+
+def cpu_threads() -> int:
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:  # pragma: no cover
+        return os.cpu_count() or 1
+
+
+def cpu_model() -> str:
+    try:
+        for line in Path("/proc/cpuinfo").read_text().splitlines():
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return platform.processor()
+
+
+def cpu_baseline(x_host, w_codes, w_scales, bias, seconds: float) -> dict:
+    """The reference's weight-only CPU path, timed on a bounded row sample."""
+    from oracle.fp8 import weight_only_linear
+
+    threads = cpu_threads()
+    torch.set_num_threads(threads)
+    rows = 1024
+    sample = x_host[:rows].contiguous()
+    weight_only_linear(sample[:16], w_codes, w_scales, bias)  # warm-up
+    reps, elapsed = 0, 0.0
+    while elapsed < seconds or reps < 1:
+        t0 = time.perf_counter()
+        weight_only_linear(sample, w_codes, w_scales, bias)
+        elapsed += time.perf_counter() - t0
+        reps += 1
+    flop = 2.0 * rows * N_QKV * K * reps
+    return {"value": round(flop / elapsed / 1e12, 4), "unit": "TFLOP/s", "cores": threads,
+            "kind": "port", "cpu": cpu_model(),
+            "sample": f"{reps} x RowFP8Execution('weight-only').linear on {rows} of {M} rows "
+                      f"(dequantise W to bf16 each call, then F.linear on bf16), {elapsed:.1f} s"}
+
+
+def run_reference(args) -> None:
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    from oracle.fp8 import weight_only_linear
+
+    threads = cpu_threads()
+    torch.set_num_threads(threads)
+    rows = args.reference_rows
+    gen = torch.Generator().manual_seed(1001)
+    x = torch.randn(rows, K, generator=gen)
+    count = round(0.001 * rows * K)
+    idx = torch.randperm(rows * K, generator=torch.Generator().manual_seed(1002))[:count]
+    x.view(-1)[idx] *= 20
+    x = x.to(torch.bfloat16)
+    w = (torch.randn(N_QKV, K, generator=torch.Generator().manual_seed(2010)) * 0.02)
+    from oracle.fp8 import quantize_weight
+
+    codes, scales = quantize_weight(w.numpy())
+    w_codes = torch.from_numpy(codes).view(torch.float8_e4m3fn)
+    w_scales = torch.from_numpy(scales)
+    bias = (torch.randn(N_QKV, generator=torch.Generator().manual_seed(3001)) * 0.01).to(torch.bfloat16)
+    for _ in range(args.warmup):
+        weight_only_linear(x, w_codes, w_scales, bias)
+    times = []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        y = weight_only_linear(x, w_codes, w_scales, bias)
+        q, k, v = y.chunk(3, dim=-1)
+        times.append(time.perf_counter() - t0)
+    total = sum(times)
+    flop = 2.0 * rows * N_QKV * K
+    value = args.steps * flop / total / 1e12
+    sample = (f"{rows} of {M} rows per step through RowFP8Execution('weight-only').linear "
+              f"(reference CPU path: dequantise W to bf16, F.linear) + chunk(3)")
+    line = {
+        "impl": "reference",
+        "metric": METRIC, "value": round(value, 4), "unit": "TFLOP/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(1e3 * total / args.steps, 3), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16 (dequantised e4m3 weights)",
+        "data": "synthetic (seeded, same generators as the GPU arm)",
+        "config": {"workload": WORKLOAD, "M": M, "N": N_QKV, "K": K, "bias": True,
+                   "sample_rows": rows, "parallelism": "host CPU"},
+        "cpu_baseline": {"value": round(value, 4), "unit": "TFLOP/s", "cores": threads,
+                         "kind": "port", "cpu": cpu_model(), "sample": sample},
+        "e2e": {"value": round(value, 4), "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main() -> None:
+    parser = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    parser.add_argument("--gpus", type=int, default=1)
+    parser.add_argument("--steps", type=int, default=20)
+    parser.add_argument("--warmup", type=int, default=5)
+    parser.add_argument("--impl", choices=["vflash_b200", "reference"], default="vflash_b200")
+    parser.add_argument("--cpu-seconds", type=float, default=10.0)
+    parser.add_argument("--reference-rows", type=int, default=1024)
+    parser.add_argument("--no-cpu-baseline", action="store_true")
+    parser.add_argument("--no-library-probe", action="store_true")
+    args = parser.parse_args()
+    args.warmup = max(3, args.warmup)  # the timing rules require >= 3 warm-up steps
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_gpu(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,131 @@
+/*
+ * vflash_b200 — C ABI of the B200 (sm_100a) quantised-linear hot path.
+ *
+ * Every entry point is stream-ordered, allocates nothing (the caller owns
+ * every buffer) and returns 0 on success or a VFB_E* code; the message of the
+ * last failure on the calling host thread is available from vfb_last_error().
+ * Pointers are CUDA device pointers of the current device unless stated.
+ * Row strides ("ld*") are in elements.  `stream` is a cudaStream_t (0 = the
+ * legacy default stream).  Shapes are validated before any launch; nothing is
+ * retried and there is no fallback arithmetic.
+ *
+ * The reference interfaces these replace live in Hansimov/vflash
+ * (paths relative to its repository root):
+ *   src/vflash/native/h3_fp8_activation.py   quantize_activation / _rows_fp8
+ *   src/vflash/native/h3_fp8_linear.py       RowFP8Execution.linear (w8a8)
+ *   src/vflash/native/h3_nvfp4_linear.py     NVFP4Execution.linear
+ *   src/vflash/native/h3_fused_ops.py        triton_strict_bf16_* epilogues
+ */
+#ifndef VFLASH_B200_H
+#define VFLASH_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define VFB_API __attribute__((visibility("default")))
+#else
+#define VFB_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes ------------------------------------------------------ */
+#define VFB_OK 0
+#define VFB_EINVAL 1      /* shape, stride, alignment or pointer rejected   */
+#define VFB_ECUDA 2       /* a CUDA runtime call failed                     */
+#define VFB_EDEVICE 3     /* current device is not compute capability 10.0  */
+#define VFB_ETIMEOUT 4    /* a kernel's bounded wait expired (device flag)  */
+
+/* Message of the last error raised on this host thread ("" if none). */
+VFB_API const char *vfb_last_error(void);
+
+/* Library version string, e.g. "vflash_b200 0.1.0 sm_100a". */
+VFB_API const char *vfb_version(void);
+
+/* Read (and optionally clear) the device-side status word of the current
+ * device.  Kernels whose bounded waits expire record VFB_ETIMEOUT there and
+ * return instead of hanging.  Synchronises the device. */
+VFB_API int vfb_device_status(int *status, int clear);
+
+/* ---- FP8 per-token activation quantisation -------------------------------
+ * Replaces quantize_activation / _rows_fp8
+ * (src/vflash/native/h3_fp8_activation.py:13-55) and the portable expression
+ * _quantize_activation_torch (src/vflash/native/h3_fp8_linear.py:18-31):
+ *   amax   = max_k |x[m,k]|                       (fp32)
+ *   scale  = amax > 0 ? max(amax / 448, FLT_MIN) : 1   (IEEE division)
+ *   codes  = e4m3_rn(clamp(x / scale, -448, 448))      (IEEE division)
+ * x: bf16 [M,K] with row stride ldx >= K.  codes: e4m3 [M_pad,K] contiguous,
+ * scales: fp32 [M_pad].  Rows M..M_pad-1 get codes 0 and scale 1.
+ * Requires 1 <= K <= 32768 and M_pad >= M. */
+VFB_API int vfb_fp8_quant_rows(const void *x, int64_t M, int64_t K, int64_t ldx,
+                       void *codes, float *scales, int64_t M_pad,
+                       void *stream);
+
+/* ---- FP8 row-scaled GEMM with fused epilogues ----------------------------
+ * Replaces torch._scaled_mm(codes, weight.t(), scale_a, scale_b.t(),
+ * out_dtype=bf16) plus the following bias add
+ * (src/vflash/native/h3_fp8_linear.py:109-121) and, per epilogue kind, the
+ * separate strict-BF16 elementwise launch that follows the linear:
+ *   y[m,n] = bf16( sa[m] * sw[n] * sum_k A[m,k] W[n,k] )     (fp32 accumulate)
+ *   y      = bf16( y + bias[n] )                    if bias != NULL
+ * then the epilogue `kind`:
+ *   VFB_EPI_STORE     out = y, optionally merged with three LoRA branches
+ *                     (triton_strict_bf16_qkv_direct_merge,
+ *                     src/vflash/native/h3_fused_ops.py:901-979):
+ *                     out = bf16(y + bf16(adapter_p[m,c] * scaling[p]))
+ *   VFB_EPI_GELU_TANH out = bf16(gelu_tanh(y))
+ *   VFB_EPI_SWIGLU    out[m,j] = bf16(v * bf16(silu(g))) with v = y[m,j] and
+ *                     g = y[m,F+j] (triton_strict_bf16_silu_mul,
+ *                     src/vflash/native/h3_fused_ops.py:185-224,660-700);
+ *                     N is the packed width 2F, the output is [M,F]
+ *   VFB_EPI_RESIDUAL  out = bf16(residual + bf16(gate[t,n] * y)) with
+ *                     t = m % tokens, or bf16(residual + y) when gate == NULL
+ *                     (triton_strict_bf16_gate_residual,
+ *                     src/vflash/native/h3_fused_ops.py:125-170,614-657)
+ * Output column n of a STORE/GELU/RESIDUAL epilogue goes to plane
+ * p = n / plane_width (plane_width = 0: one plane of width N) at
+ *   out + p * plane_stride + m * ldo + (n % plane_width),
+ * which writes the Q, K and V planes of a merged projection directly.
+ * A: e4m3 [M rows, K] with row stride lda bytes (multiple of 16); sa: [>=M].
+ * W: e4m3 [N,K] row-major with row stride ldw bytes (multiple of 16);
+ * sw: [N].  K % 16 == 0.  N % 32 == 0 (SWIGLU: F % 32 == 0).
+ * ---------------------------------------------------------------------- */
+#define VFB_EPI_STORE 0
+#define VFB_EPI_GELU_TANH 1
+#define VFB_EPI_SWIGLU 2
+#define VFB_EPI_RESIDUAL 3
+
+typedef struct vfb_epilogue {
+  int32_t kind;              /* VFB_EPI_*                                   */
+  int32_t reserved0;
+  void *out;                 /* bf16 output                                 */
+  int64_t ldo;               /* output row stride (elements)                */
+  int64_t plane_width;       /* 0 or a multiple of 32 dividing N            */
+  int64_t plane_stride;      /* elements between output planes              */
+  const void *bias;          /* bf16 [N] or NULL                            */
+  /* STORE: optional LoRA branches, one per plane (NULL = none)             */
+  const void *adapter[3];    /* bf16 [M, plane_width], row stride adapter_ld*/
+  int64_t adapter_ld;
+  float scaling[3];
+  int32_t reserved1;
+  /* RESIDUAL                                                               */
+  const void *residual;      /* bf16 [M, N], row stride ldr                 */
+  int64_t ldr;
+  const void *gate;          /* bf16 [tokens, N] strided, or NULL           */
+  int64_t gate_token_stride; /* elements                                    */
+  int64_t gate_hidden_stride;/* elements                                    */
+  int64_t tokens;            /* gate row = m % tokens                       */
+} vfb_epilogue;
+
+VFB_API int vfb_fp8_gemm(const void *A, int64_t lda, const float *sa,
+                 const void *W, int64_t ldw, const float *sw,
+                 int64_t M, int64_t N, int64_t K,
+                 const vfb_epilogue *ep, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* VFLASH_B200_H */

@@ -1,0 +1,111 @@
+"""CPU restatement of the strict-BF16 elementwise steps around the linears (test infrastructure only).
+
+Each function keeps the rounding boundaries of the reference kernel it cites
+(Hansimov/vflash, src/vflash/native/h3_fused_ops.py); inputs and outputs are
+bf16 bit patterns (uint16) so that results can be compared bit for bit.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+
+from .fp8 import bf16_bits, bf16_round, bf16_value
+
+
+def silu_f32(g: np.ndarray) -> np.ndarray:
+    g = np.asarray(g, dtype=np.float32)
+    with np.errstate(over="ignore"):
+        return (g / (np.float32(1.0) + np.exp(-g))).astype(np.float32)
+
+
+def gelu_tanh_f32(y: np.ndarray) -> np.ndarray:
+    """0.5 y (1 + tanh(sqrt(2/pi) (y + 0.044715 y^3))) in fp32."""
+    y = np.asarray(y, dtype=np.float32)
+    k_beta = np.float32(0.7978845608028654)
+    k_kappa = np.float32(0.044715)
+    cube = y * y * y
+    inner = k_beta * (y + k_kappa * cube)
+    return (np.float32(0.5) * y * (np.float32(1.0) + np.tanh(inner))).astype(np.float32)
+
+
+def silu_mul(packed_bits: np.ndarray) -> np.ndarray:
+    """``strict_silu_mul_kernel`` (h3_fused_ops.py:185-224): value * bf16(silu(gate)).
+
+    ``packed`` is [..., 2F]; value = first F columns, gate = last F.
+    """
+    packed = bf16_value(packed_bits)
+    width = packed.shape[-1] // 2
+    value, gate = packed[..., :width], packed[..., width:]
+    return bf16_bits(value * bf16_round(silu_f32(gate)))
+
+
+def gelu_tanh(y_bits: np.ndarray) -> np.ndarray:
+    """torch ``F.gelu(y, approximate="tanh")`` on a bf16 linear output."""
+    return bf16_bits(gelu_tanh_f32(bf16_value(y_bits)))
+
+
+def gate_residual(residual_bits, gate_bits, projected_bits) -> np.ndarray:
+    """``strict_gate_residual_kernel`` (h3_fused_ops.py:125-170): residual + bf16(gate * projected).
+
+    residual/projected [B,S,H]; gate [S,H] broadcast over the batch.
+    """
+    residual = bf16_value(residual_bits)
+    gate = bf16_value(gate_bits)
+    projected = bf16_value(projected_bits)
+    return bf16_bits(residual + bf16_round(gate * projected))
+
+
+def qkv_direct_merge(base_bits, adapter_bits, scalings) -> np.ndarray:
+    """``strict_qkv_direct_merge_kernel`` (h3_fused_ops.py:901-949).
+
+    base [..., 3H]; adapters 3 x [..., H]; per branch b:
+    base_b = bf16(base_b + bf16(adapter_b * scaling_b)).
+    """
+    base = bf16_value(base_bits).copy()
+    width = base.shape[-1] // 3
+    for b in range(3):
+        adapter = bf16_value(adapter_bits[b])
+        sl = slice(b * width, (b + 1) * width)
+        base[..., sl] = base[..., sl] + bf16_round(adapter * np.float32(scalings[b]))
+    return bf16_bits(base)
+
+
+def ffn_adapter_silu(base_bits, adapter_bits, scaling) -> np.ndarray:
+    """``strict_ffn_adapter_silu_kernel`` (h3_fused_ops.py:254-284).
+
+    value = bf16(base_v + bf16(adapter_v * s)), gate = bf16(base_g + bf16(adapter_g * s)),
+    out = bf16(value * bf16(silu(gate))).
+    """
+    base = bf16_value(base_bits)
+    adapter = bf16_value(adapter_bits)
+    width = base.shape[-1] // 2
+    s = np.float32(scaling)
+    value = bf16_round(base[..., :width] + bf16_round(adapter[..., :width] * s))
+    gate = bf16_round(base[..., width:] + bf16_round(adapter[..., width:] * s))
+    return bf16_bits(value * bf16_round(silu_f32(gate)))
+
+
+def adapter_merge(base_bits, adapter_bits, scalings) -> np.ndarray:
+    """``strict_adapter_merge_kernel`` (h3_fused_ops.py:298-339): base + bf16(adapter * s_branch).
+
+    ``scalings`` has one entry per equal-width branch of the last dimension.
+    """
+    base = bf16_value(base_bits)
+    adapter = bf16_value(adapter_bits)
+    branches = len(scalings)
+    width = base.shape[-1] // branches
+    scale = np.repeat(np.asarray(scalings, dtype=np.float32), width)
+    return bf16_bits(base + bf16_round(adapter * scale))
+
+
+def adapter_gate_residual(base_bits, adapter_bits, residual_bits, gate_bits, scaling) -> np.ndarray:
+    """``strict_adapter_gate_residual_kernel`` (h3_fused_ops.py:342-415).
+
+    residual + bf16(gate * bf16(base + bf16(adapter * s))).
+    """
+    base = bf16_value(base_bits)
+    adapter = bf16_value(adapter_bits)
+    residual = bf16_value(residual_bits)
+    gate = bf16_value(gate_bits)
+    adapted = bf16_round(base + bf16_round(adapter * np.float32(scaling)))
+    return bf16_bits(residual + bf16_round(gate * adapted))

@@ -1,0 +1,91 @@
+"""The C-ABI library builds, loads and exports every symbol include/vflash_b200.h declares.
+
+No compute call is made here; only argument validation that returns before
+touching a device.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+
+from vflash_b200 import _lib
+
+HEADER = Path(__file__).resolve().parent.parent / "include" / "vflash_b200.h"
+
+
+def declared_symbols() -> list[str]:
+    text = HEADER.read_text()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(vfb_\w+)\s*\(", text)))
+
+
+def exported_symbols(path: Path) -> set[str]:
+    import subprocess
+
+    out = subprocess.run(["nm", "-D", "--defined-only", str(path)], capture_output=True, text=True,
+                         check=True).stdout
+    return {line.split()[-1] for line in out.splitlines() if line.strip()}
+
+
+def test_header_declares_the_bound_symbols():
+    assert declared_symbols() == sorted(_lib.SIGNATURES)
+
+
+def test_library_exports_every_declared_symbol():
+    lib = _lib.load()
+    exported = exported_symbols(_lib.LIBRARY_PATH)
+    for name in declared_symbols():
+        assert name in exported, name
+        assert getattr(lib, name) is not None
+    # nothing else leaks from the shared object's C ABI namespace
+    assert {s for s in exported if s.startswith("vfb_")} == set(declared_symbols())
+
+
+def test_version_and_error_strings():
+    assert _lib.load().vfb_version().decode().startswith("vflash_b200")
+    assert isinstance(_lib.last_error(), str)
+
+
+def test_epilogue_struct_layout_matches_header():
+    # 8-byte aligned fields as declared in vfb_epilogue
+    assert ctypes.sizeof(_lib.Epilogue) == 4 + 4 + 8 * 5 + 8 * 3 + 8 + 4 * 3 + 4 + 8 * 6
+    assert _lib.Epilogue.adapter.offset == 48
+    assert _lib.Epilogue.residual.offset == 96
+
+
+@pytest.mark.parametrize(
+    "args",
+    [
+        (None, 4, 0, 4, None, None, 16, None),  # K = 0
+        (None, 4, 40000, 40000, None, None, 16, None),  # K > 32768
+        (None, 4, 64, 32, None, None, 16, None),  # ldx < K
+        (None, 20, 64, 64, None, None, 16, None),  # M_pad < M
+    ],
+)
+def test_quantiser_rejects_bad_shapes_before_any_launch(args):
+    rc = _lib.load().vfb_fp8_quant_rows(*args)
+    assert rc == _lib.VFB_EINVAL
+    assert "vfb_fp8_quant_rows" in _lib.last_error()
+
+
+def test_gemm_rejects_bad_shapes_before_any_launch():
+    lib = _lib.load()
+    ep = _lib.Epilogue()
+    ep.kind = _lib.EPI_STORE
+    assert lib.vfb_fp8_gemm(None, 64, None, None, 64, None, 4, 48, 64, ctypes.byref(ep), None) == _lib.VFB_EINVAL
+    assert "N % 32" in _lib.last_error()
+    ep.kind = 9
+    assert lib.vfb_fp8_gemm(None, 64, None, None, 64, None, 4, 64, 64, ctypes.byref(ep), None) == _lib.VFB_EINVAL
+    assert "unknown epilogue" in _lib.last_error()
+    assert lib.vfb_fp8_gemm(None, 64, None, None, 64, None, 4, 64, 64, None, None) == _lib.VFB_EINVAL
+
+
+def test_missing_library_fails_loudly(monkeypatch, tmp_path):
+    monkeypatch.setattr(_lib, "LIBRARY_PATH", tmp_path / "absent.so")
+    monkeypatch.setattr(_lib, "_handle", None)
+    with pytest.raises(_lib.NativeLibraryError, match="missing"):
+        _lib.load()

@@ -1,0 +1,115 @@
+"""Pin the CPU oracle against golden vectors frozen from the reference itself.
+
+The fixtures come from tests/golden/make_golden.py, which imports Hansimov/vflash's
+own ``_quantize_activation_torch`` and ``RowFP8Execution`` (CPU paths).
+Quantisation must match bit for bit; linear outputs and transcendental
+epilogues within the stated tolerances.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+from oracle import epilogues as ep
+from oracle import fp8
+
+QUANT_CASES = ["outliers", "wide", "k16", "k24", "k40", "ties", "subnormal", "zeros"]
+
+
+@pytest.mark.parametrize("name", QUANT_CASES)
+def test_quantizer_matches_reference_bit_for_bit(golden, name):
+    codes, scales = fp8.quantize_activation(golden[f"q_{name}_x"])
+    np.testing.assert_array_equal(codes, golden[f"q_{name}_codes"])
+    np.testing.assert_array_equal(scales.view(np.uint32), golden[f"q_{name}_scales"].view(np.uint32))
+
+
+@pytest.mark.parametrize("rows", [1, 16, 17])
+def test_strided_value_half_matches_reference(golden, rows):
+    # tests/test_fp8_linear.py:99-120 of the reference: the value half of a
+    # packed FFN projection (doubled row stride), a zero row and a bf16.tiny row.
+    base = golden[f"q_strided{rows}_base"]
+    codes, scales = fp8.quantize_activation(base[:, :64])
+    np.testing.assert_array_equal(codes, golden[f"q_strided{rows}_codes"])
+    np.testing.assert_array_equal(scales, golden[f"q_strided{rows}_scales"])
+    padded = (rows + 15) // 16 * 16
+    assert codes.shape == (padded, 64) and scales.shape == (padded, 1)
+    assert scales[0, 0] == 1 and (codes[0] == 0).all()
+    assert (codes[rows:] == 0).all() and (scales[rows:] == 1).all()
+
+
+def test_e4m3_codec_round_trips_every_finite_code():
+    codes = np.arange(256, dtype=np.uint8)
+    values = fp8.e4m3_decode(codes)
+    finite = ~np.isnan(values)
+    np.testing.assert_array_equal(fp8.e4m3_encode(values[finite]), codes[finite])
+    assert np.isnan(values[0x7F]) and np.isnan(values[0xFF])
+    assert values[0x7E] == 448 and values[0x01] == 2.0**-9
+
+
+def test_e4m3_encoder_rounds_to_nearest_even_against_torch():
+    torch = pytest.importorskip("torch")
+    gen = np.random.default_rng(5)
+    x = np.concatenate([
+        gen.normal(0, 50, 20000), gen.normal(0, 0.01, 20000),
+        (np.arange(-3600, 3601) / 8.0),
+    ]).astype(np.float32)
+    x = np.clip(x, -448, 448)
+    expected = torch.from_numpy(x).to(torch.float8_e4m3fn).view(torch.uint8).numpy()
+    np.testing.assert_array_equal(fp8.e4m3_encode(x), expected)
+
+
+def test_bf16_rounding_matches_torch():
+    torch = pytest.importorskip("torch")
+    x = np.random.default_rng(6).normal(0, 1e3, 50000).astype(np.float32)
+    expected = torch.from_numpy(x).to(torch.bfloat16).view(torch.int16).numpy().view(np.uint16)
+    np.testing.assert_array_equal(fp8.bf16_bits(x), expected)
+
+
+def test_weight_only_linear_matches_reference(golden):
+    torch = pytest.importorskip("torch")
+    for case in ("wo_small", "wo_mid"):
+        x = torch.from_numpy(golden[f"{case}_x"].view(np.int16)).view(torch.bfloat16)
+        codes = torch.from_numpy(golden[f"{case}_codes"]).view(torch.float8_e4m3fn)
+        scales = torch.from_numpy(golden[f"{case}_scales"])
+        bias = torch.from_numpy(golden[f"{case}_bias"].view(np.int16)).view(torch.bfloat16)
+        y = fp8.weight_only_linear(x, codes, scales, bias)
+        expected = fp8.bf16_value(golden[f"{case}_y"])
+        actual = y.float().numpy()
+        # oneDNN's bf16 GEMM may block its reduction differently on another
+        # host CPU; the result must still agree to bf16 precision.
+        assert fp8.rel_l2(actual, expected) <= 4e-3, case
+
+
+def test_weight_quantiser_matches_reference_expression(golden):
+    # make_golden.py quantised the mid-size weight with the reference's own
+    # activation expression per output row; the oracle's weight quantiser is
+    # that expression without row padding.
+    w = fp8.bf16_value(golden["wo_mid_w"])
+    codes, scales = fp8.quantize_weight(w)
+    np.testing.assert_array_equal(codes, golden["wo_mid_codes"])
+    np.testing.assert_array_equal(scales, golden["wo_mid_scales"])
+
+
+def test_strict_epilogues_match_eager_compositions(golden):
+    np.testing.assert_array_equal(ep.silu_mul(golden["silu_packed"]), golden["silu_out"])
+    np.testing.assert_array_equal(
+        ep.gate_residual(golden["gr_residual"], golden["gr_gate"], golden["gr_projected"]),
+        golden["gr_out"])
+    np.testing.assert_array_equal(
+        ep.qkv_direct_merge(golden["qkv_base"], golden["qkv_adapters"], golden["qkv_scalings"]),
+        golden["qkv_out"])
+    # tanh differs in the last fp32 bit between libraries (and where 1 + tanh
+    # cancels, one library returns exactly 0): one bf16 ulp or 1e-6 absolute.
+    got = fp8.bf16_value(ep.gelu_tanh(golden["gelu_y"]))
+    want = fp8.bf16_value(golden["gelu_out"])
+    np.testing.assert_allclose(got, want, rtol=2.0**-7, atol=1e-6)
+    assert (got != want).mean() < 0.02
+
+
+def test_w8a8_emulation_agrees_with_dequantised_matmul(golden):
+    x = golden["wo_mid_x"]
+    a_codes, a_scale = fp8.quantize_activation(x)
+    y = fp8.w8a8_reference(a_codes[:33], a_scale[:33], golden["wo_mid_codes"], golden["wo_mid_scales"])
+    f32 = fp8.dequant_matmul_f32(a_codes[:33], a_scale[:33], golden["wo_mid_codes"], golden["wo_mid_scales"])
+    assert fp8.rel_l2(y, f32) < 5e-3

@@ -1,0 +1,94 @@
+// Error reporting, device checks and the device status word of the C ABI.
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+
+#include "common.cuh"
+
+namespace {
+
+thread_local char g_last_error[512] = "";
+
+constexpr int kMaxDevices = 64;
+std::mutex g_mutex;
+int g_sm_count[kMaxDevices];          // 0 = not queried yet
+int *g_status_ptr[kMaxDevices];       // device address of g_device_status
+
+}  // namespace
+
+// One status word per device; kernels receive its address as an argument.
+static __device__ int g_device_status = 0;
+
+namespace vfb {
+
+int set_error(int code, const char *fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_last_error, sizeof(g_last_error), fmt, ap);
+  va_end(ap);
+  return code;
+}
+
+// Checks that the current device is a compute capability 10.0 part (B200)
+// and returns its SM count.
+int check_device(int *sm_count) {
+  int dev = 0;
+  cudaError_t err = cudaGetDevice(&dev);
+  if (err != cudaSuccess) return set_error(VFB_ECUDA, "cudaGetDevice: %s", cudaGetErrorString(err));
+  if (dev < 0 || dev >= kMaxDevices) return set_error(VFB_EDEVICE, "device ordinal %d out of range", dev);
+  std::lock_guard<std::mutex> lock(g_mutex);
+  if (g_sm_count[dev] == 0) {
+    int major = 0, minor = 0, sms = 0;
+    if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+      return set_error(VFB_ECUDA, "cudaDeviceGetAttribute failed on device %d", dev);
+    if (major != 10 || minor != 0)
+      return set_error(VFB_EDEVICE,
+                       "vflash_b200 kernels are built for sm_100a only; device %d is sm_%d%d", dev,
+                       major, minor);
+    g_sm_count[dev] = sms;
+  }
+  if (sm_count) *sm_count = g_sm_count[dev];
+  return VFB_OK;
+}
+
+// Device address of this device's status word (looked up once per device).
+int *device_status_ptr() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return nullptr;
+  std::lock_guard<std::mutex> lock(g_mutex);
+  if (g_status_ptr[dev] == nullptr) {
+    void *ptr = nullptr;
+    if (cudaGetSymbolAddress(&ptr, g_device_status) != cudaSuccess) return nullptr;
+    g_status_ptr[dev] = static_cast<int *>(ptr);
+  }
+  return g_status_ptr[dev];
+}
+
+}  // namespace vfb
+
+extern "C" const char *vfb_last_error(void) { return g_last_error; }
+
+extern "C" const char *vfb_version(void) { return "vflash_b200 0.1.0 sm_100a"; }
+
+extern "C" int vfb_device_status(int *status, int clear) {
+  if (status == nullptr) return vfb::set_error(VFB_EINVAL, "vfb_device_status: status is NULL");
+  int rc = vfb::check_device(nullptr);
+  if (rc != VFB_OK) return rc;
+  int *ptr = vfb::device_status_ptr();
+  if (ptr == nullptr) return vfb::set_error(VFB_ECUDA, "cannot resolve the device status word");
+  cudaError_t err = cudaDeviceSynchronize();
+  if (err != cudaSuccess)
+    return vfb::set_error(VFB_ECUDA, "cudaDeviceSynchronize: %s", cudaGetErrorString(err));
+  err = cudaMemcpy(status, ptr, sizeof(int), cudaMemcpyDeviceToHost);
+  if (err != cudaSuccess) return vfb::set_error(VFB_ECUDA, "status read: %s", cudaGetErrorString(err));
+  if (clear) {
+    err = cudaMemset(ptr, 0, sizeof(int));
+    if (err != cudaSuccess) return vfb::set_error(VFB_ECUDA, "status clear: %s", cudaGetErrorString(err));
+    err = cudaDeviceSynchronize();
+    if (err != cudaSuccess) return vfb::set_error(VFB_ECUDA, "status clear sync: %s", cudaGetErrorString(err));
+  }
+  return VFB_OK;
+}

@@ -1,0 +1,528 @@
+// Row-scaled FP8 (e4m3 x e4m3 -> fp32) GEMM for sm_100a with fused epilogues.
+//
+// Replaces torch._scaled_mm(codes, weight.t(), scale_a, scale_b.t(), bf16)
+// and the bias add that follows it (src/vflash/native/h3_fp8_linear.py:109-121),
+// plus the strict-BF16 elementwise launch that the H3 block runs next
+// (src/vflash/native/h3_fused_ops.py: silu_mul 185-224, gate_residual
+// 125-170, qkv_direct_merge 901-949).  Every BF16 rounding boundary of those
+// eager/Triton sequences is kept: the GEMM result is rounded to BF16 first,
+// then each elementwise step rounds where the reference rounds.
+//
+// Structure (one persistent CTA per SM, 192 threads):
+//   warp 0      TMA producer: A tile 128x128 B and B tile 256x128 B per stage
+//               (128-byte swizzle) into a STAGES-deep shared-memory ring.
+//   warp 1      allocates 512 TMEM columns (two 128x256 fp32 accumulators) and
+//               one elected lane issues tcgen05.mma kind::f8f6f4 (M=128,
+//               N=256, K=32; four per stage), committing each stage back to
+//               the producer and each finished tile to the epilogue.
+//   warps 2-5   epilogue: tcgen05.ld 32 columns at a time (warp w reads TMEM
+//               lanes 32*(w%4)..+31 = tile rows), apply scales / bias /
+//               activation / residual in registers and store BF16 rows with
+//               16-byte stores.  The second accumulator lets the epilogue of
+//               tile i overlap the main loop of tile i+1.
+// Tiles are visited with the N index fastest so that the CTAs running at the
+// same time share one A row-block and stream the weight through L2.
+// No TMA multicast is used: every CTA loads its own operands.
+#include <cudaTypedefs.h>
+
+#include <mutex>
+
+#include "common.cuh"
+
+namespace vfb {
+namespace {
+
+constexpr int BM = 128;
+constexpr int BN = 256;
+constexpr int BK = 128;  // bytes = e4m3 elements per stage
+constexpr int UMMA_K = 32;
+constexpr int STAGES = 4;
+constexpr int A_STAGE_BYTES = BM * BK;  // 16 KB
+constexpr int B_STAGE_BYTES = BN * BK;  // 32 KB
+constexpr int NUM_THREADS = 192;
+constexpr int TMEM_COLS = 512;
+constexpr size_t SMEM_BYTES = 1024 + STAGES * (A_STAGE_BYTES + B_STAGE_BYTES) + 256;
+
+struct EpiParams {
+  __nv_bfloat16 *out;
+  int64_t ldo;
+  int64_t plane_width;
+  int64_t plane_stride;
+  const __nv_bfloat16 *bias;
+  const __nv_bfloat16 *adapter[3];
+  int64_t adapter_ld;
+  float scaling[3];
+  const __nv_bfloat16 *residual;
+  int64_t ldr;
+  const __nv_bfloat16 *gate;
+  int64_t gate_ts;
+  int64_t gate_hs;
+  int64_t tokens;
+  int64_t ffn_width;  // SWIGLU: F (value columns [0,F), gate columns [F,2F))
+};
+
+struct GemmParams {
+  int64_t M;
+  int64_t N;  // output columns of the GEMM (packed 2F for SWIGLU)
+  int64_t K;
+  const float *sa;
+  const float *sw;
+  int num_m_tiles;
+  int num_n_tiles;
+  int num_kb;
+  int *status;
+  EpiParams ep;
+};
+
+__device__ __forceinline__ float gelu_tanh(float y) {
+  // 0.5 y (1 + tanh(sqrt(2/pi) (y + 0.044715 y^3)))
+  const float k_beta = 0.7978845608028654f;
+  const float k_kappa = 0.044715f;
+  const float cube = y * y * y;
+  const float inner = k_beta * (y + k_kappa * cube);
+  return 0.5f * y * (1.0f + tanhf(inner));
+}
+
+__device__ __forceinline__ float silu(float g) { return g / (1.0f + expf(-g)); }
+
+__device__ __forceinline__ void load_f32x32(const float *__restrict__ p, float (&r)[32]) {
+  const float4 *q = reinterpret_cast<const float4 *>(p);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    float4 t = __ldg(q + i);
+    r[4 * i] = t.x;
+    r[4 * i + 1] = t.y;
+    r[4 * i + 2] = t.z;
+    r[4 * i + 3] = t.w;
+  }
+}
+
+__device__ __forceinline__ void load_bf16x32(const __nv_bfloat16 *p, float (&r)[32]) {
+  const uint4 *q = reinterpret_cast<const uint4 *>(p);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    uint4 t = __ldg(q + i);
+    const __nv_bfloat162 *h = reinterpret_cast<const __nv_bfloat162 *>(&t);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      float2 f = __bfloat1622float2(h[j]);
+      r[8 * i + 2 * j] = f.x;
+      r[8 * i + 2 * j + 1] = f.y;
+    }
+  }
+}
+
+__device__ __forceinline__ void store_bf16x32(__nv_bfloat16 *p, const float (&y)[32]) {
+  uint4 *q = reinterpret_cast<uint4 *>(p);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    uint4 t;
+    t.x = pack_bf16x2(y[8 * i + 0], y[8 * i + 1]);
+    t.y = pack_bf16x2(y[8 * i + 2], y[8 * i + 3]);
+    t.z = pack_bf16x2(y[8 * i + 4], y[8 * i + 5]);
+    t.w = pack_bf16x2(y[8 * i + 6], y[8 * i + 7]);
+    q[i] = t;
+  }
+}
+
+// y = bf16(acc * sa * sw) then bf16(y + bias): the _scaled_mm output followed
+// by the separate bias add of the reference.
+__device__ __forceinline__ void scale_bias(float (&v)[32], float sa, const float *sw,
+                                           const __nv_bfloat16 *bias) {
+  float w[32];
+  load_f32x32(sw, w);
+#pragma unroll
+  for (int j = 0; j < 32; ++j) v[j] = bf16r(v[j] * sa * w[j]);
+  if (bias != nullptr) {
+    float b[32];
+    load_bf16x32(bias, b);
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] = bf16r(v[j] + b[j]);
+  }
+}
+
+template <int EPI>
+__global__ void __launch_bounds__(NUM_THREADS, 1)
+    fp8_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                    const __grid_constant__ CUtensorMap tmB2, const GemmParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                              ~static_cast<uintptr_t>(1023));
+  uint8_t *sA = smem;
+  uint8_t *sB = smem + STAGES * A_STAGE_BYTES;
+  uint64_t *full_bar = reinterpret_cast<uint64_t *>(sB + STAGES * B_STAGE_BYTES);
+  uint64_t *empty_bar = full_bar + STAGES;
+  uint64_t *tfull_bar = empty_bar + STAGES;
+  uint64_t *tempty_bar = tfull_bar + 2;
+  uint64_t *drain_bar = tempty_bar + 2;
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(drain_bar + 1);
+  volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
+
+  const int warp = threadIdx.x / 32;
+  const int lane = threadIdx.x % 32;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&empty_bar[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull_bar[a], 1);
+      mbar_init(&tempty_bar[a], 128);
+    }
+    mbar_init(drain_bar, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+    if (EPI == VFB_EPI_SWIGLU) tma_prefetch_desc(&tmB2);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  const int num_tiles = p.num_m_tiles * p.num_n_tiles;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---------------- TMA producer ----------------
+      int s = 0;
+      uint32_t ph = 0;
+      uint32_t issued_phase[STAGES];
+      bool issued[STAGES];
+      for (int i = 0; i < STAGES; ++i) issued[i] = false;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+        const int m_tile = tile / p.num_n_tiles;
+        const int n_tile = tile % p.num_n_tiles;
+        for (int kb = 0; kb < p.num_kb; ++kb) {
+          if (!mbar_wait(&empty_bar[s], ph ^ 1, abort_flag, p.status)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&full_bar[s], A_STAGE_BYTES + B_STAGE_BYTES);
+          tma_load_2d(sA + s * A_STAGE_BYTES, &tmA, &full_bar[s], kb * BK, m_tile * BM);
+          if (EPI == VFB_EPI_SWIGLU) {
+            tma_load_2d(sB + s * B_STAGE_BYTES, &tmB, &full_bar[s], kb * BK, n_tile * (BN / 2));
+            tma_load_2d(sB + s * B_STAGE_BYTES + B_STAGE_BYTES / 2, &tmB2, &full_bar[s], kb * BK,
+                        n_tile * (BN / 2));
+          } else {
+            tma_load_2d(sB + s * B_STAGE_BYTES, &tmB, &full_bar[s], kb * BK, n_tile * BN);
+          }
+          issued[s] = true;
+          issued_phase[s] = ph;
+          if (++s == STAGES) {
+            s = 0;
+            ph ^= 1;
+          }
+        }
+      }
+      // Drain: every load this thread issued has landed before the CTA exits.
+      for (int i = 0; i < STAGES; ++i)
+        if (issued[i]) mbar_wait(&full_bar[i], issued_phase[i], abort_flag, p.status);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ---------------- MMA issuer ----------------
+      constexpr uint32_t idesc = idesc_e4m3_f32(BM, BN);
+      int s = 0;
+      uint32_t ph = 0;
+      int t = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x, ++t) {
+        const int acc = t & 1;
+        const uint32_t acc_ph = (t >> 1) & 1;
+        if (!mbar_wait(&tempty_bar[acc], acc_ph ^ 1, abort_flag, p.status)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * BN;
+        for (int kb = 0; kb < p.num_kb; ++kb) {
+          if (!mbar_wait(&full_bar[s], ph, abort_flag, p.status)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint64_t a_desc = sw128_kmajor_desc(smem_u32(sA + s * A_STAGE_BYTES));
+          const uint64_t b_desc = sw128_kmajor_desc(smem_u32(sB + s * B_STAGE_BYTES));
+#pragma unroll
+          for (int k = 0; k < BK / UMMA_K; ++k) {
+            // +32 bytes along K inside the swizzled 128-byte row = +2 in 16-byte units.
+            mma_f8f6f4(d_tmem, a_desc + 2 * k, b_desc + 2 * k, idesc, (kb | k) != 0);
+          }
+          tc_commit(&empty_bar[s]);
+          if (++s == STAGES) {
+            s = 0;
+            ph ^= 1;
+          }
+        }
+        if (!ok) break;
+        tc_commit(&tfull_bar[acc]);
+      }
+      // Drain: all MMAs issued by this thread are complete before TMEM is freed.
+      tc_commit(drain_bar);
+      mbar_wait(drain_bar, 0, abort_flag, p.status);
+    }
+  } else {
+    // ---------------- epilogue (warps 2..5) ----------------
+    const int q = warp & 3;  // TMEM lane quarter this warp may access
+    const int row = q * 32 + lane;
+    const EpiParams &ep = p.ep;
+    int t = 0;
+    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++t) {
+      const int acc = t & 1;
+      const uint32_t acc_ph = (t >> 1) & 1;
+      if (!mbar_wait(&tfull_bar[acc], acc_ph, abort_flag, p.status)) break;
+      tc_fence_after();
+      const int m_tile = tile / p.num_n_tiles;
+      const int n_tile = tile % p.num_n_tiles;
+      const int64_t m = static_cast<int64_t>(m_tile) * BM + row;
+      const bool live = m < p.M;
+      const float sa = live ? __ldg(p.sa + m) : 0.0f;
+      const uint32_t t_row = tmem_base + acc * BN + (static_cast<uint32_t>(q * 32) << 16);
+
+      if (EPI == VFB_EPI_SWIGLU) {
+        const int64_t F = ep.ffn_width;
+#pragma unroll 1
+        for (int c = 0; c < BN / 2 / 32; ++c) {
+          const int64_t f = static_cast<int64_t>(n_tile) * (BN / 2) + c * 32;
+          if (f >= F) break;  // warp-uniform
+          float v[32], g[32];
+          tmem_ld_32x32b_x32(t_row + c * 32, v);
+          tmem_ld_32x32b_x32(t_row + BN / 2 + c * 32, g);
+          if (live) {
+            scale_bias(v, sa, p.sw + f, ep.bias ? ep.bias + f : nullptr);
+            scale_bias(g, sa, p.sw + F + f, ep.bias ? ep.bias + F + f : nullptr);
+#pragma unroll
+            for (int j = 0; j < 32; ++j) v[j] = v[j] * bf16r(silu(g[j]));
+            store_bf16x32(ep.out + m * ep.ldo + f, v);
+          }
+        }
+      } else {
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; ++c) {
+          const int64_t n = static_cast<int64_t>(n_tile) * BN + c * 32;
+          if (n >= p.N) break;  // warp-uniform
+          float v[32];
+          tmem_ld_32x32b_x32(t_row + c * 32, v);
+          if (live) {
+          scale_bias(v, sa, p.sw + n, ep.bias ? ep.bias + n : nullptr);
+          int64_t plane = 0, col = n;
+          if (ep.plane_width > 0) {
+            plane = n / ep.plane_width;
+            col = n - plane * ep.plane_width;
+          }
+          __nv_bfloat16 *dst = ep.out + plane * ep.plane_stride + m * ep.ldo + col;
+          if (EPI == VFB_EPI_STORE) {
+            const __nv_bfloat16 *ad = plane < 3 ? ep.adapter[plane] : nullptr;
+            if (ad != nullptr) {
+              float a[32];
+              load_bf16x32(ad + m * ep.adapter_ld + col, a);
+              const float sc = ep.scaling[plane];
+#pragma unroll
+              for (int j = 0; j < 32; ++j) v[j] = v[j] + bf16r(a[j] * sc);
+            }
+          } else if (EPI == VFB_EPI_GELU_TANH) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) v[j] = gelu_tanh(v[j]);
+          } else if (EPI == VFB_EPI_RESIDUAL) {
+            if (ep.gate != nullptr) {
+              const __nv_bfloat16 *gp = ep.gate + (m % ep.tokens) * ep.gate_ts + n * ep.gate_hs;
+#pragma unroll
+              for (int j = 0; j < 32; ++j) v[j] = bf16r(__bfloat162float(gp[j * ep.gate_hs]) * v[j]);
+            }
+            float r[32];
+            load_bf16x32(ep.residual + m * ep.ldr + n, r);
+#pragma unroll
+            for (int j = 0; j < 32; ++j) v[j] = r[j] + v[j];
+          }
+          store_bf16x32(dst, v);
+          }
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&tempty_bar[acc]);
+    }
+  }
+
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem_base, TMEM_COLS);
+  }
+}
+
+// ---- host side ---------------------------------------------------------------
+
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void *ptr = nullptr;
+    cudaDriverEntryPointQueryResult qres;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &qres) ==
+            cudaSuccess &&
+        qres == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  });
+  return fn;
+}
+
+// Tensor map over an 8-bit [rows, cols] matrix (row stride ld bytes) with a
+// 128-byte-swizzled box of box_rows x 128 bytes.
+int make_map_u8(CUtensorMap *map, const void *base, int64_t rows, int64_t cols, int64_t ld,
+                int box_rows) {
+  auto encode = tensor_map_encoder();
+  if (encode == nullptr) return set_error(VFB_ECUDA, "cuTensorMapEncodeTiled is unavailable");
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld)};
+  cuuint32_t box[2] = {static_cast<cuuint32_t>(BK), static_cast<cuuint32_t>(box_rows)};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void *>(base), dims,
+                      strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                      CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                      CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return set_error(VFB_ECUDA, "cuTensorMapEncodeTiled failed (%d) rows=%lld cols=%lld ld=%lld",
+                     static_cast<int>(r), (long long)rows, (long long)cols, (long long)ld);
+  return VFB_OK;
+}
+
+bool aligned16(const void *ptr) { return reinterpret_cast<uintptr_t>(ptr) % 16 == 0; }
+
+template <int EPI>
+int launch(const CUtensorMap &a, const CUtensorMap &b, const CUtensorMap &b2, const GemmParams &p,
+           int sm_count, cudaStream_t stream) {
+  auto kernel = fp8_gemm_kernel<EPI>;
+  cudaError_t err =
+      cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+  if (err != cudaSuccess)
+    return set_error(VFB_ECUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(err));
+  const int tiles = p.num_m_tiles * p.num_n_tiles;
+  const int grid = tiles < sm_count ? tiles : sm_count;
+  kernel<<<grid, NUM_THREADS, SMEM_BYTES, stream>>>(a, b, b2, p);
+  err = cudaGetLastError();
+  if (err != cudaSuccess)
+    return set_error(VFB_ECUDA, "vfb_fp8_gemm launch: %s", cudaGetErrorString(err));
+  return VFB_OK;
+}
+
+}  // namespace
+}  // namespace vfb
+
+extern "C" int vfb_fp8_gemm(const void *A, int64_t lda, const float *sa, const void *W, int64_t ldw,
+                            const float *sw, int64_t M, int64_t N, int64_t K,
+                            const vfb_epilogue *ep, void *stream) {
+  using namespace vfb;
+  if (ep == nullptr) return set_error(VFB_EINVAL, "vfb_fp8_gemm: epilogue is NULL");
+  const int kind = ep->kind;
+  if (kind < VFB_EPI_STORE || kind > VFB_EPI_RESIDUAL)
+    return set_error(VFB_EINVAL, "vfb_fp8_gemm: unknown epilogue kind %d", kind);
+  if (M < 0 || N <= 0 || K <= 0 || K % 16 || N % 32)
+    return set_error(VFB_EINVAL, "vfb_fp8_gemm: need M >= 0, N > 0 with N %% 32 == 0, K > 0 with "
+                                 "K %% 16 == 0 (M=%lld N=%lld K=%lld)",
+                     (long long)M, (long long)N, (long long)K);
+  if (M == 0) return VFB_OK;
+  if (M > (int64_t)BM * 0x7FFFFF || N > (int64_t)1 << 24 || K > (int64_t)1 << 20)
+    return set_error(VFB_EINVAL, "vfb_fp8_gemm: problem too large");
+  if (A == nullptr || W == nullptr || sa == nullptr || sw == nullptr || ep->out == nullptr)
+    return set_error(VFB_EINVAL, "vfb_fp8_gemm: NULL operand");
+  if (lda < K || ldw < K || lda % 16 || ldw % 16 || !aligned16(A) || !aligned16(W))
+    return set_error(VFB_EINVAL, "vfb_fp8_gemm: A/W need 16-byte aligned bases and row strides");
+  if (!aligned16(sw) || !aligned16(ep->out) || ep->ldo % 8)
+    return set_error(VFB_EINVAL, "vfb_fp8_gemm: sw/out need 16-byte alignment, ldo %% 8 == 0");
+  if (ep->bias != nullptr && !aligned16(ep->bias))
+    return set_error(VFB_EINVAL, "vfb_fp8_gemm: bias needs 16-byte alignment");
+
+  int sm_count = 0;
+  int rc = check_device(&sm_count);
+  if (rc != VFB_OK) return rc;
+
+  GemmParams p{};
+  p.M = M;
+  p.N = N;
+  p.K = K;
+  p.sa = sa;
+  p.sw = sw;
+  p.num_m_tiles = static_cast<int>((M + BM - 1) / BM);
+  p.num_kb = static_cast<int>((K + BK - 1) / BK);
+  p.status = device_status_ptr();
+  EpiParams &e = p.ep;
+  e.out = static_cast<__nv_bfloat16 *>(ep->out);
+  e.ldo = ep->ldo;
+  e.bias = static_cast<const __nv_bfloat16 *>(ep->bias);
+
+  CUtensorMap ta, tb, tb2;
+  rc = make_map_u8(&ta, A, M, K, lda, BM);
+  if (rc != VFB_OK) return rc;
+
+  if (kind == VFB_EPI_SWIGLU) {
+    if (N % 64)
+      return set_error(VFB_EINVAL, "vfb_fp8_gemm: SWIGLU needs the packed width N = 2F, F %% 32 == 0");
+    const int64_t F = N / 2;
+    if (ep->ldo < F) return set_error(VFB_EINVAL, "vfb_fp8_gemm: SWIGLU output ldo < F");
+    e.ffn_width = F;
+    p.num_n_tiles = static_cast<int>((F + BN / 2 - 1) / (BN / 2));
+    const uint8_t *gate_rows = static_cast<const uint8_t *>(W) + F * ldw;
+    if ((rc = make_map_u8(&tb, W, F, K, ldw, BN / 2)) != VFB_OK) return rc;
+    if ((rc = make_map_u8(&tb2, gate_rows, F, K, ldw, BN / 2)) != VFB_OK) return rc;
+  } else {
+    e.plane_width = ep->plane_width;
+    e.plane_stride = ep->plane_stride;
+    if (e.plane_width < 0 || (e.plane_width > 0 && (e.plane_width % 32 || N % e.plane_width)))
+      return set_error(VFB_EINVAL, "vfb_fp8_gemm: plane_width must be 0 or a multiple of 32 dividing N");
+    if (e.plane_stride % 8)
+      return set_error(VFB_EINVAL, "vfb_fp8_gemm: plane_stride %% 8 != 0");
+    const int64_t width = e.plane_width > 0 ? e.plane_width : N;
+    if (ep->ldo < width) return set_error(VFB_EINVAL, "vfb_fp8_gemm: ldo smaller than the plane width");
+    p.num_n_tiles = static_cast<int>((N + BN - 1) / BN);
+    if ((rc = make_map_u8(&tb, W, N, K, ldw, BN)) != VFB_OK) return rc;
+    tb2 = tb;
+    if (kind == VFB_EPI_STORE) {
+      const int planes = e.plane_width > 0 ? static_cast<int>(N / e.plane_width) : 1;
+      for (int i = 0; i < 3; ++i) {
+        e.adapter[i] = static_cast<const __nv_bfloat16 *>(ep->adapter[i]);
+        e.scaling[i] = ep->scaling[i];
+        if (e.adapter[i] != nullptr) {
+          if (i >= planes || !aligned16(e.adapter[i]) || ep->adapter_ld % 8 || ep->adapter_ld < width)
+            return set_error(VFB_EINVAL, "vfb_fp8_gemm: adapter %d misaligned or beyond the planes", i);
+        }
+      }
+      e.adapter_ld = ep->adapter_ld;
+    }
+    if (kind == VFB_EPI_RESIDUAL) {
+      if (ep->residual == nullptr || !aligned16(ep->residual) || ep->ldr % 8 || ep->ldr < N)
+        return set_error(VFB_EINVAL, "vfb_fp8_gemm: residual needs a 16-byte aligned [M,N] view");
+      if (e.plane_width != 0)
+        return set_error(VFB_EINVAL, "vfb_fp8_gemm: RESIDUAL writes one plane");
+      e.residual = static_cast<const __nv_bfloat16 *>(ep->residual);
+      e.ldr = ep->ldr;
+      e.gate = static_cast<const __nv_bfloat16 *>(ep->gate);
+      if (e.gate != nullptr) {
+        if (ep->tokens <= 0)
+          return set_error(VFB_EINVAL, "vfb_fp8_gemm: gate needs tokens > 0");
+        e.gate_ts = ep->gate_token_stride;
+        e.gate_hs = ep->gate_hidden_stride;
+        e.tokens = ep->tokens;
+      }
+    }
+  }
+
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  switch (kind) {
+    case VFB_EPI_STORE:
+      return launch<VFB_EPI_STORE>(ta, tb, tb2, p, sm_count, s);
+    case VFB_EPI_GELU_TANH:
+      return launch<VFB_EPI_GELU_TANH>(ta, tb, tb2, p, sm_count, s);
+    case VFB_EPI_SWIGLU:
+      return launch<VFB_EPI_SWIGLU>(ta, tb, tb2, p, sm_count, s);
+    default:
+      return launch<VFB_EPI_RESIDUAL>(ta, tb, tb2, p, sm_count, s);
+  }
+}

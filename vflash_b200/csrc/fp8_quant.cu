@@ -1,0 +1,199 @@
+// Per-token dynamic e4m3 activation quantisation (HBM-bound).
+//
+// Arithmetic follows _quantize_activation_torch
+// (src/vflash/native/h3_fp8_linear.py:18-31) and the Triton _rows_fp8 kernel
+// (src/vflash/native/h3_fp8_activation.py:13-28) bit for bit:
+//   amax  = max |x| over the row (fp32)
+//   scale = amax > 0 ? max(amax / 448, FLT_MIN) : 1      (IEEE division)
+//   code  = e4m3_rn(clamp(x / scale, -448, 448))         (IEEE division)
+// Rows are padded to the caller's M_pad (16 in the reference) with code 0 and
+// scale 1.  A NaN anywhere in a row makes amax NaN as in torch, so the row's
+// scale is 1 and NaN inputs stay NaN codes.
+//
+// Layout: one group of TPR threads (a multiple of 32) owns one row and keeps
+// the whole row in registers as packed bf16 (4 x 16-byte loads per thread, so
+// K <= 32768 needs at most 1024 threads); the row maximum is reduced with warp
+// shuffles and, across the row's warps, through shared memory.  Each byte of
+// x is read once and each code written once: 3 bytes of traffic per element.
+#include <cfloat>
+
+#include "common.cuh"
+
+namespace vfb {
+namespace {
+
+constexpr int kVecPerThread = 4;     // 16-byte vectors (8 bf16) per thread
+constexpr int kBlockThreads = 256;
+
+__device__ __forceinline__ float clamp448(float q) {
+  // NaN-preserving clamp (torch.clamp keeps NaN).
+  q = q > 448.0f ? 448.0f : q;
+  q = q < -448.0f ? -448.0f : q;
+  return q;
+}
+
+__device__ __forceinline__ float row_scale(float amax, bool nan) {
+  if (nan || !(amax > 0.0f)) return 1.0f;
+  return fmaxf(__fdiv_rn(amax, 448.0f), FLT_MIN);
+}
+
+// Vector path: x rows 16-byte aligned, K % 8 == 0.
+__global__ void __launch_bounds__(1024) fp8_quant_rows_vec(
+    const __nv_bfloat16 *__restrict__ x, int64_t M, int64_t K, int64_t ldx,
+    uint8_t *__restrict__ codes, float *__restrict__ scales, int64_t M_pad, int tpr) {
+  extern __shared__ float red[];  // [rows per block][warps per row] maxima + nan flags
+  const int rows_per_block = blockDim.x / tpr;
+  const int r_local = threadIdx.x / tpr;
+  const int t = threadIdx.x % tpr;
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * rows_per_block + r_local;
+  const int warps_per_row = tpr / 32;
+  const int64_t nvec = K / 8;
+
+  uint4 v[kVecPerThread];
+  float amax = 0.0f;
+  bool nan = false;
+  const bool live = row < M;
+  if (live) {
+    const uint4 *src = reinterpret_cast<const uint4 *>(x + row * ldx);
+#pragma unroll
+    for (int i = 0; i < kVecPerThread; ++i) {
+      const int64_t c = static_cast<int64_t>(i) * tpr + t;
+      v[i] = c < nvec ? __ldcs(src + c) : make_uint4(0, 0, 0, 0);
+    }
+#pragma unroll
+    for (int i = 0; i < kVecPerThread; ++i) {
+      const __nv_bfloat162 *h = reinterpret_cast<const __nv_bfloat162 *>(&v[i]);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        float2 f = __bfloat1622float2(h[j]);
+        nan |= (f.x != f.x) | (f.y != f.y);
+        amax = fmaxf(amax, fmaxf(fabsf(f.x), fabsf(f.y)));
+      }
+    }
+  }
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
+  nan = __any_sync(0xffffffffu, nan);
+  if (warps_per_row > 1) {
+    float *row_red = red + r_local * warps_per_row * 2;
+    if ((t & 31) == 0) {
+      row_red[t / 32] = amax;
+      row_red[warps_per_row + t / 32] = nan ? 1.0f : 0.0f;
+    }
+    __syncthreads();
+    amax = 0.0f;
+    float any_nan = 0.0f;
+    for (int w = 0; w < warps_per_row; ++w) {
+      amax = fmaxf(amax, row_red[w]);
+      any_nan = fmaxf(any_nan, row_red[warps_per_row + w]);
+    }
+    nan = any_nan != 0.0f;
+  }
+  if (row >= M_pad) return;
+  const float scale = live ? row_scale(amax, nan) : 1.0f;
+  uint2 *dst = reinterpret_cast<uint2 *>(codes + row * K);
+#pragma unroll
+  for (int i = 0; i < kVecPerThread; ++i) {
+    const int64_t c = static_cast<int64_t>(i) * tpr + t;
+    if (c >= nvec) continue;
+    uint2 out = make_uint2(0, 0);
+    if (live) {
+      const __nv_bfloat162 *h = reinterpret_cast<const __nv_bfloat162 *>(&v[i]);
+      uint16_t q[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        float2 f = __bfloat1622float2(h[j]);
+        q[j] = pack_e4m3x2(clamp448(__fdiv_rn(f.x, scale)), clamp448(__fdiv_rn(f.y, scale)));
+      }
+      out.x = static_cast<uint32_t>(q[0]) | (static_cast<uint32_t>(q[1]) << 16);
+      out.y = static_cast<uint32_t>(q[2]) | (static_cast<uint32_t>(q[3]) << 16);
+    }
+    dst[c] = out;
+  }
+  if (t == 0) scales[row] = scale;
+}
+
+// Generic path (any K, any alignment): one block per row, two passes over
+// the row (the second from cache).
+__global__ void __launch_bounds__(kBlockThreads) fp8_quant_rows_scalar(
+    const __nv_bfloat16 *__restrict__ x, int64_t M, int64_t K, int64_t ldx,
+    uint8_t *__restrict__ codes, float *__restrict__ scales, int64_t M_pad) {
+  __shared__ float red[kBlockThreads / 32 * 2];
+  const int64_t row = blockIdx.x;
+  const bool live = row < M;
+  float amax = 0.0f;
+  bool nan = false;
+  if (live) {
+    for (int64_t c = threadIdx.x; c < K; c += blockDim.x) {
+      float f = __bfloat162float(x[row * ldx + c]);
+      nan |= f != f;
+      amax = fmaxf(amax, fabsf(f));
+    }
+  }
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
+  nan = __any_sync(0xffffffffu, nan);
+  const int warps = blockDim.x / 32;
+  if ((threadIdx.x & 31) == 0) {
+    red[threadIdx.x / 32] = amax;
+    red[warps + threadIdx.x / 32] = nan ? 1.0f : 0.0f;
+  }
+  __syncthreads();
+  amax = 0.0f;
+  float any_nan = 0.0f;
+  for (int w = 0; w < warps; ++w) {
+    amax = fmaxf(amax, red[w]);
+    any_nan = fmaxf(any_nan, red[warps + w]);
+  }
+  const float scale = live ? row_scale(amax, any_nan != 0.0f) : 1.0f;
+  for (int64_t c = threadIdx.x; c < K; c += blockDim.x) {
+    uint8_t q = 0;
+    if (live) {
+      float f = __bfloat162float(x[row * ldx + c]);
+      q = static_cast<uint8_t>(pack_e4m3x2(clamp448(__fdiv_rn(f, scale)), 0.0f) & 0xFF);
+    }
+    codes[row * K + c] = q;
+  }
+  if (threadIdx.x == 0) scales[row] = scale;
+}
+
+}  // namespace
+}  // namespace vfb
+
+extern "C" int vfb_fp8_quant_rows(const void *x, int64_t M, int64_t K, int64_t ldx, void *codes,
+                                  float *scales, int64_t M_pad, void *stream) {
+  using namespace vfb;
+  if (M < 0 || K < 1 || K > 32768 || ldx < K || M_pad < M)
+    return set_error(VFB_EINVAL,
+                     "vfb_fp8_quant_rows: need M >= 0, 1 <= K <= 32768, ldx >= K, M_pad >= M "
+                     "(M=%lld K=%lld ldx=%lld M_pad=%lld)",
+                     (long long)M, (long long)K, (long long)ldx, (long long)M_pad);
+  if (M_pad == 0) return VFB_OK;
+  if ((M > 0 && x == nullptr) || codes == nullptr || scales == nullptr)
+    return set_error(VFB_EINVAL, "vfb_fp8_quant_rows: NULL pointer");
+  int rc = check_device(nullptr);
+  if (rc != VFB_OK) return rc;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const bool vec = (K % 8 == 0) && (ldx % 8 == 0) && (reinterpret_cast<uintptr_t>(x) % 16 == 0) &&
+                   (reinterpret_cast<uintptr_t>(codes) % 8 == 0);
+  if (vec) {
+    const int64_t nvec = K / 8;
+    int tpr = static_cast<int>((nvec + kVecPerThread - 1) / kVecPerThread);
+    tpr = (tpr + 31) / 32 * 32;
+    const int rows_per_block = tpr >= kBlockThreads ? 1 : kBlockThreads / tpr;
+    const int threads = tpr * rows_per_block;
+    const int64_t blocks = (M_pad + rows_per_block - 1) / rows_per_block;
+    const size_t smem = static_cast<size_t>(rows_per_block) * (tpr / 32) * 2 * sizeof(float);
+    fp8_quant_rows_vec<<<static_cast<unsigned>(blocks), threads, smem, s>>>(
+        static_cast<const __nv_bfloat16 *>(x), M, K, ldx, static_cast<uint8_t *>(codes), scales,
+        M_pad, tpr);
+  } else {
+    fp8_quant_rows_scalar<<<static_cast<unsigned>(M_pad), kBlockThreads, 0, s>>>(
+        static_cast<const __nv_bfloat16 *>(x), M, K, ldx, static_cast<uint8_t *>(codes), scales,
+        M_pad);
+  }
+  cudaError_t err = cudaGetLastError();
+  if (err != cudaSuccess)
+    return set_error(VFB_ECUDA, "vfb_fp8_quant_rows launch: %s", cudaGetErrorString(err));
+  return VFB_OK;
+}

@@ -1,0 +1,302 @@
+"""Explicit approximate row-scaled E4M3 linear execution on SM100 (drop-in).
+
+Mirrors ``RowFP8Execution`` / ``RowFP8Linear`` of Hansimov/vflash
+(src/vflash/native/h3_fp8_linear.py:34-149): same constructor arguments,
+attributes (``mode``, ``calls``, ``observer``, ``measure``), validation order
+and error messages, same weight layout (e4m3 ``[N, K]`` + fp32 ``row_scale``
+``[N, 1]``) and same output (bf16 ``[..., N]``).
+
+* ``weight-only`` keeps the reference's restored-weight expression verbatim
+  (h3_fp8_linear.py:88-91); it is the reference's explicit alternative mode,
+  not the W8A8 hot path, and never runs in its place.
+* ``w8a8`` runs the native SM100 path: the per-token e4m3 quantiser
+  (``vfb_fp8_quant_rows``) and the tcgen05 GEMM (``vfb_fp8_gemm``) with the
+  row x column scales and bias fused into its epilogue.  Both
+  ``activation_quantizer`` values select the same native quantiser (the
+  reference's two choices compute identical bits).  ``fast_accum`` is kept
+  for compatibility: the tcgen05 path always accumulates in fp32 TMEM.
+  Non-SM100 devices and non-bf16 inputs raise; nothing falls back.
+
+New fused entry points (``qkv_linear``, ``gelu_linear``, ``swiglu_linear``,
+``gate_residual_linear``, ``ffn``) run the same GEMM with the elementwise step
+that the H3 block performs next fused into the epilogue; each keeps the BF16
+rounding boundaries of the reference's separate launch.
+"""
+
+from __future__ import annotations
+
+from collections.abc import Callable
+from contextlib import AbstractContextManager, nullcontext
+from typing import Any
+
+import torch
+
+from .. import _lib
+from ..kernels import Epilogue, fp8_gemm, quantize_fp8_rows
+
+
+def _on_sm100(device: torch.device) -> bool:
+    return device.type == "cuda" and torch.cuda.get_device_capability(device) == (10, 0)
+
+
+class RowFP8Execution:
+    """Own precision choice and counters without changing any process globals.
+
+    Weight-only restores approximate weights for the ordinary GEMM. W8A8 uses
+    BF16 input, E4M3 activations/weights and FP32 per-row scales on SM100.
+    ``measure`` may supply asynchronous profiling scopes; this class inserts no
+    synchronization, model reads, environment changes or device selection.
+    """
+
+    def __init__(
+        self,
+        mode: str = "weight-only",
+        *,
+        activation_quantizer: str = "torch",
+        fast_accum: bool = False,
+        measure: Callable[[str], AbstractContextManager[Any]] | None = None,
+    ) -> None:
+        if activation_quantizer not in ("torch", "triton"):
+            raise ValueError("unknown FP8 activation quantizer")
+        if type(fast_accum) is not bool:
+            raise ValueError("fast_accum must be an explicit boolean")
+        self.activation_quantizer = activation_quantizer
+        self.fast_accum = fast_accum
+        self.measure = measure if measure is not None else lambda _name: nullcontext()
+        self.observer: Callable[[], None] | None = None
+        self.calls = {"weight_only": 0, "w8a8": 0}
+        self.select(mode)
+
+    def select(self, mode: str) -> None:
+        if mode not in ("weight-only", "w8a8"):
+            raise ValueError("unknown FP8 execution mode")
+        self.mode = mode
+
+    # -- validation shared by every entry point (h3_fp8_linear.py:70-87) -------
+    @staticmethod
+    def _validate(value, weight, scale, bias) -> None:
+        if (
+            weight.ndim != 2
+            or value.ndim < 1
+            or min(weight.shape) <= 0
+            or value.shape[-1] != weight.shape[1]
+            or weight.dtype != torch.float8_e4m3fn
+            or scale.dtype != torch.float32
+            or scale.shape != (weight.shape[0], 1)
+            or weight.device != value.device
+            or scale.device != value.device
+        ):
+            raise ValueError("FP8 codes/scales differ from the declared layout")
+        if bias is not None and (
+            bias.shape != (weight.shape[0],)
+            or bias.device != value.device
+            or bias.dtype != value.dtype
+        ):
+            raise ValueError("FP8 bias differs from the declared output")
+
+    @staticmethod
+    def _require_w8a8_device(value) -> None:
+        if value.dtype != torch.bfloat16 or not _on_sm100(value.device):
+            raise ValueError("W8A8 requires SM100 (B200) BF16 inputs")
+
+    def _observe(self) -> None:
+        if self.observer is not None and sum(self.calls.values()) % 200 == 0:
+            self.observer()
+
+    def _quantize(self, matrix):
+        with self.measure("linear.activation_quantize"):
+            return quantize_fp8_rows(matrix, pad_to=16)
+
+    def linear(self, value, weight, scale, bias=None):
+        self._observe()
+        self._validate(value, weight, scale, bias)
+        if self.mode == "weight-only":
+            self.calls["weight_only"] += 1
+            restored = (weight.float() * scale).to(value.dtype)
+            return torch.nn.functional.linear(value, restored, bias)
+        self._require_w8a8_device(value)
+        self.calls["w8a8"] += 1
+        shape = value.shape
+        matrix = value.reshape(-1, shape[-1])
+        rows = matrix.shape[0]
+        codes, act_scale = self._quantize(matrix)
+        with self.measure("linear.fp8_gemm"):
+            output = fp8_gemm(codes, act_scale, rows, weight, scale, Epilogue(bias=bias))
+        return output.reshape(*shape[:-1], weight.shape[0])
+
+    # -- fused entry points ------------------------------------------------------
+    def _fused_prologue(self, value, weight, scale, bias):
+        self._observe()
+        self._validate(value, weight, scale, bias)
+        if self.mode != "w8a8":
+            raise ValueError("fused FP8 epilogues require the w8a8 mode")
+        self._require_w8a8_device(value)
+        self.calls["w8a8"] += 1
+        matrix = value.reshape(-1, value.shape[-1])
+        return value.shape, matrix, matrix.shape[0]
+
+    def qkv_linear(self, value, weight, scale, bias=None, *, adapters=None, scalings=None):
+        """Merged QKV projection writing Q, K and V planes directly.
+
+        Equivalent to ``linear(value, weight, scale, bias).chunk(3, -1)``
+        (src/vflash/native/h3_native_denoiser.py:541) followed, when
+        ``adapters`` is given, by ``triton_strict_bf16_qkv_direct_merge``
+        (src/vflash/native/h3_fused_ops.py:954-979): per branch
+        ``bf16(base + bf16(adapter * scaling))``.  Returns three contiguous
+        ``[..., N/3]`` tensors that are views of one ``[3, rows, N/3]`` buffer.
+        """
+        shape, matrix, rows = self._fused_prologue(value, weight, scale, bias)
+        n = weight.shape[0]
+        if n % 3:
+            raise ValueError("merged QKV weight rows must be divisible by three")
+        width = n // 3
+        flat_adapters = None
+        scales = (0.0, 0.0, 0.0)
+        if adapters is not None:
+            if (not isinstance(adapters, tuple) or len(adapters) != 3 or scalings is None
+                    or len(scalings) != 3):
+                raise ValueError("QKV merge requires three adapters and three scalings")
+            flat_adapters = tuple(a.reshape(rows, width) for a in adapters)
+            scales = tuple(float(s) for s in scalings)
+        codes, act_scale = self._quantize(matrix)
+        with self.measure("linear.fp8_gemm"):
+            planes = fp8_gemm(codes, act_scale, rows, weight, scale,
+                              Epilogue(bias=bias, planes=3, adapters=flat_adapters, scalings=scales))
+        return tuple(planes[i].reshape(*shape[:-1], width) for i in range(3))
+
+    def gelu_linear(self, value, weight, scale, bias=None):
+        """``F.gelu(linear(...), approximate="tanh")`` with the GELU in the epilogue."""
+        shape, matrix, rows = self._fused_prologue(value, weight, scale, bias)
+        codes, act_scale = self._quantize(matrix)
+        with self.measure("linear.fp8_gemm"):
+            out = fp8_gemm(codes, act_scale, rows, weight, scale,
+                           Epilogue(kind=_lib.EPI_GELU_TANH, bias=bias))
+        return out.reshape(*shape[:-1], weight.shape[0])
+
+    def swiglu_linear(self, value, weight, scale, bias=None):
+        """Packed FFN input projection with ``value * bf16(silu(gate))`` fused.
+
+        ``weight`` is the packed ``[2F, K]`` ffn_in matrix (value rows first,
+        src/vflash/native/h3_native_denoiser.py:369-373); the result equals
+        ``triton_strict_bf16_silu_mul(linear(...))`` and has width F.
+        """
+        shape, matrix, rows = self._fused_prologue(value, weight, scale, bias)
+        if weight.shape[0] % 64:
+            raise ValueError("packed SwiGLU weight needs 2F rows with F % 32 == 0")
+        codes, act_scale = self._quantize(matrix)
+        with self.measure("linear.fp8_gemm"):
+            out = fp8_gemm(codes, act_scale, rows, weight, scale,
+                           Epilogue(kind=_lib.EPI_SWIGLU, bias=bias))
+        return out.reshape(*shape[:-1], weight.shape[0] // 2)
+
+    def gate_residual_linear(self, value, weight, scale, residual, gate=None, bias=None):
+        """``residual + bf16(gate * linear(...))`` fused (gate optional).
+
+        Matches ``triton_strict_bf16_gate_residual`` (h3_fused_ops.py:614-657)
+        applied to the linear output: ``residual`` is ``[B, S, N]`` and
+        ``gate`` ``[S, N]`` indexed by token; without ``gate`` it is a plain
+        BF16 residual add.
+        """
+        shape, matrix, rows = self._fused_prologue(value, weight, scale, bias)
+        n = weight.shape[0]
+        if residual.dtype != torch.bfloat16 or residual.shape != (*shape[:-1], n):
+            raise ValueError("FP8 residual differs from the declared output")
+        res = residual.reshape(rows, n)
+        tokens = 0
+        if gate is not None:
+            if gate.dtype != torch.bfloat16 or gate.ndim != 2 or gate.shape[1] != n:
+                raise ValueError("FP8 gate must be BF16 [S, N]")
+            tokens = gate.shape[0]
+            if len(shape) < 2 or shape[-2] != tokens:
+                raise ValueError("FP8 gate tokens differ from the activation")
+        codes, act_scale = self._quantize(matrix)
+        with self.measure("linear.fp8_gemm"):
+            out = fp8_gemm(codes, act_scale, rows, weight, scale,
+                           Epilogue(kind=_lib.EPI_RESIDUAL, bias=bias, residual=res, gate=gate,
+                                    tokens=tokens))
+        return out.reshape(*shape[:-1], n)
+
+    def ffn(self, value, up_weight, up_scale, down_weight, down_scale, *, activation="gelu_tanh",
+            up_bias=None, down_bias=None, residual=None, gate=None):
+        """Fused FFN: up GEMM + activation epilogue -> per-token e4m3 requant -> down GEMM.
+
+        ``activation`` is ``"gelu_tanh"`` (up weight ``[F, H]``) or ``"swiglu"``
+        (packed up weight ``[2F, H]``).  The down GEMM's epilogue adds
+        ``residual`` (and multiplies by ``gate`` first) when given.  The
+        bf16 intermediate is requantised per token over its full row, exactly
+        as the reference quantises the activation of the next linear
+        (src/vflash/native/h3_fp8_activation.py:16-19).
+        """
+        if (
+            down_weight.ndim != 2
+            or down_weight.dtype != torch.float8_e4m3fn
+            or down_scale.dtype != torch.float32
+            or down_scale.shape != (down_weight.shape[0], 1)
+            or down_weight.device != value.device
+            or down_scale.device != value.device
+        ):
+            raise ValueError("FP8 codes/scales differ from the declared layout")
+        if down_bias is not None and (
+            down_bias.shape != (down_weight.shape[0],)
+            or down_bias.device != value.device
+            or down_bias.dtype != value.dtype
+        ):
+            raise ValueError("FP8 bias differs from the declared output")
+        shape, matrix, rows = self._fused_prologue(value, up_weight, up_scale, up_bias)
+        hidden = down_weight.shape[0]
+        codes, act_scale = self._quantize(matrix)
+        with self.measure("linear.fp8_gemm"):
+            if activation == "gelu_tanh":
+                mid = fp8_gemm(codes, act_scale, rows, up_weight, up_scale,
+                               Epilogue(kind=_lib.EPI_GELU_TANH, bias=up_bias))
+            elif activation == "swiglu":
+                mid = fp8_gemm(codes, act_scale, rows, up_weight, up_scale,
+                               Epilogue(kind=_lib.EPI_SWIGLU, bias=up_bias))
+            else:
+                raise ValueError("unknown FFN activation")
+        if mid.shape[1] != down_weight.shape[1]:
+            raise ValueError("FFN down weight differs from the intermediate width")
+        mid_codes, mid_scale = self._quantize(mid)
+        self.calls["w8a8"] += 1
+        with self.measure("linear.fp8_gemm"):
+            if residual is None:
+                out = fp8_gemm(mid_codes, mid_scale, rows, down_weight, down_scale,
+                               Epilogue(bias=down_bias))
+            else:
+                if residual.dtype != torch.bfloat16 or residual.shape != (*shape[:-1], hidden):
+                    raise ValueError("FP8 residual differs from the declared output")
+                tokens = 0 if gate is None else gate.shape[0]
+                out = fp8_gemm(mid_codes, mid_scale, rows, down_weight, down_scale,
+                               Epilogue(kind=_lib.EPI_RESIDUAL, bias=down_bias,
+                                        residual=residual.reshape(rows, hidden), gate=gate,
+                                        tokens=tokens))
+        return out.reshape(*shape[:-1], hidden)
+
+
+class RowFP8Linear(torch.nn.Module):
+    """Meta-initialized Linear replacement; assign trusted codes and row_scale.
+
+    The original bias is preserved. A loader must assign all meta tensors before
+    execution, and retain the intended host/device placement of each module.
+    (Hansimov/vflash src/vflash/native/h3_fp8_linear.py:124-149.)
+    """
+
+    def __init__(self, original: torch.nn.Linear, execution: RowFP8Execution):
+        super().__init__()
+        self.in_features = original.in_features
+        self.out_features = original.out_features
+        self.weight = torch.nn.Parameter(
+            torch.empty(
+                (self.out_features, self.in_features), device="meta", dtype=torch.float8_e4m3fn
+            ),
+            requires_grad=False,
+        )
+        self.register_buffer(
+            "row_scale",
+            torch.empty((self.out_features, 1), device="meta", dtype=torch.float32),
+        )
+        self.bias = original.bias
+        self.execution = execution
+
+    def forward(self, value):
+        return self.execution.linear(value, self.weight, self.row_scale, self.bias)
