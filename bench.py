@@ -43,7 +43,6 @@ ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
 M, K, N_QKV, HEADS = 32760, 4096, 12288, 32
-FLOP_PER_STEP = 2.0 * M * N_QKV * K
 METRIC = "FP8/NVFP4 linear TFLOP/s/GPU & % of tcgen05 peak; DiT-block linear ms at 1-8 GPU"
 WORKLOAD = "c1 merged QKV FP8: X bf16 [32760,4096] -> e4m3 per-token, W e4m3 [12288,4096], bias, Q/K/V [32760,32,128]"
 NOMINAL_FP8_TFLOPS = 4500.0
@@ -69,29 +68,43 @@ def profile_traffic() -> float | None:
 
 
 class ClockSampler:
-    """Samples SM clocks and throttle reasons with nvidia-smi during the timed region."""
+    """Samples SM clocks and throttle reasons with nvidia-smi around the timed region.
 
-    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+    nvidia-smi needs about a second to start, so sampling starts before the
+    warm-up; ``mark_start``/``mark_end`` bracket the timed region and only
+    samples stamped inside it are summarised (the nearest sample when the
+    region is shorter than the sampling period).
+    """
+
+    QUERY = ("timestamp,index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
     def __init__(self, index: int):
         self.index = index
         self.proc = None
+        self.lines: list[str] = []
+        self.t0 = self.t1 = None
 
-    def __enter__(self):
+    def start(self):
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.QUERY}",
-                 "--format=csv,noheader,nounits", "-lms", "100"],
+                 "--format=csv,noheader,nounits", "-lms", "20"],
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except OSError:
             self.proc = None
         return self
 
-    def __exit__(self, *exc):
-        self.lines = []
+    def mark_start(self):
+        self.t0 = time.time()
+
+    def mark_end(self):
+        self.t1 = time.time()
+
+    def stop(self):
         if self.proc is not None:
+            time.sleep(0.1)
             self.proc.terminate()
             try:
                 out, _ = self.proc.communicate(timeout=5)
@@ -101,25 +114,33 @@ class ClockSampler:
             self.lines = [line for line in out.splitlines() if line.strip()]
 
     def summary(self) -> dict:
-        clocks, max_clock, reasons = [], None, set()
+        import datetime
+
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for line in getattr(self, "lines", []):
+        samples = []
+        for line in self.lines:
             parts = [p.strip() for p in line.split(",")]
-            if len(parts) < 9:
+            if len(parts) < 10:
                 continue
             try:
-                clocks.append(float(parts[1]))
-                max_clock = float(parts[2])
+                stamp = datetime.datetime.strptime(parts[0], "%Y/%m/%d %H:%M:%S.%f").timestamp()
+                samples.append((stamp, float(parts[2]), float(parts[3]), float(parts[4]),
+                                [n for n, f in zip(names, parts[6:10]) if f.lower() == "active"]))
             except ValueError:
                 continue
-            for name, flag in zip(names, parts[5:9]):
-                if flag.lower() == "active":
-                    reasons.add(name)
-        return {"sm_mhz": statistics.median(clocks) if clocks else None, "sm_max_mhz": max_clock,
-                "reasons": sorted(reasons), "samples": len(clocks)}
+        if not samples or self.t0 is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        inside = [s for s in samples if self.t0 <= s[0] <= self.t1]
+        if not inside:
+            mid = 0.5 * (self.t0 + self.t1)
+            inside = [min(samples, key=lambda s: abs(s[0] - mid))]
+        reasons = sorted({r for s in inside for r in s[4]})
+        return {"sm_mhz": statistics.median(s[1] for s in inside), "sm_max_mhz": inside[0][2],
+                "power_w_max": max(s[3] for s in inside), "reasons": reasons,
+                "samples": len(inside)}
 
 
-def synthetic_workload(device: torch.device, rank: int):
+def synthetic_workload(device: torch.device, rank: int, M: int):
     """Seeded inputs of BASELINE config 1 (seeds X 1001, W 2010, bias 3001; offset by rank)."""
     gen = torch.Generator().manual_seed(1001 + 97 * rank)
     x = torch.randn(M, K, generator=gen)
@@ -138,10 +159,38 @@ def synthetic_workload(device: torch.device, rank: int):
     return x, w_codes, w_scales, bias.to(device)
 
 
+def run_e2e(args, M, x_host, w_codes, w_scales, bias, device, stream, barrier):
+    """Same step through the public drop-in API, host (pinned) buffers in and out."""
+    from vflash_b200.native.h3_fp8_linear import RowFP8Execution
+
+    execution = RowFP8Execution("w8a8", activation_quantizer="triton")
+    x_pinned = x_host.pin_memory()
+    x_dev = torch.empty(x_host.shape, dtype=x_host.dtype, device=device)
+    head_dim = K // HEADS
+    outs_host = [torch.empty((M, HEADS, head_dim), dtype=torch.bfloat16).pin_memory() for _ in range(3)]
+
+    def e2e_step():
+        x_dev.copy_(x_pinned, non_blocking=True)
+        q, k, v = execution.qkv_linear(x_dev, w_codes, w_scales, bias)
+        for host, plane in zip(outs_host, (q, k, v)):
+            host.copy_(plane.view(M, HEADS, head_dim), non_blocking=True)
+
+    for _ in range(args.warmup):
+        e2e_step()
+    barrier()
+    steps = max(3, min(args.steps, 10))
+    s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s0.record(stream)
+    for _ in range(steps):
+        e2e_step()
+    s1.record(stream)
+    barrier()
+    return s0.elapsed_time(s1), steps
+
+
 def run_gpu(args) -> None:
     from vflash_b200 import _lib
     from vflash_b200.kernels import Epilogue, fp8_gemm, quantize_fp8_rows
-    from vflash_b200.native.h3_fp8_linear import RowFP8Execution
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -163,7 +212,16 @@ def run_gpu(args) -> None:
             torch.distributed.barrier()
         torch.cuda.synchronize(device)
 
-    x_host, w_codes, w_scales, bias = synthetic_workload(device, rank)
+    def max_over_ranks(value: float) -> float:
+        if not distributed:
+            return value
+        t = torch.tensor([value], device=device)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        return t.item()
+
+    M = args.rows
+    flop_per_step = 2.0 * M * N_QKV * K
+    x_host, w_codes, w_scales, bias = synthetic_workload(device, rank, M)
     x = x_host.to(device)
     flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=device)
     stream = torch.cuda.current_stream(device)
@@ -175,56 +233,32 @@ def run_gpu(args) -> None:
         fp8_gemm(codes, scales, M, w_codes, w_scales, Epilogue(bias=bias, planes=3))
         ev[2].record(stream)
 
+    clocks = ClockSampler(local_rank).start()
     for _ in range(args.warmup):
         step([torch.cuda.Event(enable_timing=True) for _ in range(3)])
     barrier()
+    time.sleep(1.0)  # nvidia-smi is sampling by now
     events = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(args.steps)]
-    with ClockSampler(local_rank) as clocks:
-        barrier()
-        wall0 = time.perf_counter()
-        for i in range(args.steps):
-            flush.fill_(float(i))
-            step(events[i])
-        barrier()
-        wall = time.perf_counter() - wall0
+    barrier()
+    clocks.mark_start()
+    wall0 = time.perf_counter()
+    for i in range(args.steps):
+        flush.fill_(float(i))
+        step(events[i])
+    barrier()
+    wall = time.perf_counter() - wall0
+    clocks.mark_end()
+    clocks.stop()
     step_ms = [e[0].elapsed_time(e[2]) for e in events]
     quant_ms = [e[0].elapsed_time(e[1]) for e in events]
     gemm_ms = [e[1].elapsed_time(e[2]) for e in events]
-    total_ms = sum(step_ms)
-    if distributed:
-        t = torch.tensor([total_ms], device=device)
-        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-        total_ms = t.item()
+    total_ms = max_over_ranks(sum(step_ms))
     status = _lib.device_status(clear=True)
 
-    # ---- e2e through the public API with host buffers -----------------------
-    execution = RowFP8Execution("w8a8", activation_quantizer="triton")
-    x_pinned = x_host.pin_memory()
-    x_dev = torch.empty_like(x)
-    outs_host = [torch.empty((M, HEADS, K // HEADS), dtype=torch.bfloat16).pin_memory() for _ in range(3)]
-    w_e2e = w_codes
-
-    def e2e_step():
-        x_dev.copy_(x_pinned, non_blocking=True)
-        q, k, v = execution.qkv_linear(x_dev, w_e2e, w_scales, bias)
-        for host, plane in zip(outs_host, (q, k, v)):
-            host.copy_(plane.view(M, HEADS, K // HEADS), non_blocking=True)
-
-    for _ in range(max(1, args.warmup)):
-        e2e_step()
-    barrier()
-    e2e_steps = max(3, min(args.steps, 10))
-    s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    s0.record(stream)
-    for _ in range(e2e_steps):
-        e2e_step()
-    s1.record(stream)
-    barrier()
-    e2e_ms = s0.elapsed_time(s1)
-    if distributed:
-        t = torch.tensor([e2e_ms], device=device)
-        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-        e2e_ms = t.item()
+    e2e_ms, e2e_steps = float("nan"), 0
+    if not args.no_e2e:
+        e2e_ms, e2e_steps = run_e2e(args, M, x_host, w_codes, w_scales, bias, device, stream, barrier)
+        e2e_ms = max_over_ranks(e2e_ms)
 
     library = None
     if rank == 0 and not args.no_library_probe:
@@ -246,11 +280,10 @@ def run_gpu(args) -> None:
         peak = 2.0 * 1590.0
         peak_src = "2 x fallback bf16 1.59 PFLOP/s"
     gemm_mean = statistics.mean(gemm_ms)
-    achieved = FLOP_PER_STEP / (gemm_mean * 1e-3) / 1e12
-    value = world * args.steps * FLOP_PER_STEP / (total_ms * 1e-3) / 1e12
-    e2e_value = world * e2e_steps * FLOP_PER_STEP / (e2e_ms * 1e-3) / 1e12
+    achieved = flop_per_step / (gemm_mean * 1e-3) / 1e12
+    value = world * args.steps * flop_per_step / (total_ms * 1e-3) / 1e12
     quant_mean = statistics.mean(quant_ms)
-    quant_bytes = M * K * 2 + M * K + 32768 * 4
+    quant_bytes = M * K * 2 + M * K + (M + 15) // 16 * 16 * 4
     hbm = float(peaks.get("hbm_gbs", 6650.0))
     line = {
         "metric": METRIC,
@@ -265,7 +298,8 @@ def run_gpu(args) -> None:
         "vs_baseline": None,
         "dtype": "e4m3 x e4m3 -> fp32 acc -> bf16",
         "data": "synthetic (seeded N(0,1) activations with 0.1% x20 outliers; N(0,0.02) weights, per-row e4m3)",
-        "config": {"workload": WORKLOAD, "M": M, "N": N_QKV, "K": K, "bias": True,
+        "config": {"workload": WORKLOAD if M == 32760 else f"profiling case: c1 with M={M}",
+                   "M": M, "N": N_QKV, "K": K, "bias": True,
                    "l2": "flushed between steps (256 MB buffer written outside the timed events)",
                    "parallelism": f"token-sharded dp{world} (weights replicated)",
                    "step": "fp8 quantiser + tcgen05 GEMM with QKV-plane epilogue"},
@@ -274,17 +308,20 @@ def run_gpu(args) -> None:
                      "kernel": "fp8_gemm_kernel<STORE> (QKV planes)", "peak_source": peak_src,
                      "frac_of_nominal_4500": round(achieved / NOMINAL_FP8_TFLOPS, 4),
                      "gemm_ms": round(gemm_mean, 4)},
-        "quantiser": {"ms": round(quant_mean, 4), "gb_per_s": round(quant_bytes / (quant_mean * 1e-3) / 1e9, 1),
+        "quantiser": {"ms": round(quant_mean, 4),
+                      "gb_per_s": round(quant_bytes / (quant_mean * 1e-3) / 1e9, 1),
                       "frac_of_measured_hbm": round(quant_bytes / (quant_mean * 1e-3) / 1e9 / hbm, 4)},
-        "e2e": {"value": round(e2e_value, 2), "unit": "TFLOP/s",
-                "h2d_bytes_per_step": M * K * 2, "d2h_bytes_per_step": 3 * M * (N_QKV // 3) * 2,
-                "api": "RowFP8Execution('w8a8').qkv_linear, pinned host in/out",
-                "ms_per_step": round(e2e_ms / e2e_steps, 3)},
         "gpu_launches": 2 * args.steps,
         "clocks": clocks.summary(),
         "wall_s_timed_region": round(wall, 3),
         "device_status": status,
     }
+    if e2e_steps:
+        line["e2e"] = {"value": round(world * e2e_steps * flop_per_step / (e2e_ms * 1e-3) / 1e12, 2),
+                       "unit": "TFLOP/s", "h2d_bytes_per_step": M * K * 2,
+                       "d2h_bytes_per_step": M * N_QKV * 2,
+                       "api": "RowFP8Execution('w8a8').qkv_linear, pinned host in/out",
+                       "ms_per_step": round(e2e_ms / e2e_steps, 3)}
     if library is not None:
         line["library_fp8_tflops"] = library
     if cpu is not None:
@@ -409,13 +446,16 @@ def run_reference(args) -> None:
 def main() -> None:
     parser = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     parser.add_argument("--gpus", type=int, default=1)
-    parser.add_argument("--steps", type=int, default=20)
+    parser.add_argument("--steps", type=int, default=50)
     parser.add_argument("--warmup", type=int, default=5)
     parser.add_argument("--impl", choices=["vflash_b200", "reference"], default="vflash_b200")
     parser.add_argument("--cpu-seconds", type=float, default=10.0)
     parser.add_argument("--reference-rows", type=int, default=1024)
     parser.add_argument("--no-cpu-baseline", action="store_true")
     parser.add_argument("--no-library-probe", action="store_true")
+    parser.add_argument("--no-e2e", action="store_true")
+    parser.add_argument("--rows", type=int, default=M,
+                        help="token rows M (default 32760 = BASELINE config 1; smaller only for profiling)")
     args = parser.parse_args()
     args.warmup = max(3, args.warmup)  # the timing rules require >= 3 warm-up steps
     if args.impl == "reference":

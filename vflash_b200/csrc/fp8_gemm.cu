@@ -32,22 +32,26 @@
 namespace vfb {
 namespace {
 
-constexpr int BM = 128;
-constexpr int BN = 256;
-constexpr int BK = 128;  // bytes = e4m3 elements per stage
+constexpr int BM = 128;       // A rows per CTA (a CTA pair covers 256 rows)
+constexpr int BN = 256;       // output columns per pair tile
+constexpr int BN_HALF = BN / 2;  // weight rows each CTA of the pair loads
+constexpr int BK = 128;       // bytes = e4m3 elements per stage
 constexpr int UMMA_K = 32;
-constexpr int STAGES = 4;
-constexpr int A_STAGE_BYTES = BM * BK;  // 16 KB
-constexpr int B_STAGE_BYTES = BN * BK;  // 32 KB
+constexpr int STAGES = 5;
+constexpr int A_STAGE_BYTES = BM * BK;       // 16 KB
+constexpr int B_STAGE_BYTES = BN_HALF * BK;  // 16 KB
 constexpr int NUM_THREADS = 192;
 constexpr int TMEM_COLS = 512;
-constexpr size_t SMEM_BYTES = 1024 + STAGES * (A_STAGE_BYTES + B_STAGE_BYTES) + 256;
+// Epilogue staging: per epilogue warp a ring of EPI_BOXES 32 x 32 bf16 boxes
+// (2 KB each), so TMA stores drain while the warp fills the next boxes.
+constexpr int EPI_BOXES = 4;
+constexpr int EPI_BOX_BYTES = 32 * 32 * 2;
+constexpr int EPI_SMEM_BYTES = 4 * EPI_BOXES * EPI_BOX_BYTES;
+constexpr size_t SMEM_BYTES =
+    1024 + STAGES * (A_STAGE_BYTES + B_STAGE_BYTES) + EPI_SMEM_BYTES + 256;
 
 struct EpiParams {
-  __nv_bfloat16 *out;
-  int64_t ldo;
-  int64_t plane_width;
-  int64_t plane_stride;
+  int32_t plane_width;  // columns per output plane (N when there is one plane)
   const __nv_bfloat16 *bias;
   const __nv_bfloat16 *adapter[3];
   int64_t adapter_ld;
@@ -58,7 +62,6 @@ struct EpiParams {
   int64_t gate_ts;
   int64_t gate_hs;
   int64_t tokens;
-  int64_t ffn_width;  // SWIGLU: F (value columns [0,F), gate columns [F,2F))
 };
 
 struct GemmParams {
@@ -125,6 +128,37 @@ __device__ __forceinline__ void store_bf16x32(__nv_bfloat16 *p, const float (&y)
   }
 }
 
+// Writes one 32 x 32 output box: lane i holds row i of the warp's 32 rows.
+// The rows go to shared memory in the 64-byte swizzle the output tensor map
+// uses (conflict-free 16-byte stores), then lane 0 issues one TMA store.
+// Each warp cycles through EPI_BOXES staging boxes; a box is rewritten only
+// after the store issued from it EPI_BOXES chunks earlier has read it.
+__device__ __forceinline__ void store_box(uint8_t *warp_smem, int &box, const CUtensorMap *map,
+                                          const float (&y)[32], int lane, int32_t col, int32_t row0,
+                                          int32_t plane, bool any_row) {
+  uint8_t *buf = warp_smem + box * EPI_BOX_BYTES;
+  if (lane == 0) bulk_wait_group_read<EPI_BOXES - 1>();
+  __syncwarp();
+  uint4 *row = reinterpret_cast<uint4 *>(buf + lane * 64);
+  const int sw = (lane >> 1) & 3;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    uint4 t;
+    t.x = pack_bf16x2(y[8 * j + 0], y[8 * j + 1]);
+    t.y = pack_bf16x2(y[8 * j + 2], y[8 * j + 3]);
+    t.z = pack_bf16x2(y[8 * j + 4], y[8 * j + 5]);
+    t.w = pack_bf16x2(y[8 * j + 6], y[8 * j + 7]);
+    row[j ^ sw] = t;
+  }
+  fence_proxy_async_smem();
+  __syncwarp();
+  if (lane == 0 && any_row) {
+    tma_store_3d(map, buf, col, row0, plane);
+    bulk_commit_group();
+  }
+  box = box + 1 == EPI_BOXES ? 0 : box + 1;
+}
+
 // y = bf16(acc * sa * sw) then bf16(y + bias): the _scaled_mm output followed
 // by the separate bias add of the reference.
 __device__ __forceinline__ void scale_bias(float (&v)[32], float sa, const float *sw,
@@ -144,13 +178,15 @@ __device__ __forceinline__ void scale_bias(float (&v)[32], float sa, const float
 template <int EPI>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     fp8_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                    const __grid_constant__ CUtensorMap tmB2, const GemmParams p) {
+                    const __grid_constant__ CUtensorMap tmB2, const __grid_constant__ CUtensorMap tmOut,
+                    const GemmParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                               ~static_cast<uintptr_t>(1023));
   uint8_t *sA = smem;
   uint8_t *sB = smem + STAGES * A_STAGE_BYTES;
-  uint64_t *full_bar = reinterpret_cast<uint64_t *>(sB + STAGES * B_STAGE_BYTES);
+  uint8_t *sEpi = sB + STAGES * B_STAGE_BYTES;
+  uint64_t *full_bar = reinterpret_cast<uint64_t *>(sEpi + EPI_SMEM_BYTES);
   uint64_t *empty_bar = full_bar + STAGES;
   uint64_t *tfull_bar = empty_bar + STAGES;
   uint64_t *tempty_bar = tfull_bar + 2;
@@ -160,15 +196,18 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 
   const int warp = threadIdx.x / 32;
   const int lane = threadIdx.x % 32;
+  const uint32_t rank = cluster_ctarank();  // 0 = leader of the CTA pair
+  const int pair = blockIdx.x / 2;
+  const int num_pairs = gridDim.x / 2;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
-      mbar_init(&full_bar[s], 1);
-      mbar_init(&empty_bar[s], 1);
+      mbar_init(&full_bar[s], 1);   // leader: one expect_tx arrival + both CTAs' bytes
+      mbar_init(&empty_bar[s], 1);  // one commit from the leader's MMA thread
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tfull_bar[a], 1);
-      mbar_init(&tempty_bar[a], 128);
+      mbar_init(&tempty_bar[a], 2 * 128);  // leader: every epilogue thread of both CTAs
     }
     mbar_init(drain_bar, 1);
     *abort_flag = 0;
@@ -179,12 +218,14 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     tma_prefetch_desc(&tmB);
     if (EPI == VFB_EPI_SWIGLU) tma_prefetch_desc(&tmB2);
   }
+  if (warp == 2 && lane == 0) tma_prefetch_desc(&tmOut);
   if (warp == 1) {
-    tmem_alloc(tmem_slot, TMEM_COLS);
-    tmem_relinquish();
+    tmem_alloc_pair(tmem_slot, TMEM_COLS);
+    tmem_relinquish_pair();
   }
   tc_fence_before();
   __syncthreads();
+  cluster_sync();  // the peer's barriers are initialised before any remote arrival
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
@@ -192,29 +233,32 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 
   if (warp == 0) {
     if (lane == 0) {
-      // ---------------- TMA producer ----------------
+      // ---------------- TMA producer (both CTAs) ----------------
       int s = 0;
       uint32_t ph = 0;
       uint32_t issued_phase[STAGES];
       bool issued[STAGES];
       for (int i = 0; i < STAGES; ++i) issued[i] = false;
       bool ok = true;
-      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+      for (int tile = pair; tile < num_tiles && ok; tile += num_pairs) {
         const int m_tile = tile / p.num_n_tiles;
         const int n_tile = tile % p.num_n_tiles;
+        const int32_t a_row = m_tile * (2 * BM) + static_cast<int32_t>(rank) * BM;
         for (int kb = 0; kb < p.num_kb; ++kb) {
           if (!mbar_wait(&empty_bar[s], ph ^ 1, abort_flag, p.status)) {
             ok = false;
             break;
           }
-          mbar_arrive_expect_tx(&full_bar[s], A_STAGE_BYTES + B_STAGE_BYTES);
-          tma_load_2d(sA + s * A_STAGE_BYTES, &tmA, &full_bar[s], kb * BK, m_tile * BM);
+          const uint32_t full_leader = map_to_rank(smem_u32(&full_bar[s]), 0);
+          if (rank == 0) mbar_arrive_expect_tx(&full_bar[s], 2 * (A_STAGE_BYTES + B_STAGE_BYTES));
+          tma_load_2d_pair(sA + s * A_STAGE_BYTES, &tmA, full_leader, kb * BK, a_row);
           if (EPI == VFB_EPI_SWIGLU) {
-            tma_load_2d(sB + s * B_STAGE_BYTES, &tmB, &full_bar[s], kb * BK, n_tile * (BN / 2));
-            tma_load_2d(sB + s * B_STAGE_BYTES + B_STAGE_BYTES / 2, &tmB2, &full_bar[s], kb * BK,
-                        n_tile * (BN / 2));
+            // leader: value rows [n*128, +128); peer: the matching gate rows
+            tma_load_2d_pair(sB + s * B_STAGE_BYTES, rank == 0 ? &tmB : &tmB2, full_leader,
+                             kb * BK, n_tile * BN_HALF);
           } else {
-            tma_load_2d(sB + s * B_STAGE_BYTES, &tmB, &full_bar[s], kb * BK, n_tile * BN);
+            tma_load_2d_pair(sB + s * B_STAGE_BYTES, &tmB, full_leader, kb * BK,
+                             n_tile * BN + static_cast<int32_t>(rank) * BN_HALF);
           }
           issued[s] = true;
           issued_phase[s] = ph;
@@ -224,19 +268,20 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           }
         }
       }
-      // Drain: every load this thread issued has landed before the CTA exits.
-      for (int i = 0; i < STAGES; ++i)
-        if (issued[i]) mbar_wait(&full_bar[i], issued_phase[i], abort_flag, p.status);
+      // Drain: the leader waits until every load it accounted has landed.
+      if (rank == 0)
+        for (int i = 0; i < STAGES; ++i)
+          if (issued[i]) mbar_wait(&full_bar[i], issued_phase[i], abort_flag, p.status);
     }
   } else if (warp == 1) {
-    if (lane == 0) {
-      // ---------------- MMA issuer ----------------
-      constexpr uint32_t idesc = idesc_e4m3_f32(BM, BN);
+    if (lane == 0 && rank == 0) {
+      // ---------------- MMA issuer (leader CTA only) ----------------
+      constexpr uint32_t idesc = idesc_e4m3_f32(2 * BM, BN);
       int s = 0;
       uint32_t ph = 0;
       int t = 0;
       bool ok = true;
-      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x, ++t) {
+      for (int tile = pair; tile < num_tiles && ok; tile += num_pairs, ++t) {
         const int acc = t & 1;
         const uint32_t acc_ph = (t >> 1) & 1;
         if (!mbar_wait(&tempty_bar[acc], acc_ph ^ 1, abort_flag, p.status)) break;
@@ -253,108 +298,120 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 #pragma unroll
           for (int k = 0; k < BK / UMMA_K; ++k) {
             // +32 bytes along K inside the swizzled 128-byte row = +2 in 16-byte units.
-            mma_f8f6f4(d_tmem, a_desc + 2 * k, b_desc + 2 * k, idesc, (kb | k) != 0);
+            mma_f8f6f4_pair(d_tmem, a_desc + 2 * k, b_desc + 2 * k, idesc, (kb | k) != 0);
           }
-          tc_commit(&empty_bar[s]);
+          tc_commit_pair(smem_u32(&empty_bar[s]));
+          tc_commit_pair(map_to_rank(smem_u32(&empty_bar[s]), 1));
           if (++s == STAGES) {
             s = 0;
             ph ^= 1;
           }
         }
         if (!ok) break;
-        tc_commit(&tfull_bar[acc]);
+        tc_commit_pair(smem_u32(&tfull_bar[acc]));
+        tc_commit_pair(map_to_rank(smem_u32(&tfull_bar[acc]), 1));
       }
       // Drain: all MMAs issued by this thread are complete before TMEM is freed.
-      tc_commit(drain_bar);
+      tc_commit_pair(smem_u32(drain_bar));
       mbar_wait(drain_bar, 0, abort_flag, p.status);
     }
   } else {
-    // ---------------- epilogue (warps 2..5) ----------------
+    // ---------------- epilogue (warps 2..5 of both CTAs) ----------------
     const int q = warp & 3;  // TMEM lane quarter this warp may access
     const int row = q * 32 + lane;
     const EpiParams &ep = p.ep;
+    uint8_t *warp_smem = sEpi + q * EPI_BOXES * EPI_BOX_BYTES;
+    int box = 0;
     int t = 0;
-    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++t) {
+    for (int tile = pair; tile < num_tiles; tile += num_pairs, ++t) {
       const int acc = t & 1;
       const uint32_t acc_ph = (t >> 1) & 1;
       if (!mbar_wait(&tfull_bar[acc], acc_ph, abort_flag, p.status)) break;
       tc_fence_after();
       const int m_tile = tile / p.num_n_tiles;
       const int n_tile = tile % p.num_n_tiles;
-      const int64_t m = static_cast<int64_t>(m_tile) * BM + row;
+      const int64_t row0 = static_cast<int64_t>(m_tile) * (2 * BM) + rank * BM + q * 32;
+      const int64_t m = row0 + lane;
       const bool live = m < p.M;
+      const bool any_row = row0 < p.M;  // warp-uniform
       const float sa = live ? __ldg(p.sa + m) : 0.0f;
       const uint32_t t_row = tmem_base + acc * BN + (static_cast<uint32_t>(q * 32) << 16);
 
       if (EPI == VFB_EPI_SWIGLU) {
-        const int64_t F = ep.ffn_width;
+        const int32_t F = ep.plane_width;
 #pragma unroll 1
-        for (int c = 0; c < BN / 2 / 32; ++c) {
-          const int64_t f = static_cast<int64_t>(n_tile) * (BN / 2) + c * 32;
+        for (int c = 0; c < BN_HALF / 32; ++c) {
+          const int32_t f = n_tile * BN_HALF + c * 32;
           if (f >= F) break;  // warp-uniform
           float v[32], g[32];
           tmem_ld_32x32b_x32(t_row + c * 32, v);
-          tmem_ld_32x32b_x32(t_row + BN / 2 + c * 32, g);
+          tmem_ld_32x32b_x32(t_row + BN_HALF + c * 32, g);
           if (live) {
             scale_bias(v, sa, p.sw + f, ep.bias ? ep.bias + f : nullptr);
             scale_bias(g, sa, p.sw + F + f, ep.bias ? ep.bias + F + f : nullptr);
 #pragma unroll
             for (int j = 0; j < 32; ++j) v[j] = v[j] * bf16r(silu(g[j]));
-            store_bf16x32(ep.out + m * ep.ldo + f, v);
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) v[j] = 0.0f;
           }
+          store_box(warp_smem, box, &tmOut, v, lane, f, static_cast<int32_t>(row0), 0, any_row);
         }
       } else {
 #pragma unroll 1
         for (int c = 0; c < BN / 32; ++c) {
-          const int64_t n = static_cast<int64_t>(n_tile) * BN + c * 32;
+          const int32_t n = n_tile * BN + c * 32;
           if (n >= p.N) break;  // warp-uniform
           float v[32];
           tmem_ld_32x32b_x32(t_row + c * 32, v);
+          const int32_t plane = n / ep.plane_width;
+          const int32_t col = n - plane * ep.plane_width;
           if (live) {
-          scale_bias(v, sa, p.sw + n, ep.bias ? ep.bias + n : nullptr);
-          int64_t plane = 0, col = n;
-          if (ep.plane_width > 0) {
-            plane = n / ep.plane_width;
-            col = n - plane * ep.plane_width;
-          }
-          __nv_bfloat16 *dst = ep.out + plane * ep.plane_stride + m * ep.ldo + col;
-          if (EPI == VFB_EPI_STORE) {
-            const __nv_bfloat16 *ad = plane < 3 ? ep.adapter[plane] : nullptr;
-            if (ad != nullptr) {
-              float a[32];
-              load_bf16x32(ad + m * ep.adapter_ld + col, a);
-              const float sc = ep.scaling[plane];
+            scale_bias(v, sa, p.sw + n, ep.bias ? ep.bias + n : nullptr);
+            if (EPI == VFB_EPI_STORE) {
+              const __nv_bfloat16 *ad = plane < 3 ? ep.adapter[plane] : nullptr;
+              if (ad != nullptr) {
+                float a[32];
+                load_bf16x32(ad + m * ep.adapter_ld + col, a);
+                const float sc = ep.scaling[plane];
 #pragma unroll
-              for (int j = 0; j < 32; ++j) v[j] = v[j] + bf16r(a[j] * sc);
+                for (int j = 0; j < 32; ++j) v[j] = v[j] + bf16r(a[j] * sc);
+              }
+            } else if (EPI == VFB_EPI_GELU_TANH) {
+#pragma unroll
+              for (int j = 0; j < 32; ++j) v[j] = gelu_tanh(v[j]);
+            } else if (EPI == VFB_EPI_RESIDUAL) {
+              if (ep.gate != nullptr) {
+                const __nv_bfloat16 *gp = ep.gate + (m % ep.tokens) * ep.gate_ts + n * ep.gate_hs;
+#pragma unroll
+                for (int j = 0; j < 32; ++j)
+                  v[j] = bf16r(__bfloat162float(gp[j * ep.gate_hs]) * v[j]);
+              }
+              float r[32];
+              load_bf16x32(ep.residual + m * ep.ldr + n, r);
+#pragma unroll
+              for (int j = 0; j < 32; ++j) v[j] = r[j] + v[j];
             }
-          } else if (EPI == VFB_EPI_GELU_TANH) {
+          } else {
 #pragma unroll
-            for (int j = 0; j < 32; ++j) v[j] = gelu_tanh(v[j]);
-          } else if (EPI == VFB_EPI_RESIDUAL) {
-            if (ep.gate != nullptr) {
-              const __nv_bfloat16 *gp = ep.gate + (m % ep.tokens) * ep.gate_ts + n * ep.gate_hs;
-#pragma unroll
-              for (int j = 0; j < 32; ++j) v[j] = bf16r(__bfloat162float(gp[j * ep.gate_hs]) * v[j]);
-            }
-            float r[32];
-            load_bf16x32(ep.residual + m * ep.ldr + n, r);
-#pragma unroll
-            for (int j = 0; j < 32; ++j) v[j] = r[j] + v[j];
+            for (int j = 0; j < 32; ++j) v[j] = 0.0f;
           }
-          store_bf16x32(dst, v);
-          }
+          store_box(warp_smem, box, &tmOut, v, lane, col, static_cast<int32_t>(row0), plane, any_row);
         }
       }
       tc_fence_before();
-      mbar_arrive(&tempty_bar[acc]);
+      mbar_arrive_cluster(map_to_rank(smem_u32(&tempty_bar[acc]), 0));
     }
+    if (lane == 0) bulk_wait_group_all();  // output stores complete before the CTA exits
   }
 
   __syncthreads();
+  __syncwarp();
+  cluster_sync();  // both CTAs are done with TMEM before the pair frees it
   if (warp == 1) {
     __syncwarp();
     tc_fence_after();
-    tmem_dealloc(tmem_base, TMEM_COLS);
+    tmem_dealloc_pair(tmem_base, TMEM_COLS);
   }
 }
 
@@ -394,20 +451,53 @@ int make_map_u8(CUtensorMap *map, const void *base, int64_t rows, int64_t cols, 
   return VFB_OK;
 }
 
+// Tensor map over the bf16 output viewed as [planes][rows][width] (row stride
+// ld elements, plane stride plane_stride elements), 32 x 32 boxes with the
+// 64-byte swizzle the epilogue writes its staging boxes in.
+int make_map_out(CUtensorMap *map, void *base, int64_t width, int64_t rows, int64_t planes,
+                 int64_t ld, int64_t plane_stride) {
+  auto encode = tensor_map_encoder();
+  if (encode == nullptr) return set_error(VFB_ECUDA, "cuTensorMapEncodeTiled is unavailable");
+  cuuint64_t dims[3] = {static_cast<cuuint64_t>(width), static_cast<cuuint64_t>(rows),
+                        static_cast<cuuint64_t>(planes)};
+  cuuint64_t strides[2] = {static_cast<cuuint64_t>(ld) * 2, static_cast<cuuint64_t>(plane_stride) * 2};
+  cuuint32_t box[3] = {32, 32, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, base, dims, strides, box, estr,
+                      CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B,
+                      CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return set_error(VFB_ECUDA, "cuTensorMapEncodeTiled (output) failed (%d)", static_cast<int>(r));
+  return VFB_OK;
+}
+
 bool aligned16(const void *ptr) { return reinterpret_cast<uintptr_t>(ptr) % 16 == 0; }
 
 template <int EPI>
-int launch(const CUtensorMap &a, const CUtensorMap &b, const CUtensorMap &b2, const GemmParams &p,
-           int sm_count, cudaStream_t stream) {
+int launch(const CUtensorMap &a, const CUtensorMap &b, const CUtensorMap &b2, const CUtensorMap &o,
+           const GemmParams &p, int sm_count, cudaStream_t stream) {
   auto kernel = fp8_gemm_kernel<EPI>;
   cudaError_t err =
       cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
   if (err != cudaSuccess)
     return set_error(VFB_ECUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(err));
+  // Persistent grid of CTA pairs, one CTA per SM.
   const int tiles = p.num_m_tiles * p.num_n_tiles;
-  const int grid = tiles < sm_count ? tiles : sm_count;
-  kernel<<<grid, NUM_THREADS, SMEM_BYTES, stream>>>(a, b, b2, p);
-  err = cudaGetLastError();
+  const int max_pairs = sm_count / 2;
+  const int pairs = tiles < max_pairs ? tiles : max_pairs;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(2 * pairs, 1, 1);
+  cfg.blockDim = dim3(NUM_THREADS, 1, 1);
+  cfg.dynamicSmemBytes = SMEM_BYTES;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  err = cudaLaunchKernelEx(&cfg, kernel, a, b, b2, o, p);
   if (err != cudaSuccess)
     return set_error(VFB_ECUDA, "vfb_fp8_gemm launch: %s", cudaGetErrorString(err));
   return VFB_OK;
@@ -429,7 +519,7 @@ extern "C" int vfb_fp8_gemm(const void *A, int64_t lda, const float *sa, const v
                                  "K %% 16 == 0 (M=%lld N=%lld K=%lld)",
                      (long long)M, (long long)N, (long long)K);
   if (M == 0) return VFB_OK;
-  if (M > (int64_t)BM * 0x7FFFFF || N > (int64_t)1 << 24 || K > (int64_t)1 << 20)
+  if (M > (int64_t)2 * BM * 0x3FFFFF || N > (int64_t)1 << 24 || K > (int64_t)1 << 20)
     return set_error(VFB_EINVAL, "vfb_fp8_gemm: problem too large");
   if (A == nullptr || W == nullptr || sa == nullptr || sw == nullptr || ep->out == nullptr)
     return set_error(VFB_EINVAL, "vfb_fp8_gemm: NULL operand");
@@ -450,15 +540,13 @@ extern "C" int vfb_fp8_gemm(const void *A, int64_t lda, const float *sa, const v
   p.K = K;
   p.sa = sa;
   p.sw = sw;
-  p.num_m_tiles = static_cast<int>((M + BM - 1) / BM);
+  p.num_m_tiles = static_cast<int>((M + 2 * BM - 1) / (2 * BM));
   p.num_kb = static_cast<int>((K + BK - 1) / BK);
   p.status = device_status_ptr();
   EpiParams &e = p.ep;
-  e.out = static_cast<__nv_bfloat16 *>(ep->out);
-  e.ldo = ep->ldo;
   e.bias = static_cast<const __nv_bfloat16 *>(ep->bias);
 
-  CUtensorMap ta, tb, tb2;
+  CUtensorMap ta, tb, tb2, to;
   rc = make_map_u8(&ta, A, M, K, lda, BM);
   if (rc != VFB_OK) return rc;
 
@@ -467,25 +555,27 @@ extern "C" int vfb_fp8_gemm(const void *A, int64_t lda, const float *sa, const v
       return set_error(VFB_EINVAL, "vfb_fp8_gemm: SWIGLU needs the packed width N = 2F, F %% 32 == 0");
     const int64_t F = N / 2;
     if (ep->ldo < F) return set_error(VFB_EINVAL, "vfb_fp8_gemm: SWIGLU output ldo < F");
-    e.ffn_width = F;
-    p.num_n_tiles = static_cast<int>((F + BN / 2 - 1) / (BN / 2));
+    e.plane_width = static_cast<int32_t>(F);
+    p.num_n_tiles = static_cast<int>((F + BN_HALF - 1) / BN_HALF);
+    if ((rc = make_map_out(&to, ep->out, F, M, 1, ep->ldo, M * ep->ldo)) != VFB_OK) return rc;
     const uint8_t *gate_rows = static_cast<const uint8_t *>(W) + F * ldw;
-    if ((rc = make_map_u8(&tb, W, F, K, ldw, BN / 2)) != VFB_OK) return rc;
-    if ((rc = make_map_u8(&tb2, gate_rows, F, K, ldw, BN / 2)) != VFB_OK) return rc;
+    if ((rc = make_map_u8(&tb, W, F, K, ldw, BN_HALF)) != VFB_OK) return rc;
+    if ((rc = make_map_u8(&tb2, gate_rows, F, K, ldw, BN_HALF)) != VFB_OK) return rc;
   } else {
-    e.plane_width = ep->plane_width;
-    e.plane_stride = ep->plane_stride;
-    if (e.plane_width < 0 || (e.plane_width > 0 && (e.plane_width % 32 || N % e.plane_width)))
+    if (ep->plane_width < 0 || (ep->plane_width > 0 && (ep->plane_width % 32 || N % ep->plane_width)))
       return set_error(VFB_EINVAL, "vfb_fp8_gemm: plane_width must be 0 or a multiple of 32 dividing N");
-    if (e.plane_stride % 8)
-      return set_error(VFB_EINVAL, "vfb_fp8_gemm: plane_stride %% 8 != 0");
-    const int64_t width = e.plane_width > 0 ? e.plane_width : N;
+    const int64_t width = ep->plane_width > 0 ? ep->plane_width : N;
+    const int64_t planes = N / width;
     if (ep->ldo < width) return set_error(VFB_EINVAL, "vfb_fp8_gemm: ldo smaller than the plane width");
+    const int64_t plane_stride = planes > 1 ? ep->plane_stride : M * ep->ldo;
+    if (plane_stride % 8 || (planes > 1 && plane_stride < M * ep->ldo))
+      return set_error(VFB_EINVAL, "vfb_fp8_gemm: plane_stride must be a multiple of 8 and >= M*ldo");
+    e.plane_width = static_cast<int32_t>(width);
+    if ((rc = make_map_out(&to, ep->out, width, M, planes, ep->ldo, plane_stride)) != VFB_OK) return rc;
     p.num_n_tiles = static_cast<int>((N + BN - 1) / BN);
-    if ((rc = make_map_u8(&tb, W, N, K, ldw, BN)) != VFB_OK) return rc;
+    if ((rc = make_map_u8(&tb, W, N, K, ldw, BN_HALF)) != VFB_OK) return rc;
     tb2 = tb;
     if (kind == VFB_EPI_STORE) {
-      const int planes = e.plane_width > 0 ? static_cast<int>(N / e.plane_width) : 1;
       for (int i = 0; i < 3; ++i) {
         e.adapter[i] = static_cast<const __nv_bfloat16 *>(ep->adapter[i]);
         e.scaling[i] = ep->scaling[i];
@@ -499,7 +589,7 @@ extern "C" int vfb_fp8_gemm(const void *A, int64_t lda, const float *sa, const v
     if (kind == VFB_EPI_RESIDUAL) {
       if (ep->residual == nullptr || !aligned16(ep->residual) || ep->ldr % 8 || ep->ldr < N)
         return set_error(VFB_EINVAL, "vfb_fp8_gemm: residual needs a 16-byte aligned [M,N] view");
-      if (e.plane_width != 0)
+      if (planes != 1)
         return set_error(VFB_EINVAL, "vfb_fp8_gemm: RESIDUAL writes one plane");
       e.residual = static_cast<const __nv_bfloat16 *>(ep->residual);
       e.ldr = ep->ldr;
@@ -517,12 +607,12 @@ extern "C" int vfb_fp8_gemm(const void *A, int64_t lda, const float *sa, const v
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   switch (kind) {
     case VFB_EPI_STORE:
-      return launch<VFB_EPI_STORE>(ta, tb, tb2, p, sm_count, s);
+      return launch<VFB_EPI_STORE>(ta, tb, tb2, to, p, sm_count, s);
     case VFB_EPI_GELU_TANH:
-      return launch<VFB_EPI_GELU_TANH>(ta, tb, tb2, p, sm_count, s);
+      return launch<VFB_EPI_GELU_TANH>(ta, tb, tb2, to, p, sm_count, s);
     case VFB_EPI_SWIGLU:
-      return launch<VFB_EPI_SWIGLU>(ta, tb, tb2, p, sm_count, s);
+      return launch<VFB_EPI_SWIGLU>(ta, tb, tb2, to, p, sm_count, s);
     default:
-      return launch<VFB_EPI_RESIDUAL>(ta, tb, tb2, p, sm_count, s);
+      return launch<VFB_EPI_RESIDUAL>(ta, tb, tb2, to, p, sm_count, s);
   }
 }

@@ -5,7 +5,8 @@
 // (src/vflash/native/h3_fp8_activation.py:13-28) bit for bit:
 //   amax  = max |x| over the row (fp32)
 //   scale = amax > 0 ? max(amax / 448, FLT_MIN) : 1      (IEEE division)
-//   code  = e4m3_rn(clamp(x / scale, -448, 448))         (IEEE division)
+//   code  = e4m3_rn(clamp(x / scale, -448, 448))         (correctly rounded
+//           quotient: reciprocal per row + one FMA correction per element)
 // Rows are padded to the caller's M_pad (16 in the reference) with code 0 and
 // scale 1.  A NaN anywhere in a row makes amax NaN as in torch, so the row's
 // scale is 1 and NaN inputs stay NaN codes.
@@ -37,8 +38,57 @@ __device__ __forceinline__ float row_scale(float amax, bool nan) {
   return fmaxf(__fdiv_rn(amax, 448.0f), FLT_MIN);
 }
 
+// Correctly rounded x / scale for a finite, normal scale (the row scale is
+// >= FLT_MIN by construction) given recip = RN(1 / scale).  Markstein's
+// theorem (P. Markstein, "Computation of elementary functions on the IBM
+// RISC System/6000 processor", IBM J. Res. Dev. 34(1), 1990): when recip is
+// the correctly rounded reciprocal and q = RN(x * recip) is within one ulp
+// of x / scale, the remainder x - q * scale is exact under FMA and
+// RN(q + remainder * recip) is the correctly rounded quotient.  Quotients
+// small enough to lose precision to fp32 underflow lie far below half the
+// smallest e4m3 subnormal, so their codes (signed zero) are unaffected.
+// The scale is positive, so the quotient carries the sign of x; copying it
+// back keeps -0 / scale = -0 (the correction step would produce +0).
+__device__ __forceinline__ float div_rn_by_scale(float x, float scale, float recip) {
+  const float q = x * recip;
+  const float rem = fmaf(-q, scale, x);
+  return copysignf(fmaf(rem, recip, q), x);
+}
+
+// Quotient used for the codes: exact division routine for non-finite scales.
+__device__ __forceinline__ float quotient(float x, float scale, float recip, bool fast) {
+  return fast ? div_rn_by_scale(x, scale, recip) : __fdiv_rn(x, scale);
+}
+
+// Codes of 8 bf16 values (one 16-byte vector) for a finite scale.
+__device__ __forceinline__ uint2 quantize8(const uint4 &v, float scale, float recip) {
+  const __nv_bfloat162 *h = reinterpret_cast<const __nv_bfloat162 *>(&v);
+  uint16_t q[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    float2 f = __bfloat1622float2(h[j]);
+    q[j] = pack_e4m3x2(clamp448(div_rn_by_scale(f.x, scale, recip)),
+                       clamp448(div_rn_by_scale(f.y, scale, recip)));
+  }
+  return make_uint2(static_cast<uint32_t>(q[0]) | (static_cast<uint32_t>(q[1]) << 16),
+                    static_cast<uint32_t>(q[2]) | (static_cast<uint32_t>(q[3]) << 16));
+}
+
+// Same for a non-finite scale (a row containing +-inf): IEEE division.
+__device__ __noinline__ uint2 quantize8_ieee(uint4 v, float scale) {
+  const __nv_bfloat162 *h = reinterpret_cast<const __nv_bfloat162 *>(&v);
+  uint16_t q[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    float2 f = __bfloat1622float2(h[j]);
+    q[j] = pack_e4m3x2(clamp448(__fdiv_rn(f.x, scale)), clamp448(__fdiv_rn(f.y, scale)));
+  }
+  return make_uint2(static_cast<uint32_t>(q[0]) | (static_cast<uint32_t>(q[1]) << 16),
+                    static_cast<uint32_t>(q[2]) | (static_cast<uint32_t>(q[3]) << 16));
+}
+
 // Vector path: x rows 16-byte aligned, K % 8 == 0.
-__global__ void __launch_bounds__(1024) fp8_quant_rows_vec(
+__global__ void __launch_bounds__(1024, 1) fp8_quant_rows_vec(
     const __nv_bfloat16 *__restrict__ x, int64_t M, int64_t K, int64_t ldx,
     uint8_t *__restrict__ codes, float *__restrict__ scales, int64_t M_pad, int tpr) {
   extern __shared__ float red[];  // [rows per block][warps per row] maxima + nan flags
@@ -91,23 +141,15 @@ __global__ void __launch_bounds__(1024) fp8_quant_rows_vec(
   }
   if (row >= M_pad) return;
   const float scale = live ? row_scale(amax, nan) : 1.0f;
+  const bool fast = isfinite(scale);
+  const float recip = fast ? __frcp_rn(scale) : 0.0f;
   uint2 *dst = reinterpret_cast<uint2 *>(codes + row * K);
 #pragma unroll
   for (int i = 0; i < kVecPerThread; ++i) {
     const int64_t c = static_cast<int64_t>(i) * tpr + t;
     if (c >= nvec) continue;
     uint2 out = make_uint2(0, 0);
-    if (live) {
-      const __nv_bfloat162 *h = reinterpret_cast<const __nv_bfloat162 *>(&v[i]);
-      uint16_t q[4];
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        float2 f = __bfloat1622float2(h[j]);
-        q[j] = pack_e4m3x2(clamp448(__fdiv_rn(f.x, scale)), clamp448(__fdiv_rn(f.y, scale)));
-      }
-      out.x = static_cast<uint32_t>(q[0]) | (static_cast<uint32_t>(q[1]) << 16);
-      out.y = static_cast<uint32_t>(q[2]) | (static_cast<uint32_t>(q[3]) << 16);
-    }
+    if (live) out = fast ? quantize8(v[i], scale, recip) : quantize8_ieee(v[i], scale);
     dst[c] = out;
   }
   if (t == 0) scales[row] = scale;
@@ -146,11 +188,13 @@ __global__ void __launch_bounds__(kBlockThreads) fp8_quant_rows_scalar(
     any_nan = fmaxf(any_nan, red[warps + w]);
   }
   const float scale = live ? row_scale(amax, any_nan != 0.0f) : 1.0f;
+  const bool fast = isfinite(scale);
+  const float recip = fast ? __frcp_rn(scale) : 0.0f;
   for (int64_t c = threadIdx.x; c < K; c += blockDim.x) {
     uint8_t q = 0;
     if (live) {
       float f = __bfloat162float(x[row * ldx + c]);
-      q = static_cast<uint8_t>(pack_e4m3x2(clamp448(__fdiv_rn(f, scale)), 0.0f) & 0xFF);
+      q = static_cast<uint8_t>(pack_e4m3x2(clamp448(quotient(f, scale, recip, fast)), 0.0f) & 0xFF);
     }
     codes[row * K + c] = q;
   }
