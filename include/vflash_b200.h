@@ -125,6 +125,57 @@ VFB_API int vfb_fp8_gemm(const void *A, int64_t lda, const float *sa,
                  int64_t M, int64_t N, int64_t K,
                  const vfb_epilogue *ep, void *stream);
 
+/* ---- strict-BF16 elementwise steps -----------------------------------------
+ * Standalone versions of the epilogues above, for callers whose GEMM is not
+ * this library's.  bf16 tensors; the last dimension is contiguous and its
+ * width a multiple of 8; other strides as stated.  Rounding boundaries follow
+ * the reference kernels in src/vflash/native/h3_fused_ops.py (line ranges
+ * given per entry point).  `out` may not alias inputs unless stated. */
+
+/* triton_strict_bf16_silu_mul (h3_fused_ops.py:185-224, 660-700):
+ * packed [rows, 2*width] -> out[r, c] = bf16(v * bf16(silu(g))), v = packed[r, c],
+ * g = packed[r, width + c]; out row stride out_ld (out may be the value half
+ * of packed itself, out_ld = 2*width). */
+VFB_API int vfb_silu_mul(const void *packed, int64_t rows, int64_t width, void *out,
+                         int64_t out_ld, void *stream);
+
+/* triton_strict_bf16_ffn_adapter_silu (h3_fused_ops.py:254-284, 703-762):
+ * base/adapter [rows, 2*width]; value and gate halves each merged as
+ * bf16(b + bf16(a * scaling)), then out = bf16(value * bf16(silu(gate))).
+ * out row stride out_ld; out may be the value half of base (reuse_base). */
+VFB_API int vfb_ffn_adapter_silu(const void *base, const void *adapter, int64_t rows,
+                                 int64_t width, float scaling, void *out, int64_t out_ld,
+                                 void *stream);
+
+/* triton_strict_bf16_gate_residual (h3_fused_ops.py:125-170, 614-657):
+ * residual/projected [rows, hidden] contiguous (rows = batch * tokens),
+ * gate [tokens, hidden] with row stride gate_token_stride:
+ * out = bf16(residual + bf16(gate[r % tokens] * projected)). */
+VFB_API int vfb_gate_residual(const void *residual, const void *gate, int64_t gate_token_stride,
+                              const void *projected, int64_t rows, int64_t tokens,
+                              int64_t hidden, void *out, void *stream);
+
+/* triton_strict_bf16_adapter_gate_residual (h3_fused_ops.py:342-415, 982-1028):
+ * out = bf16(residual + bf16(gate * bf16(base + bf16(adapter * scaling)))). */
+VFB_API int vfb_adapter_gate_residual(const void *base, const void *adapter, const void *residual,
+                                      const void *gate, int64_t gate_token_stride, int64_t rows,
+                                      int64_t tokens, int64_t hidden, float scaling, void *out,
+                                      void *stream);
+
+/* triton_strict_bf16_adapter_merge / _qkv_adapter_merge (h3_fused_ops.py:298-339,
+ * 765-838): base/adapter [rows, width], `branches` (1..3) equal column
+ * branches: out = bf16(base + bf16(adapter * scalings[branch])). */
+VFB_API int vfb_adapter_merge(const void *base, const void *adapter, int64_t rows, int64_t width,
+                              int32_t branches, const float *scalings, void *out, void *stream);
+
+/* triton_strict_bf16_qkv_direct_merge (h3_fused_ops.py:901-979), in place:
+ * base [rows, 3*width]; base[:, b*width:(b+1)*width] =
+ * bf16(base_b + bf16(adapter_b * scalings[b])) for b = q, k, v.
+ * `scalings` is a host pointer to three floats. */
+VFB_API int vfb_qkv_direct_merge(void *base, const void *adapter_q, const void *adapter_k,
+                                 const void *adapter_v, int64_t rows, int64_t width,
+                                 const float *scalings, void *stream);
+
 #ifdef __cplusplus
 }
 #endif
