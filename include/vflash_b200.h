@@ -125,6 +125,30 @@ VFB_API int vfb_fp8_gemm(const void *A, int64_t lda, const float *sa,
                  int64_t M, int64_t N, int64_t K,
                  const vfb_epilogue *ep, void *stream);
 
+/* ---- NVFP4 ----------------------------------------------------------------
+ * Activation quantiser: replaces FlashInfer nvfp4_quantize(x, global_scale,
+ * sfLayout=128x4, do_shuffle=False) as NVFP4Execution.linear calls it
+ * (src/vflash/native/h3_nvfp4_linear.py:102).  x: [M,K] bf16 (dtype 0) or fp16
+ * (dtype 1), row stride ldx; global_scale: device fp32 scalar (gsf).  Per 16
+ * elements: sf = e4m3(gsf * amax / 6), codes = e2m1(x / (sf / gsf)) with the
+ * reference's rcp.approx.ftz arithmetic.  codes: [M, K/2] bytes (element 2i in
+ * the low nibble); sf: ceil128(M) * ceil4(K/16) bytes in the 128x4 layout,
+ * padding written as 0.  K % 16 == 0. */
+VFB_API int vfb_nvfp4_quant_rows(const void *x, int32_t dtype, int64_t M, int64_t K, int64_t ldx,
+                                 const float *global_scale, void *codes, void *sf, void *stream);
+
+/* Block-scaled GEMM: replaces FlashInfer mm_fp4(codes, packed.T, scales,
+ * weight_scales.T, alpha, bf16, backend="cutlass") and the bias add
+ * (src/vflash/native/h3_nvfp4_linear.py:118-139):
+ *   out = bf16(alpha * sum_k A(m,k) W(n,k)) [then bf16(out + bias)]
+ * A: [M, K/2] codes with scales sfa (128x4 layout, ceil128(M) rows); W: the
+ * NVFP4Weight packed [N, K/2] codes and scales [N, K/16] (128x4 layout).
+ * alpha: device fp32 scalar.  out: bf16 [planes, M, N/planes] contiguous
+ * (planes = 1: [M, N]).  K % 64 == 0, N % 128 == 0. */
+VFB_API int vfb_nvfp4_gemm(const void *A, const void *sfa, const void *W, const void *sfw,
+                           const float *alpha, int64_t M, int64_t N, int64_t K, const void *bias,
+                           void *out, int64_t planes, void *stream);
+
 /* ---- strict-BF16 elementwise steps -----------------------------------------
  * Standalone versions of the epilogues above, for callers whose GEMM is not
  * this library's.  bf16 tensors; the last dimension is contiguous and its

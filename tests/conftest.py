@@ -7,6 +7,7 @@ library; those tests are skipped, not silently passed, when no GPU is present.
 
 from __future__ import annotations
 
+import os
 import sys
 from pathlib import Path
 
@@ -18,6 +19,12 @@ if str(ROOT) not in sys.path:
     sys.path.insert(0, str(ROOT))
 
 GOLDEN = ROOT / "tests" / "golden"
+
+# FlashInfer (the reference's NVFP4 backend, used only as the GPU checker)
+# loads its prebuilt modules from the in-tree cache that
+# tests/golden/build_flashinfer_reference.py builds.
+os.environ.setdefault("FLASHINFER_WORKSPACE_BASE", str(ROOT / "tests" / ".flashinfer_ref"))
+os.environ.setdefault("FLASHINFER_CUDA_ARCH_LIST", "10.0a")
 
 
 def pytest_configure(config):

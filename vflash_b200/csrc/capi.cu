@@ -4,6 +4,8 @@
 #include <cstring>
 #include <mutex>
 
+#include <cudaTypedefs.h>
+
 #include "common.cuh"
 
 namespace {
@@ -65,6 +67,22 @@ int *device_status_ptr() {
     g_status_ptr[dev] = static_cast<int *>(ptr);
   }
   return g_status_ptr[dev];
+}
+
+// cuTensorMapEncodeTiled from the driver, looked up once through the runtime
+// (no link-time dependency on libcuda).
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void *ptr = nullptr;
+    cudaDriverEntryPointQueryResult qres;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &qres) ==
+            cudaSuccess &&
+        qres == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  });
+  return fn;
 }
 
 }  // namespace vfb

@@ -8,6 +8,7 @@
 
 #include <cuda.h>
 #include <cuda_bf16.h>
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -219,6 +220,81 @@ __device__ __forceinline__ void tmem_ld_32x32b_x32(uint32_t taddr, float (&v)[32
   for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
 
+// ---- block-scaled (NVFP4) helpers --------------------------------------------
+// Contiguous global -> shared copy of `bytes` (multiple of 16, both addresses
+// 16-byte aligned) counted as transaction bytes on `bar`.
+__device__ __forceinline__ void bulk_load(void *smem_dst, const void *gmem_src, uint32_t bytes,
+                                          uint64_t *bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(gmem_src)), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+
+// Shared-memory descriptor of a 512-byte scale-factor block: 32 rows of 16
+// bytes, no swizzle (8-row core matrices 128 bytes apart).
+__device__ __forceinline__ uint64_t sf_block_desc(uint32_t smem_addr) {
+  uint64_t desc = 0;
+  desc |= static_cast<uint64_t>((smem_addr & 0x3FFFFu) >> 4);
+  desc |= static_cast<uint64_t>(1) << 16;          // leading offset (one 16-byte column)
+  desc |= static_cast<uint64_t>(128 >> 4) << 32;   // stride offset between 8-row groups
+  desc |= static_cast<uint64_t>(1) << 46;          // descriptor version (sm_100)
+  return desc;                                     // layout 0: no swizzle
+}
+
+// Copy one 32 x 128-bit shared block into TMEM lanes 0-31 and replicate it to
+// the other three 32-lane sub-partitions (4 columns of 32 bits).
+__device__ __forceinline__ void tmem_cp_32x128b_warpx4(uint32_t taddr, uint64_t src_desc) {
+  asm volatile("tcgen05.cp.cta_group::1.32x128b.warpx4 [%0], %1;" ::"r"(taddr), "l"(src_desc)
+               : "memory");
+}
+
+// D[tmem] (+)= (A * SFA) (B * SFB)^T for e2m1 operands with one ue4m3 scale
+// per 16 K-elements (kind::mxf4nvf4, block16), scales read from TMEM.
+__device__ __forceinline__ void mma_mxf4nvf4(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                             uint32_t idesc, uint32_t sfa_tmem, uint32_t sfb_tmem,
+                                             uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::mxf4nvf4.block_scale.block16 [%0], %1, %2, %3, [%5], [%6], p;\n\t}" ::
+          "r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(sfa_tmem), "r"(sfb_tmem)
+      : "memory");
+}
+
+// Instruction descriptor: e2m1 x e2m1 with ue4m3 block scales, f32 accumulate,
+// both operands K-major, K = 64 per instruction.
+__host__ __device__ constexpr uint32_t idesc_nvf4_f32(int m, int n) {
+  return (1u << 7) | (1u << 10)                     // A, B format e2m1
+         | (static_cast<uint32_t>(n >> 3) << 17)    // N / 8
+         | (0u << 23)                               // scale format ue4m3
+         | (static_cast<uint32_t>(m >> 4) << 24);   // M / 16
+}
+
+// Approximate reciprocal with denormals flushed (PTX rcp.approx.ftz.f32).
+__device__ __forceinline__ float rcp_approx_ftz(float x) {
+  float r;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
+  return r;
+}
+
+// Eight floats -> eight e2m1 codes (round to nearest even, saturating to
+// +-6), element 2i in the low nibble of byte i.
+__device__ __forceinline__ uint32_t pack_e2m1x8(const float (&v)[8]) {
+  uint32_t r;
+  asm("{\n\t.reg .b8 b0, b1, b2, b3;\n\t"
+      "cvt.rn.satfinite.e2m1x2.f32 b0, %2, %1;\n\t"
+      "cvt.rn.satfinite.e2m1x2.f32 b1, %4, %3;\n\t"
+      "cvt.rn.satfinite.e2m1x2.f32 b2, %6, %5;\n\t"
+      "cvt.rn.satfinite.e2m1x2.f32 b3, %8, %7;\n\t"
+      "mov.b32 %0, {b0, b1, b2, b3};\n\t}"
+      : "=r"(r)
+      : "f"(v[0]), "f"(v[1]), "f"(v[2]), "f"(v[3]), "f"(v[4]), "f"(v[5]), "f"(v[6]), "f"(v[7]));
+  return r;
+}
+
 // ---- CTA pairs (2-CTA clusters) ---------------------------------------------
 __device__ __forceinline__ uint32_t cluster_ctarank() {
   uint32_t r;
@@ -315,8 +391,10 @@ __device__ __forceinline__ uint16_t pack_e4m3x2(float lo, float hi) {
 }  // namespace vfb
 
 // Host-side helpers implemented in capi.cu.
+#include <cudaTypedefs.h>
 namespace vfb {
 int set_error(int code, const char *fmt, ...);
 int check_device(int *sm_count);
 int *device_status_ptr();
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder();
 }  // namespace vfb

@@ -417,20 +417,6 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 
 // ---- host side ---------------------------------------------------------------
 
-PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
-  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-  static std::once_flag once;
-  std::call_once(once, [] {
-    void *ptr = nullptr;
-    cudaDriverEntryPointQueryResult qres;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &qres) ==
-            cudaSuccess &&
-        qres == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
-  });
-  return fn;
-}
-
 // Tensor map over an 8-bit [rows, cols] matrix (row stride ld bytes) with a
 // 128-byte-swizzled box of box_rows x 128 bytes.
 int make_map_u8(CUtensorMap *map, const void *base, int64_t rows, int64_t cols, int64_t ld,

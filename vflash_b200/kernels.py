@@ -161,3 +161,76 @@ def fp8_gemm(a_codes: torch.Tensor, a_scales: torch.Tensor, rows: int, weight: t
             _lib.stream_handle(device))
     _lib.check(rc, "vfb_fp8_gemm")
     return out
+
+
+# ---------------------------------------------------------------------------
+# NVFP4
+# ---------------------------------------------------------------------------
+def nvfp4_sf_shape(rows: int, cols: int) -> tuple[int, int]:
+    """Padded 128x4 scale-factor shape for a [rows, cols] input: (ceil128(rows), ceil4(cols/16))."""
+    return (-(-rows // 128) * 128, -(-(cols // 16) // 4) * 4)
+
+
+def nvfp4_quantize(matrix: torch.Tensor, global_scale: torch.Tensor):
+    """e2m1 codes ``[M, K/2]`` (uint8) and 128x4 ue4m3 scales ``[ceil128(M), ceil4(K/16)]`` (uint8).
+
+    ``matrix`` is bf16 or fp16 ``[M, K]`` with unit column stride and K % 16 == 0;
+    ``global_scale`` an fp32 scalar tensor on the same device.
+    """
+    if (matrix.dtype not in (BF16, torch.float16) or matrix.ndim != 2 or matrix.stride(1) != 1
+            or matrix.shape[1] % 16):
+        raise KernelInputError("NVFP4 quantisation needs a bf16/fp16 [M,K] matrix, K % 16 == 0")
+    if (global_scale.dtype != torch.float32 or global_scale.numel() != 1
+            or global_scale.device != matrix.device):
+        raise KernelInputError("NVFP4 global scale must be an fp32 scalar on the input's device")
+    rows, cols = matrix.shape
+    codes = torch.empty((rows, cols // 2), device=matrix.device, dtype=torch.uint8)
+    sf = torch.empty(nvfp4_sf_shape(rows, cols), device=matrix.device, dtype=torch.uint8)
+    if rows == 0:
+        return codes, sf
+    lib = _lib.load()
+    with torch.cuda.device(matrix.device):
+        rc = lib.vfb_nvfp4_quant_rows(matrix.data_ptr(), 0 if matrix.dtype == BF16 else 1, rows, cols,
+                                      matrix.stride(0), global_scale.data_ptr(), codes.data_ptr(),
+                                      sf.data_ptr(), _lib.stream_handle(matrix.device))
+    _lib.check(rc, "vfb_nvfp4_quant_rows")
+    return codes, sf
+
+
+def nvfp4_gemm(a_codes: torch.Tensor, a_sf: torch.Tensor, w_packed: torch.Tensor,
+               w_scales: torch.Tensor, alpha: torch.Tensor, bias: torch.Tensor | None = None,
+               planes: int = 1) -> torch.Tensor:
+    """``bf16(alpha * A @ W^T)`` (+ bias) for NVFP4 operands in the 128x4 scale layout."""
+    rows, half_k = a_codes.shape
+    n = w_packed.shape[0]
+    k = 2 * half_k
+    if (a_codes.dtype != torch.uint8 or w_packed.dtype != torch.uint8 or w_packed.shape[1] != half_k
+            or not a_codes.is_contiguous() or not w_packed.is_contiguous()):
+        raise KernelInputError("NVFP4 GEMM codes must be contiguous uint8 [M,K/2] and [N,K/2]")
+    if k % 64 or n % 128 or n % planes or (n // planes) % 32:
+        raise KernelInputError("NVFP4 GEMM needs K % 64 == 0, N % 128 == 0")
+    pr, pc = nvfp4_sf_shape(rows, k)
+    if (a_sf.dtype != torch.uint8 or a_sf.numel() != pr * pc or not a_sf.is_contiguous()
+            or w_scales.dtype != torch.uint8 or w_scales.numel() != n * (k // 16)
+            or not w_scales.is_contiguous()):
+        raise KernelInputError("NVFP4 GEMM scales differ from the 128x4 layout")
+    if alpha.dtype != torch.float32 or alpha.numel() != 1:
+        raise KernelInputError("NVFP4 GEMM alpha must be an fp32 scalar tensor")
+    device = a_codes.device
+    for t in (a_sf, w_packed, w_scales, alpha):
+        if t.device != device:
+            raise KernelInputError("NVFP4 GEMM operands must share one device")
+    if bias is not None and (bias.dtype != BF16 or bias.shape != (n,) or not bias.is_contiguous()):
+        raise KernelInputError("NVFP4 GEMM bias must be contiguous bf16 [N]")
+    shape = (rows, n) if planes == 1 else (planes, rows, n // planes)
+    out = torch.empty(shape, device=device, dtype=BF16)
+    if rows == 0:
+        return out
+    lib = _lib.load()
+    with torch.cuda.device(device):
+        rc = lib.vfb_nvfp4_gemm(a_codes.data_ptr(), a_sf.data_ptr(), w_packed.data_ptr(),
+                                w_scales.data_ptr(), alpha.data_ptr(), rows, n, k,
+                                None if bias is None else bias.data_ptr(), out.data_ptr(), planes,
+                                _lib.stream_handle(device))
+    _lib.check(rc, "vfb_nvfp4_gemm")
+    return out
