@@ -263,6 +263,9 @@ def run_gpu(args) -> None:
     library = None
     if rank == 0 and not args.no_library_probe:
         library = library_fp8_probe(device)
+    other = None
+    if rank == 0 and not args.no_other_configs:
+        other = other_configs(device, flush, stream)
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu = cpu_baseline(x_host, w_codes.cpu(), w_scales.cpu(), bias.cpu(), args.cpu_seconds)
@@ -324,9 +327,124 @@ def run_gpu(args) -> None:
                        "ms_per_step": round(e2e_ms / e2e_steps, 3)}
     if library is not None:
         line["library_fp8_tflops"] = library
+    if other is not None:
+        line["other_configs"] = other
     if cpu is not None:
         line["cpu_baseline"] = cpu
     print(json.dumps(line), flush=True)
+
+
+def _timed(fn, flush, stream, reps: int = 5, warmup: int = 3) -> list[float]:
+    """Per-call milliseconds of ``fn`` (CUDA events, L2 flushed before each call)."""
+    for _ in range(warmup):
+        fn()
+    times = []
+    for i in range(reps):
+        flush.fill_(float(i))
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        fn()
+        e1.record(stream)
+        times.append((e0, e1))
+    torch.cuda.synchronize()
+    return [a.elapsed_time(b) for a, b in times]
+
+
+def other_configs(device, flush, stream) -> dict:
+    """BASELINE configs 0, 2 and 3 on one GPU (seeded synthetic inputs, same timing rules)."""
+    from vflash_b200 import _lib
+    from vflash_b200.kernels import Epilogue, fp8_gemm, nvfp4_gemm, nvfp4_quantize, quantize_fp8_rows
+
+    peaks = measured_peaks()
+    fp8_peak = 2.0 * float(peaks.get("bf16_tflops", 1590.0))
+    fp4_peak = 2.0 * fp8_peak
+    out: dict = {}
+
+    def seeded(rows, cols, seed, std=1.0, outliers=False):
+        gen = torch.Generator().manual_seed(seed)
+        x = torch.randn(rows, cols, generator=gen) * std
+        if outliers:
+            count = round(0.001 * rows * cols)
+            idx = torch.randperm(rows * cols, generator=torch.Generator().manual_seed(seed + 1))[:count]
+            x.view(-1)[idx] *= 20
+        return x.to(torch.bfloat16).to(device)
+
+    def summary(ms, flop, peak, extra=None):
+        med = statistics.median(ms)
+        d = {"ms": round(med, 4), "tflops": round(flop / (med * 1e-3) / 1e12, 1),
+             "frac_of_peak": round(flop / (med * 1e-3) / 1e12 / peak, 4)}
+        d.update(extra or {})
+        return d
+
+    # c0: single FP8 linear 4096^3 with bias
+    x = seeded(4096, 4096, 1000, outliers=True)
+    wc, ws = quantize_fp8_rows(seeded(4096, 4096, 2000, std=0.02), pad_to=1)
+    b = seeded(1, 4096, 3000, std=0.01).view(-1)
+
+    def c0():
+        c, s = quantize_fp8_rows(x)
+        fp8_gemm(c, s, 4096, wc, ws, Epilogue(bias=b))
+
+    out["c0_fp8_linear_4096"] = summary(_timed(c0, flush, stream), 2.0 * 4096**3, fp8_peak,
+                                        {"step": "quantiser + GEMM + bias"})
+    del x, wc, ws, b
+
+    # c2: fused FFN, GELU-tanh, per-token requant of the intermediate, residual
+    m, h, f = 32760, 4096, 16384
+    x = seeded(m, h, 1002)
+    up, ups = quantize_fp8_rows(seeded(f, h, 2020, std=0.02), pad_to=1)
+    down, downs = quantize_fp8_rows(seeded(h, f, 2021, std=0.02), pad_to=1)
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(5)]
+
+    def c2():
+        ev[0].record(stream)
+        c, s = quantize_fp8_rows(x)
+        ev[1].record(stream)
+        mid = fp8_gemm(c, s, m, up, ups, Epilogue(kind=_lib.EPI_GELU_TANH))
+        ev[2].record(stream)
+        mc, ms_ = quantize_fp8_rows(mid)
+        ev[3].record(stream)
+        fp8_gemm(mc, ms_, m, down, downs, Epilogue(kind=_lib.EPI_RESIDUAL, residual=x))
+        ev[4].record(stream)
+
+    ms = _timed(c2, flush, stream)
+    parts = [ev[i].elapsed_time(ev[i + 1]) for i in range(4)]
+    out["c2_fp8_ffn_gelu"] = summary(
+        ms, 2.0 * m * f * h * 2, fp8_peak,
+        {"step": "quant X, up GEMM + GELU-tanh epilogue, per-token requant of the bf16 intermediate, "
+                 "down GEMM + residual epilogue (four launches; intermediate round-trips HBM)",
+         "last_step_ms": {"quant_x": round(parts[0], 4), "up_gemm_gelu": round(parts[1], 4),
+                          "requant_mid": round(parts[2], 4), "down_gemm_residual": round(parts[3], 4)}})
+    del x, up, ups, down, downs
+
+    # c3: NVFP4 linear, M = 32760, K = 4096, N in {4096, 16384}
+    x = seeded(32760, 4096, 1003)
+    gsf_x = (448.0 * 6.0 / x.float().abs().max()).reshape(())
+    for n in (4096, 16384):
+        w = seeded(n, 4096, 2030 + n, std=0.02)
+        gsf_w = (448.0 * 6.0 / w.float().abs().max()).reshape(())
+        wp, wsc = nvfp4_quantize(w, gsf_w)
+        wsc = wsc.view(n, 4096 // 16)
+        alpha = ((1.0 / gsf_w) / gsf_x).to(torch.float32)
+        ev2 = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+
+        def c3():
+            ev2[0].record(stream)
+            ac, asf = nvfp4_quantize(x, gsf_x)
+            ev2[1].record(stream)
+            nvfp4_gemm(ac, asf, wp, wsc, alpha)
+            ev2[2].record(stream)
+
+        ms = _timed(c3, flush, stream)
+        gemm_ms = ev2[1].elapsed_time(ev2[2])
+        flop = 2.0 * 32760 * n * 4096
+        out[f"c3_nvfp4_n{n}"] = summary(ms, flop, fp4_peak, {
+            "step": "NVFP4 quantiser + block-scaled GEMM",
+            "gemm_only_tflops": round(flop / (gemm_ms * 1e-3) / 1e12, 1),
+            "gemm_frac_of_peak": round(flop / (gemm_ms * 1e-3) / 1e12 / fp4_peak, 4)})
+    out["peak_note"] = ("fp8 peak = 2 x measured cuBLAS bf16 burst, fp4 peak = 4 x; nominal dense "
+                        "fp8 4.5, fp4 9 PFLOP/s")
+    return out
 
 
 def library_fp8_probe(device) -> dict:
@@ -454,6 +572,8 @@ def main() -> None:
     parser.add_argument("--no-cpu-baseline", action="store_true")
     parser.add_argument("--no-library-probe", action="store_true")
     parser.add_argument("--no-e2e", action="store_true")
+    parser.add_argument("--no-other-configs", action="store_true",
+                        help="skip the extra BASELINE config 0/2/3 measurements")
     parser.add_argument("--rows", type=int, default=M,
                         help="token rows M (default 32760 = BASELINE config 1; smaller only for profiling)")
     args = parser.parse_args()
