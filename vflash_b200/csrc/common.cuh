@@ -102,6 +102,40 @@ __device__ __forceinline__ void tma_load_2d(void *smem_dst, const CUtensorMap *m
       : "memory");
 }
 
+// L2 eviction policies for TMA traffic: weights are re-read by every tile row
+// of a GEMM and should outlive the streamed activations and outputs.
+__device__ __forceinline__ uint64_t l2_policy_evict_last() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+
+__device__ __forceinline__ uint64_t l2_policy_evict_first() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+
+// tma_load_2d with an L2 cache policy.
+__device__ __forceinline__ void tma_load_2d_hint(void *smem_dst, const CUtensorMap *map, uint64_t *bar,
+                                                 int32_t x, int32_t y, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1, {%3, %4}], [%2], %5;" ::"r"(smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y), "l"(policy)
+      : "memory");
+}
+
+// 3-D tiled store with an L2 cache policy (see tma_store_3d).
+__device__ __forceinline__ void tma_store_3d_hint(const CUtensorMap *map, const void *smem_src,
+                                                  int32_t x, int32_t y, int32_t z, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.global.shared::cta.bulk_group.L2::cache_hint [%0, {%2, %3, %4}], [%1], %5;" ::"l"(
+          reinterpret_cast<uint64_t>(map)),
+      "r"(smem_u32(smem_src)), "r"(x), "r"(y), "r"(z), "l"(policy)
+      : "memory");
+}
+
 // 3-D tiled store of one shared-memory box to global memory (bulk-group
 // completion).  Coordinates outside the tensor are not written.
 __device__ __forceinline__ void tma_store_3d(const CUtensorMap *map, const void *smem_src, int32_t x,
@@ -329,6 +363,17 @@ __device__ __forceinline__ void tma_load_2d_pair(void *smem_dst, const CUtensorM
       "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
       " [%0], [%1, {%3, %4}], [%2];" ::"r"(smem_u32(smem_dst)),
       "l"(reinterpret_cast<uint64_t>(map)), "r"(bar_cluster_addr), "r"(x), "r"(y)
+      : "memory");
+}
+
+// tma_load_2d_pair with an L2 cache policy.
+__device__ __forceinline__ void tma_load_2d_pair_hint(void *smem_dst, const CUtensorMap *map,
+                                                      uint32_t bar_cluster_addr, int32_t x, int32_t y,
+                                                      uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+      ".L2::cache_hint [%0], [%1, {%3, %4}], [%2], %5;" ::"r"(smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar_cluster_addr), "r"(x), "r"(y), "l"(policy)
       : "memory");
 }
 

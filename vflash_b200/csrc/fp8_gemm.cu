@@ -153,7 +153,8 @@ __device__ __forceinline__ void store_box(uint8_t *warp_smem, int &box, const CU
   fence_proxy_async_smem();
   __syncwarp();
   if (lane == 0 && any_row) {
-    tma_store_3d(map, buf, col, row0, plane);
+    // outputs are not re-read by this kernel: evict them first from L2
+    tma_store_3d_hint(map, buf, col, row0, plane, l2_policy_evict_first());
     bulk_commit_group();
   }
   box = box + 1 == EPI_BOXES ? 0 : box + 1;
@@ -252,13 +253,15 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           const uint32_t full_leader = map_to_rank(smem_u32(&full_bar[s]), 0);
           if (rank == 0) mbar_arrive_expect_tx(&full_bar[s], 2 * (A_STAGE_BYTES + B_STAGE_BYTES));
           tma_load_2d_pair(sA + s * A_STAGE_BYTES, &tmA, full_leader, kb * BK, a_row);
+          // every tile row re-reads the whole weight: keep it resident in L2
+          const uint64_t keep = l2_policy_evict_last();
           if (EPI == VFB_EPI_SWIGLU) {
             // leader: value rows [n*128, +128); peer: the matching gate rows
-            tma_load_2d_pair(sB + s * B_STAGE_BYTES, rank == 0 ? &tmB : &tmB2, full_leader,
-                             kb * BK, n_tile * BN_HALF);
+            tma_load_2d_pair_hint(sB + s * B_STAGE_BYTES, rank == 0 ? &tmB : &tmB2, full_leader,
+                                  kb * BK, n_tile * BN_HALF, keep);
           } else {
-            tma_load_2d_pair(sB + s * B_STAGE_BYTES, &tmB, full_leader, kb * BK,
-                             n_tile * BN + static_cast<int32_t>(rank) * BN_HALF);
+            tma_load_2d_pair_hint(sB + s * B_STAGE_BYTES, &tmB, full_leader, kb * BK,
+                                  n_tile * BN + static_cast<int32_t>(rank) * BN_HALF, keep);
           }
           issued[s] = true;
           issued_phase[s] = ph;

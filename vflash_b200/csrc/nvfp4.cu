@@ -186,7 +186,7 @@ __device__ __forceinline__ void store_box(uint8_t *warp_smem, int &box, const CU
   fence_proxy_async_smem();
   __syncwarp();
   if (lane == 0 && any_row) {
-    tma_store_3d(map, buf, col, row0, plane);
+    tma_store_3d_hint(map, buf, col, row0, plane, l2_policy_evict_first());
     bulk_commit_group();
   }
   box = box + 1 == EPI_BOXES ? 0 : box + 1;
@@ -260,7 +260,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           uint8_t *st = smem + s * STAGE_BYTES;
           mbar_arrive_expect_tx(&full_bar[s], A_STAGE + B_STAGE + (1 + w_blocks) * kb_here * 512);
           tma_load_2d(st, &tmA, &full_bar[s], ks * BK_BYTES, m_tile * BM);
-          tma_load_2d(st + A_STAGE, &tmB, &full_bar[s], ks * BK_BYTES, n_tile * BN);
+          // every tile row re-reads the whole weight: keep it resident in L2
+          tma_load_2d_hint(st + A_STAGE, &tmB, &full_bar[s], ks * BK_BYTES, n_tile * BN,
+                           l2_policy_evict_last());
           const int64_t kt0 = static_cast<int64_t>(ks) * KB_PER_STAGE;
           bulk_load(st + A_STAGE + B_STAGE, p.sfa + (m_tile * (int64_t)p.ktiles + kt0) * 512,
                     kb_here * 512, &full_bar[s]);
