@@ -64,6 +64,22 @@ VFB_API int vfb_fp8_quant_rows(const void *x, int64_t M, int64_t K, int64_t ldx,
                        void *codes, float *scales, int64_t M_pad,
                        void *stream);
 
+/* Row maxima only: amax[m] = max_k |x[m,k]| (NaN for a row holding a NaN).
+ * With vfb_fp8_quant_rows_amax this quantises a row that is split over several
+ * ranks (tensor parallelism) exactly as the unsplit row: each rank takes its
+ * slice's maxima, the ranks combine them with a MAX all-reduce, and each
+ * quantises its slice with the full row's maxima.  No reference counterpart:
+ * the reference's tensor-parallel block (src/vflash/native/h3_parallel.py:
+ * 220-250) runs in BF16 and never quantises a split row. */
+VFB_API int vfb_fp8_row_absmax(const void *x, int64_t M, int64_t K, int64_t ldx, float *amax,
+                               void *stream);
+
+/* vfb_fp8_quant_rows with the row maxima given (amax[M], device) instead of
+ * computed: scale = amax > 0 ? max(amax / 448, FLT_MIN) : 1 (1 for NaN). */
+VFB_API int vfb_fp8_quant_rows_amax(const void *x, int64_t M, int64_t K, int64_t ldx,
+                                    const float *amax, void *codes, float *scales, int64_t M_pad,
+                                    void *stream);
+
 /* ---- FP8 row-scaled GEMM with fused epilogues ----------------------------
  * Replaces torch._scaled_mm(codes, weight.t(), scale_a, scale_b.t(),
  * out_dtype=bf16) plus the following bias add

@@ -98,6 +98,27 @@ def test_row_offsets_beyond_int32():
     del storage
 
 
+@pytest.mark.parametrize("cols", [4096, 1001])
+def test_row_maxima_and_given_maxima_reproduce_the_full_quantiser(cols):
+    from vflash_b200.kernels import row_absmax
+
+    x = outlier_activations(300, cols, 4).to(DEV)
+    x[7, 3] = float("nan")
+    amax = row_absmax(x)
+    want = x.float().abs().amax(dim=1)
+    assert torch.equal(torch.isnan(amax), torch.isnan(want))
+    assert torch.equal(amax[~torch.isnan(amax)], want[~torch.isnan(want)])
+    codes, scales = quantize_fp8_rows(x)
+    codes2, scales2 = quantize_fp8_rows(x, amax=amax)
+    assert torch.equal(codes.view(torch.uint8), codes2.view(torch.uint8))
+    assert torch.equal(scales, scales2)
+    # a column slice quantised with the full row's maxima gives the full row's codes
+    half = (cols // 2) // 8 * 8 or cols
+    codes3, scales3 = quantize_fp8_rows(x[:, :half], amax=amax)
+    assert torch.equal(codes3.view(torch.uint8), codes.view(torch.uint8)[:, :half])
+    assert torch.equal(scales3, scales)
+
+
 def test_drop_in_refuses_unbounded_widths():
     with pytest.raises(ValueError, match="SM100"):
         quantize_activation(torch.zeros(4, 8, dtype=torch.bfloat16, device=DEV))

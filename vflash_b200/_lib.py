@@ -63,6 +63,11 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         ctypes.c_int,
         [_vp, _c_int64, _c_int64, _c_int64, _vp, _vp, _c_int64, _vp],
     ),
+    "vfb_fp8_row_absmax": (ctypes.c_int, [_vp, _c_int64, _c_int64, _c_int64, _vp, _vp]),
+    "vfb_fp8_quant_rows_amax": (
+        ctypes.c_int,
+        [_vp, _c_int64, _c_int64, _c_int64, _vp, _vp, _vp, _c_int64, _vp],
+    ),
     "vfb_fp8_gemm": (
         ctypes.c_int,
         [_vp, _c_int64, _vp, _vp, _c_int64, _vp, _c_int64, _c_int64, _c_int64,

@@ -88,9 +88,13 @@ __device__ __noinline__ uint2 quantize8_ieee(uint4 v, float scale) {
 }
 
 // Vector path: x rows 16-byte aligned, K % 8 == 0.
+// amax_in != NULL: use these row maxima instead of reducing (a row split over
+//   several ranks quantised with the full row's scale);
+// amax_out != NULL: only write the row maxima (NaN for a row with a NaN).
 __global__ void __launch_bounds__(1024, 1) fp8_quant_rows_vec(
     const __nv_bfloat16 *__restrict__ x, int64_t M, int64_t K, int64_t ldx,
-    uint8_t *__restrict__ codes, float *__restrict__ scales, int64_t M_pad, int tpr) {
+    uint8_t *__restrict__ codes, float *__restrict__ scales, int64_t M_pad, int tpr,
+    const float *__restrict__ amax_in, float *__restrict__ amax_out) {
   extern __shared__ float red[];  // [rows per block][warps per row] maxima + nan flags
   const int rows_per_block = blockDim.x / tpr;
   const int r_local = threadIdx.x / tpr;
@@ -121,23 +125,32 @@ __global__ void __launch_bounds__(1024, 1) fp8_quant_rows_vec(
       }
     }
   }
+  if (amax_in == nullptr) {  // block-uniform
 #pragma unroll
-  for (int off = 16; off > 0; off >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
-  nan = __any_sync(0xffffffffu, nan);
-  if (warps_per_row > 1) {
-    float *row_red = red + r_local * warps_per_row * 2;
-    if ((t & 31) == 0) {
-      row_red[t / 32] = amax;
-      row_red[warps_per_row + t / 32] = nan ? 1.0f : 0.0f;
+    for (int off = 16; off > 0; off >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
+    nan = __any_sync(0xffffffffu, nan);
+    if (warps_per_row > 1) {
+      float *row_red = red + r_local * warps_per_row * 2;
+      if ((t & 31) == 0) {
+        row_red[t / 32] = amax;
+        row_red[warps_per_row + t / 32] = nan ? 1.0f : 0.0f;
+      }
+      __syncthreads();
+      amax = 0.0f;
+      float any_nan = 0.0f;
+      for (int w = 0; w < warps_per_row; ++w) {
+        amax = fmaxf(amax, row_red[w]);
+        any_nan = fmaxf(any_nan, row_red[warps_per_row + w]);
+      }
+      nan = any_nan != 0.0f;
     }
-    __syncthreads();
-    amax = 0.0f;
-    float any_nan = 0.0f;
-    for (int w = 0; w < warps_per_row; ++w) {
-      amax = fmaxf(amax, row_red[w]);
-      any_nan = fmaxf(any_nan, row_red[warps_per_row + w]);
-    }
-    nan = any_nan != 0.0f;
+  } else {
+    amax = live ? amax_in[row] : 0.0f;
+    nan = amax != amax;
+  }
+  if (amax_out != nullptr) {
+    if (live && t == 0) amax_out[row] = nan ? __int_as_float(0x7fc00000) : amax;
+    return;
   }
   if (row >= M_pad) return;
   const float scale = live ? row_scale(amax, nan) : 1.0f;
@@ -159,33 +172,43 @@ __global__ void __launch_bounds__(1024, 1) fp8_quant_rows_vec(
 // the row (the second from cache).
 __global__ void __launch_bounds__(kBlockThreads) fp8_quant_rows_scalar(
     const __nv_bfloat16 *__restrict__ x, int64_t M, int64_t K, int64_t ldx,
-    uint8_t *__restrict__ codes, float *__restrict__ scales, int64_t M_pad) {
+    uint8_t *__restrict__ codes, float *__restrict__ scales, int64_t M_pad,
+    const float *__restrict__ amax_in, float *__restrict__ amax_out) {
   __shared__ float red[kBlockThreads / 32 * 2];
   const int64_t row = blockIdx.x;
   const bool live = row < M;
   float amax = 0.0f;
-  bool nan = false;
-  if (live) {
-    for (int64_t c = threadIdx.x; c < K; c += blockDim.x) {
-      float f = __bfloat162float(x[row * ldx + c]);
-      nan |= f != f;
-      amax = fmaxf(amax, fabsf(f));
-    }
-  }
-#pragma unroll
-  for (int off = 16; off > 0; off >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
-  nan = __any_sync(0xffffffffu, nan);
-  const int warps = blockDim.x / 32;
-  if ((threadIdx.x & 31) == 0) {
-    red[threadIdx.x / 32] = amax;
-    red[warps + threadIdx.x / 32] = nan ? 1.0f : 0.0f;
-  }
-  __syncthreads();
-  amax = 0.0f;
   float any_nan = 0.0f;
-  for (int w = 0; w < warps; ++w) {
-    amax = fmaxf(amax, red[w]);
-    any_nan = fmaxf(any_nan, red[warps + w]);
+  if (amax_in == nullptr) {  // block-uniform
+    bool nan = false;
+    if (live) {
+      for (int64_t c = threadIdx.x; c < K; c += blockDim.x) {
+        float f = __bfloat162float(x[row * ldx + c]);
+        nan |= f != f;
+        amax = fmaxf(amax, fabsf(f));
+      }
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
+    nan = __any_sync(0xffffffffu, nan);
+    const int warps = blockDim.x / 32;
+    if ((threadIdx.x & 31) == 0) {
+      red[threadIdx.x / 32] = amax;
+      red[warps + threadIdx.x / 32] = nan ? 1.0f : 0.0f;
+    }
+    __syncthreads();
+    amax = 0.0f;
+    for (int w = 0; w < warps; ++w) {
+      amax = fmaxf(amax, red[w]);
+      any_nan = fmaxf(any_nan, red[warps + w]);
+    }
+  } else {
+    amax = live ? amax_in[row] : 0.0f;
+    any_nan = amax != amax ? 1.0f : 0.0f;
+  }
+  if (amax_out != nullptr) {
+    if (live && threadIdx.x == 0) amax_out[row] = any_nan != 0.0f ? __int_as_float(0x7fc00000) : amax;
+    return;
   }
   const float scale = live ? row_scale(amax, any_nan != 0.0f) : 1.0f;
   const bool fast = isfinite(scale);
@@ -201,23 +224,18 @@ __global__ void __launch_bounds__(kBlockThreads) fp8_quant_rows_scalar(
   if (threadIdx.x == 0) scales[row] = scale;
 }
 
-}  // namespace
-}  // namespace vfb
-
-extern "C" int vfb_fp8_quant_rows(const void *x, int64_t M, int64_t K, int64_t ldx, void *codes,
-                                  float *scales, int64_t M_pad, void *stream) {
-  using namespace vfb;
+int launch_quant(const char *what, const void *x, int64_t M, int64_t K, int64_t ldx, void *codes,
+                 float *scales, int64_t M_pad, const float *amax_in, float *amax_out,
+                 cudaStream_t s) {
   if (M < 0 || K < 1 || K > 32768 || ldx < K || M_pad < M)
     return set_error(VFB_EINVAL,
-                     "vfb_fp8_quant_rows: need M >= 0, 1 <= K <= 32768, ldx >= K, M_pad >= M "
+                     "%s: need M >= 0, 1 <= K <= 32768, ldx >= K, M_pad >= M "
                      "(M=%lld K=%lld ldx=%lld M_pad=%lld)",
-                     (long long)M, (long long)K, (long long)ldx, (long long)M_pad);
+                     what, (long long)M, (long long)K, (long long)ldx, (long long)M_pad);
   if (M_pad == 0) return VFB_OK;
-  if ((M > 0 && x == nullptr) || codes == nullptr || scales == nullptr)
-    return set_error(VFB_EINVAL, "vfb_fp8_quant_rows: NULL pointer");
+  if (M > 0 && x == nullptr) return set_error(VFB_EINVAL, "%s: NULL pointer", what);
   int rc = check_device(nullptr);
   if (rc != VFB_OK) return rc;
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
   const bool vec = (K % 8 == 0) && (ldx % 8 == 0) && (reinterpret_cast<uintptr_t>(x) % 16 == 0) &&
                    (reinterpret_cast<uintptr_t>(codes) % 8 == 0);
   if (vec) {
@@ -230,14 +248,40 @@ extern "C" int vfb_fp8_quant_rows(const void *x, int64_t M, int64_t K, int64_t l
     const size_t smem = static_cast<size_t>(rows_per_block) * (tpr / 32) * 2 * sizeof(float);
     fp8_quant_rows_vec<<<static_cast<unsigned>(blocks), threads, smem, s>>>(
         static_cast<const __nv_bfloat16 *>(x), M, K, ldx, static_cast<uint8_t *>(codes), scales,
-        M_pad, tpr);
+        M_pad, tpr, amax_in, amax_out);
   } else {
     fp8_quant_rows_scalar<<<static_cast<unsigned>(M_pad), kBlockThreads, 0, s>>>(
         static_cast<const __nv_bfloat16 *>(x), M, K, ldx, static_cast<uint8_t *>(codes), scales,
-        M_pad);
+        M_pad, amax_in, amax_out);
   }
   cudaError_t err = cudaGetLastError();
-  if (err != cudaSuccess)
-    return set_error(VFB_ECUDA, "vfb_fp8_quant_rows launch: %s", cudaGetErrorString(err));
+  if (err != cudaSuccess) return set_error(VFB_ECUDA, "%s launch: %s", what, cudaGetErrorString(err));
   return VFB_OK;
+}
+
+}  // namespace
+}  // namespace vfb
+
+extern "C" int vfb_fp8_quant_rows(const void *x, int64_t M, int64_t K, int64_t ldx, void *codes,
+                                  float *scales, int64_t M_pad, void *stream) {
+  if (M_pad > 0 && (codes == nullptr || scales == nullptr))
+    return vfb::set_error(VFB_EINVAL, "vfb_fp8_quant_rows: NULL pointer");
+  return vfb::launch_quant("vfb_fp8_quant_rows", x, M, K, ldx, codes, scales, M_pad, nullptr,
+                           nullptr, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int vfb_fp8_row_absmax(const void *x, int64_t M, int64_t K, int64_t ldx, float *amax,
+                                  void *stream) {
+  if (M > 0 && amax == nullptr) return vfb::set_error(VFB_EINVAL, "vfb_fp8_row_absmax: NULL pointer");
+  return vfb::launch_quant("vfb_fp8_row_absmax", x, M, K, ldx, nullptr, nullptr, M, nullptr, amax,
+                           static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int vfb_fp8_quant_rows_amax(const void *x, int64_t M, int64_t K, int64_t ldx,
+                                       const float *amax, void *codes, float *scales, int64_t M_pad,
+                                       void *stream) {
+  if (M_pad > 0 && (codes == nullptr || scales == nullptr || (M > 0 && amax == nullptr)))
+    return vfb::set_error(VFB_EINVAL, "vfb_fp8_quant_rows_amax: NULL pointer");
+  return vfb::launch_quant("vfb_fp8_quant_rows_amax", x, M, K, ldx, codes, scales, M_pad, amax,
+                           nullptr, static_cast<cudaStream_t>(stream));
 }

@@ -1,0 +1,411 @@
+// NVFP4 block-scaled GEMM for sm_100a (e2m1 x e2m1 with one ue4m3 scale per
+// 16 K-elements, fp32 accumulate, bf16 out).
+//
+// Replaces FlashInfer mm_fp4(codes, packed.T, scales, weight_scales.T, alpha,
+// bf16, backend="cutlass") plus the bias add of NVFP4Execution.linear
+// (src/vflash/native/h3_nvfp4_linear.py:118-139):
+//   out[m,n] = bf16(alpha * sum_k e2m1(A[m,k]) sfA[m,k/16] e2m1(W[n,k]) sfW[n,k/16])
+//   out      = bf16(out + bias[n])                       if bias != NULL
+//
+// Structure: persistent CTA pairs (cta_group::2), 256 x 256 output tile per
+// pair, K staged 256 elements (128 bytes of codes) at a time.  Each CTA TMA-
+// loads its own 128 A rows and 128 of the tile's 256 weight rows (128-byte
+// swizzle, no multicast), its A rows' scale blocks and the scale blocks of all
+// 256 weight rows (512-byte blocks in the 128x4 layout, loaded through 2-D
+// tensor maps over those blocks so that rows past the end read as zero).  The
+// leader's MMA thread moves each K = 64 block's scales into both CTAs' TMEM
+// with tcgen05.cp.cta_group::2.32x128b.warpx4 and issues
+// tcgen05.mma.cta_group::2.kind::mxf4nvf4.block_scale.block16 (M = 256,
+// N = 256, K = 64).  TMEM per CTA: two 256-column accumulators overlapping by
+// 64 columns ([0,256) and [192,448)) and 48 columns of scales at [448,496);
+// the epilogue drains a tile's 64 shared columns first (reverse column order
+// for even tiles, forward for odd) and then lets the next tile's MMAs start.
+#include <cudaTypedefs.h>
+
+#include "common.cuh"
+
+namespace vfb {
+namespace {
+
+constexpr int BM = 128;                    // A rows per CTA (pair: 256)
+constexpr int BN = 256;                    // output columns per pair tile
+constexpr int BN_HALF = BN / 2;            // weight rows per CTA
+constexpr int BK_BYTES = 128;              // 256 e2m1 elements per stage
+constexpr int KB_PER_STAGE = 4;            // MMAs (K = 64) per stage
+constexpr int STAGES = 5;
+constexpr int A_STAGE = BM * BK_BYTES;                 // 16 KB
+constexpr int B_STAGE = BN_HALF * BK_BYTES;            // 16 KB
+constexpr int SFA_STAGE = KB_PER_STAGE * 512;          // 2 KB: own 128 rows
+constexpr int SFB_STAGE = 2 * KB_PER_STAGE * 512;      // 4 KB: all 256 weight rows
+constexpr int STAGE_BYTES = A_STAGE + B_STAGE + SFA_STAGE + SFB_STAGE;
+constexpr int NUM_THREADS = 192;
+constexpr int TMEM_COLS = 512;
+constexpr uint32_t ACC1_COL = 192;
+constexpr uint32_t SFA_COL = 448;          // 4 columns per K = 64 block
+constexpr uint32_t SFB_COL = 464;          // 8 columns per K = 64 block
+constexpr int EPI_BOXES = 2;
+constexpr int EPI_BOX_BYTES = 32 * 32 * 2;
+constexpr int EPI_SMEM = 4 * EPI_BOXES * EPI_BOX_BYTES;
+constexpr size_t SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + EPI_SMEM + 256;
+
+struct Params {
+  int64_t M, N, K;
+  const float *alpha;
+  const __nv_bfloat16 *bias;
+  int32_t plane_width;
+  int num_m_tiles, num_n_tiles, ktiles;  // ktiles = K / 64
+  int *status;
+};
+
+__device__ __forceinline__ void store_box(uint8_t *warp_smem, int &box, const CUtensorMap *map,
+                                          const float (&y)[32], int lane, int32_t col, int32_t row0,
+                                          int32_t plane, bool any_row) {
+  uint8_t *buf = warp_smem + box * EPI_BOX_BYTES;
+  if (lane == 0) bulk_wait_group_read<EPI_BOXES - 1>();
+  __syncwarp();
+  uint4 *row = reinterpret_cast<uint4 *>(buf + lane * 64);
+  const int sw = (lane >> 1) & 3;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    uint4 t;
+    t.x = pack_bf16x2(y[8 * j + 0], y[8 * j + 1]);
+    t.y = pack_bf16x2(y[8 * j + 2], y[8 * j + 3]);
+    t.z = pack_bf16x2(y[8 * j + 4], y[8 * j + 5]);
+    t.w = pack_bf16x2(y[8 * j + 6], y[8 * j + 7]);
+    row[j ^ sw] = t;
+  }
+  fence_proxy_async_smem();
+  __syncwarp();
+  if (lane == 0 && any_row) {
+    tma_store_3d_hint(map, buf, col, row0, plane, l2_policy_evict_first());
+    bulk_commit_group();
+  }
+  box = box + 1 == EPI_BOXES ? 0 : box + 1;
+}
+
+__global__ void __launch_bounds__(NUM_THREADS, 1)
+    nvfp4_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                      const __grid_constant__ CUtensorMap tmSFA, const __grid_constant__ CUtensorMap tmSFB,
+                      const __grid_constant__ CUtensorMap tmOut, const Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                              ~static_cast<uintptr_t>(1023));
+  // per stage: A | B | SFA | SFB (every offset a multiple of 1024)
+  uint8_t *sEpi = smem + STAGES * STAGE_BYTES;
+  uint64_t *full_bar = reinterpret_cast<uint64_t *>(sEpi + EPI_SMEM);
+  uint64_t *empty_bar = full_bar + STAGES;
+  uint64_t *tfull_bar = empty_bar + STAGES;  // per CTA, one phase per tile
+  uint64_t *tfree_bar = tfull_bar + 1;       // leader: both epilogues drained the shared columns
+  uint64_t *drain_bar = tfree_bar + 1;
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(drain_bar + 1);
+  volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
+
+  const int warp = threadIdx.x / 32;
+  const int lane = threadIdx.x % 32;
+  const uint32_t rank = cluster_ctarank();
+  const int pair = blockIdx.x / 2;
+  const int num_pairs = gridDim.x / 2;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&empty_bar[s], 1);
+    }
+    mbar_init(tfull_bar, 1);
+    mbar_init(tfree_bar, 2 * 128);
+    mbar_init(drain_bar, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+    tma_prefetch_desc(&tmSFA);
+    tma_prefetch_desc(&tmSFB);
+    tma_prefetch_desc(&tmOut);
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(tmem_slot, TMEM_COLS);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  const int num_tiles = p.num_m_tiles * p.num_n_tiles;
+  const int kstages = (p.ktiles + KB_PER_STAGE - 1) / KB_PER_STAGE;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---------------- producer (both CTAs) ----------------
+      int s = 0;
+      uint32_t ph = 0;
+      uint32_t issued_phase[STAGES];
+      bool issued[STAGES];
+      for (int i = 0; i < STAGES; ++i) issued[i] = false;
+      bool ok = true;
+      const uint64_t keep = l2_policy_evict_last();
+      for (int tile = pair; tile < num_tiles && ok; tile += num_pairs) {
+        const int m_tile = tile / p.num_n_tiles;
+        const int n_tile = tile % p.num_n_tiles;
+        const int m_block = 2 * m_tile + static_cast<int>(rank);  // this CTA's 128-row block
+        for (int ks = 0; ks < kstages; ++ks) {
+          if (!mbar_wait(&empty_bar[s], ph ^ 1, abort_flag, p.status)) {
+            ok = false;
+            break;
+          }
+          const uint32_t full_leader = map_to_rank(smem_u32(&full_bar[s]), 0);
+          if (rank == 0) mbar_arrive_expect_tx(&full_bar[s], 2 * STAGE_BYTES);
+          uint8_t *st = smem + s * STAGE_BYTES;
+          const int32_t kt0 = ks * KB_PER_STAGE;
+          tma_load_2d_pair(st, &tmA, full_leader, ks * BK_BYTES, m_block * BM);
+          tma_load_2d_pair_hint(st + A_STAGE, &tmB, full_leader, ks * BK_BYTES,
+                                n_tile * BN + static_cast<int32_t>(rank) * BN_HALF, keep);
+          // scale blocks: rows of 256 bytes, two per 512-byte block
+          tma_load_2d_pair(st + A_STAGE + B_STAGE, &tmSFA, full_leader, 0,
+                           (m_block * p.ktiles + kt0) * 2);
+          for (int h = 0; h < 2; ++h)
+            tma_load_2d_pair_hint(st + A_STAGE + B_STAGE + SFA_STAGE + h * (KB_PER_STAGE * 512), &tmSFB,
+                                  full_leader, 0, ((2 * n_tile + h) * p.ktiles + kt0) * 2, keep);
+          issued[s] = true;
+          issued_phase[s] = ph;
+          if (++s == STAGES) {
+            s = 0;
+            ph ^= 1;
+          }
+        }
+      }
+      if (rank == 0)
+        for (int i = 0; i < STAGES; ++i)
+          if (issued[i]) mbar_wait(&full_bar[i], issued_phase[i], abort_flag, p.status);
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && rank == 0) {
+      // ---------------- MMA issuer (leader) ----------------
+      constexpr uint32_t idesc = idesc_nvf4_f32(2 * BM, BN);
+      int s = 0;
+      uint32_t ph = 0;
+      int t = 0;
+      bool ok = true;
+      for (int tile = pair; tile < num_tiles && ok; tile += num_pairs, ++t) {
+        if (t > 0 && !mbar_wait(tfree_bar, (t - 1) & 1, abort_flag, p.status)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + ((t & 1) ? ACC1_COL : 0u);
+        for (int ks = 0; ks < kstages; ++ks) {
+          if (!mbar_wait(&full_bar[s], ph, abort_flag, p.status)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const int kb_here = min(KB_PER_STAGE, p.ktiles - ks * KB_PER_STAGE);
+          uint8_t *st = smem + s * STAGE_BYTES;
+          const uint32_t sfa_smem = smem_u32(st + A_STAGE + B_STAGE);
+          const uint32_t sfb_smem = sfa_smem + SFA_STAGE;
+          const uint64_t a_desc = sw128_kmajor_desc(smem_u32(st));
+          const uint64_t b_desc = sw128_kmajor_desc(smem_u32(st + A_STAGE));
+          const uint64_t sfa_d = sf_block_desc(sfa_smem);
+          const uint64_t sfb_d = sf_block_desc(sfb_smem);
+          if (kb_here == KB_PER_STAGE) {
+            // full stage: fully unrolled issue (one thread issues every tcgen05 op,
+            // so its instruction count bounds the MMA rate)
+#pragma unroll
+            for (int kb = 0; kb < KB_PER_STAGE; ++kb) {
+              tmem_cp_32x128b_warpx4_pair(tmem_base + SFA_COL + 4 * kb, sfa_d + (kb * 512 >> 4));
+              tmem_cp_32x128b_warpx4_pair(tmem_base + SFB_COL + 8 * kb, sfb_d + (kb * 512 >> 4));
+              tmem_cp_32x128b_warpx4_pair(tmem_base + SFB_COL + 8 * kb + 4, sfb_d + ((KB_PER_STAGE * 512 + kb * 512) >> 4));
+            }
+#pragma unroll
+            for (int kb = 0; kb < KB_PER_STAGE; ++kb)
+              mma_mxf4nvf4_pair(d_tmem, a_desc + 2 * kb, b_desc + 2 * kb, idesc,
+                                tmem_base + SFA_COL + 4 * kb, tmem_base + SFB_COL + 8 * kb, (ks | kb) != 0);
+          } else {
+            for (int kb = 0; kb < kb_here; ++kb) {
+              tmem_cp_32x128b_warpx4_pair(tmem_base + SFA_COL + 4 * kb, sfa_d + (kb * 512 >> 4));
+              tmem_cp_32x128b_warpx4_pair(tmem_base + SFB_COL + 8 * kb, sfb_d + (kb * 512 >> 4));
+              tmem_cp_32x128b_warpx4_pair(tmem_base + SFB_COL + 8 * kb + 4, sfb_d + ((KB_PER_STAGE * 512 + kb * 512) >> 4));
+            }
+            for (int kb = 0; kb < kb_here; ++kb)
+              mma_mxf4nvf4_pair(d_tmem, a_desc + 2 * kb, b_desc + 2 * kb, idesc,
+                                tmem_base + SFA_COL + 4 * kb, tmem_base + SFB_COL + 8 * kb, (ks | kb) != 0);
+          }
+          tc_commit_pair(smem_u32(&empty_bar[s]));
+          tc_commit_pair(map_to_rank(smem_u32(&empty_bar[s]), 1));
+          if (++s == STAGES) {
+            s = 0;
+            ph ^= 1;
+          }
+        }
+        if (!ok) break;
+        tc_commit_pair(smem_u32(tfull_bar));
+        tc_commit_pair(map_to_rank(smem_u32(tfull_bar), 1));
+      }
+      tc_commit_pair(smem_u32(drain_bar));
+      mbar_wait(drain_bar, 0, abort_flag, p.status);
+    }
+  } else {
+    // ---------------- epilogue (warps 2..5 of both CTAs) ----------------
+    const int q = warp & 3;
+    uint8_t *warp_smem = sEpi + q * EPI_BOXES * EPI_BOX_BYTES;
+    int box = 0;
+    const float alpha = __ldg(p.alpha);
+    const uint32_t tfree_leader = map_to_rank(smem_u32(tfree_bar), 0);
+    int t = 0;
+    for (int tile = pair; tile < num_tiles; tile += num_pairs, ++t) {
+      if (!mbar_wait(tfull_bar, t & 1, abort_flag, p.status)) break;
+      tc_fence_after();
+      const int m_tile = tile / p.num_n_tiles;
+      const int n_tile = tile % p.num_n_tiles;
+      const int64_t row0 = static_cast<int64_t>(m_tile) * (2 * BM) + rank * BM + q * 32;
+      const bool live = row0 + lane < p.M;
+      const bool any_row = row0 < p.M;
+      const bool odd = t & 1;
+      const uint32_t t_row = tmem_base + (odd ? ACC1_COL : 0u) + (static_cast<uint32_t>(q * 32) << 16);
+#pragma unroll 1
+      for (int i = 0; i < BN / 32; ++i) {
+        const int c = odd ? i : (BN / 32 - 1 - i);
+        const int32_t n = n_tile * BN + c * 32;
+        float v[32];
+        tmem_ld_32x32b_x32(t_row + c * 32, v);
+        if (i == 1) {
+          // the 64 shared columns are in registers: release them to the MMA
+          tc_fence_before();
+          mbar_arrive_cluster(tfree_leader);
+        }
+        if (n >= p.N) continue;  // warp-uniform
+        const int32_t plane = n / p.plane_width;
+        const int32_t col = n - plane * p.plane_width;
+        if (live) {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) v[j] = bf16r(alpha * v[j]);
+          if (p.bias != nullptr) {
+            const uint4 *bq = reinterpret_cast<const uint4 *>(p.bias + n);
+#pragma unroll
+            for (int g = 0; g < 4; ++g) {
+              uint4 bt = __ldg(bq + g);
+              const __nv_bfloat162 *h = reinterpret_cast<const __nv_bfloat162 *>(&bt);
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                float2 f = __bfloat1622float2(h[e]);
+                v[8 * g + 2 * e] = bf16r(v[8 * g + 2 * e] + f.x);
+                v[8 * g + 2 * e + 1] = bf16r(v[8 * g + 2 * e + 1] + f.y);
+              }
+            }
+          }
+        } else {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) v[j] = 0.0f;
+        }
+        store_box(warp_smem, box, &tmOut, v, lane, col, static_cast<int32_t>(row0), plane, any_row);
+      }
+    }
+    if (lane == 0) bulk_wait_group_all();
+  }
+
+  __syncthreads();
+  __syncwarp();
+  cluster_sync();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, TMEM_COLS);
+  }
+}
+
+int map_u8(CUtensorMap *map, const void *base, int64_t rows, int64_t row_bytes, int box_x, int box_rows,
+           CUtensorMapSwizzle swizzle) {
+  auto encode = tensor_map_encoder();
+  if (encode == nullptr) return set_error(VFB_ECUDA, "cuTensorMapEncodeTiled is unavailable");
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(row_bytes), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(row_bytes)};
+  cuuint32_t box[2] = {static_cast<cuuint32_t>(box_x), static_cast<cuuint32_t>(box_rows)};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void *>(base), dims, strides,
+                      box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
+                      CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return set_error(VFB_ECUDA, "cuTensorMapEncodeTiled (nvfp4) failed (%d)", (int)r);
+  return VFB_OK;
+}
+
+int map_out(CUtensorMap *map, void *base, int64_t width, int64_t rows, int64_t planes) {
+  auto encode = tensor_map_encoder();
+  if (encode == nullptr) return set_error(VFB_ECUDA, "cuTensorMapEncodeTiled is unavailable");
+  cuuint64_t dims[3] = {static_cast<cuuint64_t>(width), static_cast<cuuint64_t>(rows),
+                        static_cast<cuuint64_t>(planes)};
+  cuuint64_t strides[2] = {static_cast<cuuint64_t>(width) * 2, static_cast<cuuint64_t>(width * rows) * 2};
+  cuuint32_t box[3] = {32, 32, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, base, dims, strides, box, estr,
+                      CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B,
+                      CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return set_error(VFB_ECUDA, "cuTensorMapEncodeTiled (output) failed (%d)", (int)r);
+  return VFB_OK;
+}
+
+bool a16(const void *p) { return reinterpret_cast<uintptr_t>(p) % 16 == 0; }
+
+}  // namespace
+}  // namespace vfb
+
+extern "C" int vfb_nvfp4_gemm(const void *A, const void *sfa, const void *W, const void *sfw,
+                              const float *alpha, int64_t M, int64_t N, int64_t K, const void *bias,
+                              void *out, int64_t planes, void *stream) {
+  using namespace vfb;
+  if (M < 0 || N <= 0 || K <= 0 || K % 64 || N % 128 || planes < 1 || planes > 3 || N % planes ||
+      (N / planes) % 32)
+    return set_error(VFB_EINVAL,
+                     "vfb_nvfp4_gemm: need K %% 64 == 0, N %% 128 == 0, 1..3 planes of width %% 32");
+  if (M == 0) return VFB_OK;
+  if (!A || !sfa || !W || !sfw || !alpha || !out)
+    return set_error(VFB_EINVAL, "vfb_nvfp4_gemm: NULL operand");
+  if (!a16(A) || !a16(W) || !a16(sfa) || !a16(sfw) || !a16(out) || (bias && !a16(bias)))
+    return set_error(VFB_EINVAL, "vfb_nvfp4_gemm: operands must be 16-byte aligned");
+  int sms = 0;
+  int rc = check_device(&sms);
+  if (rc != VFB_OK) return rc;
+  Params p{};
+  p.M = M;
+  p.N = N;
+  p.K = K;
+  p.alpha = alpha;
+  p.bias = static_cast<const __nv_bfloat16 *>(bias);
+  p.plane_width = static_cast<int32_t>(N / planes);
+  p.num_m_tiles = static_cast<int>((M + 2 * BM - 1) / (2 * BM));
+  p.num_n_tiles = static_cast<int>((N + BN - 1) / BN);
+  p.ktiles = static_cast<int>(K / 64);
+  p.status = device_status_ptr();
+  const int64_t a_blocks = (M + 127) / 128;  // 128-row scale blocks of the activation
+  const int64_t w_blocks = N / 128;
+  CUtensorMap ta, tb, tsa, tsb, to;
+  if ((rc = map_u8(&ta, A, M, K / 2, BK_BYTES, BM, CU_TENSOR_MAP_SWIZZLE_128B)) != VFB_OK) return rc;
+  if ((rc = map_u8(&tb, W, N, K / 2, BK_BYTES, BN_HALF, CU_TENSOR_MAP_SWIZZLE_128B)) != VFB_OK) return rc;
+  // scale buffers viewed as rows of 256 bytes (two rows per 512-byte block)
+  if ((rc = map_u8(&tsa, sfa, a_blocks * p.ktiles * 2, 256, 256, 2 * KB_PER_STAGE,
+                   CU_TENSOR_MAP_SWIZZLE_NONE)) != VFB_OK)
+    return rc;
+  if ((rc = map_u8(&tsb, sfw, w_blocks * p.ktiles * 2, 256, 256, 2 * KB_PER_STAGE,
+                   CU_TENSOR_MAP_SWIZZLE_NONE)) != VFB_OK)
+    return rc;
+  if ((rc = map_out(&to, out, N / planes, M, planes)) != VFB_OK) return rc;
+  cudaError_t err =
+      cudaFuncSetAttribute(nvfp4_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+  if (err != cudaSuccess) return set_error(VFB_ECUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(err));
+  const int tiles = p.num_m_tiles * p.num_n_tiles;
+  const int max_pairs = sms / 2;
+  const int pairs = tiles < max_pairs ? tiles : max_pairs;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(2 * pairs, 1, 1);
+  cfg.blockDim = dim3(NUM_THREADS, 1, 1);
+  cfg.dynamicSmemBytes = SMEM_BYTES;
+  cfg.stream = static_cast<cudaStream_t>(stream);
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  err = cudaLaunchKernelEx(&cfg, nvfp4_gemm_kernel, ta, tb, tsa, tsb, to, p);
+  if (err != cudaSuccess) return set_error(VFB_ECUDA, "vfb_nvfp4_gemm launch: %s", cudaGetErrorString(err));
+  return VFB_OK;
+}

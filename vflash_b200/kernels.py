@@ -37,27 +37,56 @@ def padded_rows(rows: int, multiple: int = 16) -> int:
     return -(-rows // multiple) * multiple
 
 
-def quantize_fp8_rows(matrix: torch.Tensor, *, pad_to: int = 16):
-    """Per-token e4m3 codes ``[ceil(M/pad_to)*pad_to, K]`` and fp32 scales ``[.., 1]``.
-
-    ``matrix`` is a bf16 ``[M, K]`` CUDA tensor with unit column stride (any
-    row stride, e.g. the value half of a packed FFN projection).
-    """
+def _check_fp8_input(matrix: torch.Tensor) -> tuple[int, int]:
     if matrix.dtype != BF16 or matrix.ndim != 2 or matrix.stride(1) != 1 and matrix.shape[1] > 1:
         raise KernelInputError("FP8 activation quantisation needs a bf16 [M,K] matrix with unit column stride")
     rows, cols = matrix.shape
     if not 1 <= cols <= 32768:
         raise KernelInputError("FP8 activation quantisation needs 1 <= K <= 32768")
+    return rows, cols
+
+
+def quantize_fp8_rows(matrix: torch.Tensor, *, pad_to: int = 16, amax: torch.Tensor | None = None):
+    """Per-token e4m3 codes ``[ceil(M/pad_to)*pad_to, K]`` and fp32 scales ``[.., 1]``.
+
+    ``matrix`` is a bf16 ``[M, K]`` CUDA tensor with unit column stride (any
+    row stride, e.g. the value half of a packed FFN projection).  ``amax``
+    (fp32 ``[M]``) supplies the row maxima instead of computing them — the
+    full row's maxima when ``matrix`` is one rank's slice of a split row.
+    """
+    rows, cols = _check_fp8_input(matrix)
     padded = padded_rows(rows, pad_to)
     codes = torch.empty((padded, cols), device=matrix.device, dtype=FP8)
     scales = torch.empty((padded, 1), device=matrix.device, dtype=torch.float32)
     lib = _lib.load()
+    x_ptr = matrix.data_ptr() if rows else None
+    ldx = max(matrix.stride(0), cols)
     with torch.cuda.device(matrix.device):
-        rc = lib.vfb_fp8_quant_rows(
-            matrix.data_ptr() if rows else None, rows, cols, max(matrix.stride(0), cols),
-            codes.data_ptr(), scales.data_ptr(), padded, _lib.stream_handle(matrix.device))
+        if amax is None:
+            rc = lib.vfb_fp8_quant_rows(x_ptr, rows, cols, ldx, codes.data_ptr(), scales.data_ptr(),
+                                        padded, _lib.stream_handle(matrix.device))
+        else:
+            if (amax.dtype != torch.float32 or amax.numel() != rows or not amax.is_contiguous()
+                    or amax.device != matrix.device):
+                raise KernelInputError("row maxima must be contiguous fp32 [M] on the input's device")
+            rc = lib.vfb_fp8_quant_rows_amax(x_ptr, rows, cols, ldx, amax.data_ptr(), codes.data_ptr(),
+                                             scales.data_ptr(), padded, _lib.stream_handle(matrix.device))
     _lib.check(rc, "vfb_fp8_quant_rows")
     return codes, scales
+
+
+def row_absmax(matrix: torch.Tensor) -> torch.Tensor:
+    """fp32 ``[M]`` row maxima of |x| (NaN for rows holding a NaN), as the quantiser computes them."""
+    rows, cols = _check_fp8_input(matrix)
+    amax = torch.empty(rows, device=matrix.device, dtype=torch.float32)
+    if rows == 0:
+        return amax
+    lib = _lib.load()
+    with torch.cuda.device(matrix.device):
+        rc = lib.vfb_fp8_row_absmax(matrix.data_ptr(), rows, cols, max(matrix.stride(0), cols),
+                                    amax.data_ptr(), _lib.stream_handle(matrix.device))
+    _lib.check(rc, "vfb_fp8_row_absmax")
+    return amax
 
 
 @dataclass

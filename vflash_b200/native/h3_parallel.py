@@ -1,0 +1,236 @@
+"""Multi-GPU execution of the quantised linears: token sharding and tensor parallelism.
+
+Generalises Hansimov/vflash src/vflash/native/h3_parallel.py from two devices
+in one process to ``world`` ranks, one process per GPU over NCCL:
+
+* **Token sharding** (the main mode, the reference's ``sequence`` partition,
+  ``_partition_invocation`` h3_parallel.py:364-399): rank r owns rows
+  ``[r*ceil(M/n), (r+1)*ceil(M/n))`` zero-padded to equal length; weights are
+  replicated and the linears need no collective.  ``gather_rows`` reassembles
+  full rows where a caller needs them (``all_gather`` + trim).
+* **Tensor parallelism** (only where weight memory forces it; the reference's
+  ``shard_h3_block``/``_split_matrix`` h3_parallel.py:34-88 and
+  ``_TensorBlock`` h3_parallel.py:220-250): QKV and ffn_in are split by output
+  rows with the Q/K/V (3) and value/gate (2) branch order kept, attention_out
+  and ffn_out by input features.  A row-parallel linear produces bf16 partial
+  sums on every rank, as the reference's BF16 TP block does; instead of the
+  reference's all-reduce they are combined with one NCCL reduce-scatter over
+  the token rows, which leaves the output token-sharded, and the bias /
+  gate / residual step runs after the reduction on the local token rows.
+  FP8 row scales belong to output rows, so a column split splits them with the
+  codes and a row split keeps them whole.  Each rank quantises its K-slice of
+  the activation with per-token scales over that slice.
+
+No kernel here reads peer memory; NCCL moves every byte.  The GEMM is a
+parameter (``linear``), so the host logic is testable with gloo ranks on CPU.
+"""
+
+from __future__ import annotations
+
+import datetime
+from collections.abc import Callable
+from dataclasses import dataclass
+from typing import Any
+
+import torch
+
+
+class ParallelError(ValueError):
+    """A sharding request is inconsistent with the tensors or the group."""
+
+
+# ---------------------------------------------------------------------------
+# weight sharding
+# ---------------------------------------------------------------------------
+def split_matrix(tensor: torch.Tensor, rank: int, world: int, *, axis: int, parts: int = 1) -> torch.Tensor:
+    """Compact shard ``rank`` of ``world`` along ``axis``, keeping ``parts`` branches in order.
+
+    With ``parts`` equal branches (Q/K/V = 3, value/gate = 2) each branch is
+    split separately, so shard r holds the r-th slice of every branch, in
+    branch order (h3_parallel.py:34-50 generalised from two ranks).
+    """
+    if tensor.ndim != 2 or axis not in (0, 1) or not 0 <= rank < world or parts < 1:
+        raise ParallelError("invalid matrix partition")
+    if tensor.shape[axis] % (world * parts):
+        raise ParallelError("matrix branches cannot be divided into equal shards")
+    width = tensor.shape[axis] // parts
+    piece = width // world
+    slices = [tensor.narrow(axis, part * width + rank * piece, piece) for part in range(parts)]
+    return torch.cat(slices, dim=axis).contiguous()
+
+
+@dataclass(frozen=True)
+class FP8Weight:
+    """e4m3 codes ``[N, K]`` and their fp32 per-output-row scales ``[N, 1]``."""
+
+    codes: torch.Tensor
+    row_scale: torch.Tensor
+
+
+def shard_fp8_weight(weight: FP8Weight, rank: int, world: int, *, mode: str, parts: int = 1) -> FP8Weight:
+    """Column (output rows) or row (input features) shard of an FP8 weight."""
+    if mode == "column":
+        return FP8Weight(split_matrix(weight.codes, rank, world, axis=0, parts=parts),
+                         split_matrix(weight.row_scale, rank, world, axis=0, parts=parts))
+    if mode == "row":
+        if parts != 1:
+            raise ParallelError("row shards have no branches")
+        return FP8Weight(split_matrix(weight.codes, rank, world, axis=1), weight.row_scale)
+    raise ParallelError("shard mode must be 'column' or 'row'")
+
+
+def shard_block(weights: dict[str, FP8Weight], rank: int, world: int) -> dict[str, FP8Weight]:
+    """Tensor-parallel shard of one block's four linears (qkv, attention_out, ffn_in, ffn_out)."""
+    return {
+        "qkv": shard_fp8_weight(weights["qkv"], rank, world, mode="column", parts=3),
+        "attention_out": shard_fp8_weight(weights["attention_out"], rank, world, mode="row"),
+        "ffn_in": shard_fp8_weight(weights["ffn_in"], rank, world, mode="column", parts=2),
+        "ffn_out": shard_fp8_weight(weights["ffn_out"], rank, world, mode="row"),
+    }
+
+
+# ---------------------------------------------------------------------------
+# token sharding
+# ---------------------------------------------------------------------------
+def shard_rows_count(total: int, world: int) -> int:
+    return -(-total // world)
+
+
+def partition_rows(states: torch.Tensor, rank: int, world: int, *, dim: int = 0) -> tuple[torch.Tensor, int]:
+    """Rank's token rows, zero-padded to ``ceil(total/world)``; returns (shard, valid rows)."""
+    if not 0 <= rank < world:
+        raise ParallelError("rank outside the group")
+    total = states.shape[dim]
+    rows = shard_rows_count(total, world)
+    begin = min(total, rank * rows)
+    end = min(total, begin + rows)
+    shard = states.narrow(dim, begin, end - begin)
+    valid = end - begin
+    if valid < rows:
+        pad_shape = list(shard.shape)
+        pad_shape[dim] = rows - valid
+        shard = torch.cat([shard, shard.new_zeros(pad_shape)], dim=dim)
+    return shard.contiguous(), valid
+
+
+def gather_rows(local: torch.Tensor, total: int, group=None, *, dim: int = 0) -> torch.Tensor:
+    """All-gather equal-length token shards and drop the padding rows."""
+    import torch.distributed as dist
+
+    world = dist.get_world_size(group)
+    parts = [torch.empty_like(local) for _ in range(world)]
+    dist.all_gather(parts, local.contiguous(), group=group)
+    return torch.cat(parts, dim=dim).narrow(dim, 0, total)
+
+
+Linear = Callable[[torch.Tensor, FP8Weight, Any], torch.Tensor]
+
+
+def token_sharded_linear(states: torch.Tensor, weight: FP8Weight, linear: Linear, *, rank: int, world: int,
+                         bias=None, gather: bool = False, group=None) -> torch.Tensor:
+    """Run ``linear`` on this rank's token rows (weights replicated, no collective).
+
+    With ``gather=True`` the full output is reassembled on every rank.
+    """
+    total = states.shape[0]
+    shard, _valid = partition_rows(states, rank, world)
+    out = linear(shard, weight, bias)
+    if gather:
+        return gather_rows(out, total, group)
+    return out
+
+
+def row_parallel_linear(states_cols: torch.Tensor, weight_shard: FP8Weight, linear: Linear, group=None,
+                        epilogue: Callable[[torch.Tensor], torch.Tensor] | None = None) -> torch.Tensor:
+    """Row-parallel linear: partial product on this rank's input features, then reduce-scatter.
+
+    ``states_cols`` holds all token rows and this rank's slice of the input
+    features; the bf16 partial sums of every rank are added by one
+    reduce-scatter over the token rows (rows padded to a multiple of the group
+    size), so each rank returns its token shard of the full product, and
+    ``epilogue`` (bias / gate / residual for those rows) runs after the sum.
+    """
+    import torch.distributed as dist
+
+    world = dist.get_world_size(group)
+    total = states_cols.shape[0]
+    rows = shard_rows_count(total, world)
+    partial = linear(states_cols, weight_shard, None)
+    if rows * world != total:
+        partial = torch.cat([partial, partial.new_zeros((rows * world - total, partial.shape[1]))])
+    out = torch.empty((rows, partial.shape[1]), dtype=partial.dtype, device=partial.device)
+    dist.reduce_scatter_tensor(out, partial.contiguous(), op=dist.ReduceOp.SUM, group=group)
+    return out if epilogue is None else epilogue(out)
+
+
+def row_parallel_fp8_linear(states_cols: torch.Tensor, weight_shard: FP8Weight, group=None,
+                            epilogue: Callable[[torch.Tensor], torch.Tensor] | None = None) -> torch.Tensor:
+    """Native row-parallel FP8 linear whose codes equal the unsplit quantisation.
+
+    Each rank holds every token row's slice of the input features.  The
+    per-token scale of the reference quantiser is taken over the whole row
+    (src/vflash/native/h3_fp8_linear.py:18-31), so the ranks first combine
+    their slices' row maxima with a MAX all-reduce and each quantises its
+    slice with the full row's maxima (``vfb_fp8_row_absmax`` /
+    ``vfb_fp8_quant_rows_amax``) — the codes are those of the unsplit row.
+    The partial GEMMs (bf16, no bias) are then summed by a reduce-scatter
+    over the token rows, as in ``row_parallel_linear``.
+    """
+    import torch.distributed as dist
+
+    from ..kernels import Epilogue, fp8_gemm, quantize_fp8_rows, row_absmax
+
+    rows = states_cols.shape[0]
+    amax = row_absmax(states_cols)
+    dist.all_reduce(amax, op=dist.ReduceOp.MAX, group=group)
+    codes, scales = quantize_fp8_rows(states_cols, amax=amax)
+
+    def linear(_x, w, _bias):
+        return fp8_gemm(codes, scales, rows, w.codes, w.row_scale, Epilogue())
+
+    return row_parallel_linear(states_cols, weight_shard, linear, group, epilogue)
+
+
+# ---------------------------------------------------------------------------
+# process groups and failure handling
+# ---------------------------------------------------------------------------
+def init_group(backend: str = "nccl", *, timeout_s: float = 120.0, device=None):
+    """Initialise the default process group from the launcher's environment (one rank per GPU)."""
+    import torch.distributed as dist
+
+    kwargs = {"timeout": datetime.timedelta(seconds=timeout_s)}
+    if backend == "nccl" and device is not None:
+        kwargs["device_id"] = device
+    dist.init_process_group(backend, **kwargs)
+    return dist.group.WORLD
+
+
+class RankFailure(RuntimeError):
+    """A peer rank failed; this rank's lane is closed."""
+
+
+def run_guarded(step: Callable[[], Any], *, group=None, store=None, rank: int = 0, key: str = "vfb_failed"):
+    """Run one step; on failure publish it in the store so peers stop before their next collective.
+
+    Mirrors the reference's abort-the-peer semantics (``_DevicePair.run``,
+    h3_parallel.py:311-330) for one process per rank: the failing rank records
+    its failure in the shared store and re-raises; ``check_peers`` on the other
+    ranks turns that record into ``RankFailure`` before they launch more work.
+    """
+    try:
+        return step()
+    except Exception:
+        if store is not None:
+            store.set(key, str(rank))
+        raise
+
+
+def check_peers(store, key: str = "vfb_failed") -> None:
+    """Raise ``RankFailure`` if a peer recorded a failure in the store."""
+    try:
+        if store.check([key]):
+            raise RankFailure(f"rank {store.get(key).decode()} failed; refusing further collectives")
+    except RankFailure:
+        raise
+    except Exception:  # pragma: no cover - stores without check()
+        return
