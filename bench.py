@@ -19,6 +19,11 @@ at N GPUs every rank runs its own full workload with replicated weights
 host memory and Q, K, V copied back to pinned host memory inside the timed
 region.
 
+``stack_c4`` is BASELINE config 4 on every rank: 48 blocks of FP8 linears
+over M=65520 tokens sharded across the ranks, weights streamed from the
+pinned host arena through the two-slot ring (and, for comparison, resident),
+milliseconds per denoising step as the max over ranks.
+
 ``--impl reference`` times the reference's own CPU path for this layer
 (``RowFP8Execution("weight-only").linear``: dequantise to bf16, then
 ``F.linear`` on the host cores) through the oracle's restatement, on a
@@ -260,6 +265,10 @@ def run_gpu(args) -> None:
         e2e_ms, e2e_steps = run_e2e(args, M, x_host, w_codes, w_scales, bias, device, stream, barrier)
         e2e_ms = max_over_ranks(e2e_ms)
 
+    stack = None
+    if not args.no_stack:
+        stack = stack_config(args, device, rank, world, barrier, max_over_ranks)
+
     library = None
     if rank == 0 and not args.no_library_probe:
         library = library_fp8_probe(device)
@@ -325,6 +334,8 @@ def run_gpu(args) -> None:
                        "d2h_bytes_per_step": M * N_QKV * 2,
                        "api": "RowFP8Execution('w8a8').qkv_linear, pinned host in/out",
                        "ms_per_step": round(e2e_ms / e2e_steps, 3)}
+    if stack is not None:
+        line["stack_c4"] = stack
     if library is not None:
         line["library_fp8_tflops"] = library
     if other is not None:
@@ -445,6 +456,99 @@ def other_configs(device, flush, stream) -> dict:
     out["peak_note"] = ("fp8 peak = 2 x measured cuBLAS bf16 burst, fp4 peak = 4 x; nominal dense "
                         "fp8 4.5, fp4 9 PFLOP/s")
     return out
+
+
+STACK_BLOCKS, STACK_TOKENS, STACK_HIDDEN, STACK_FFN = 48, 65520, 4096, 16384
+
+
+def stack_blocks(count: int, device):
+    """Seeded N(0,0.02) FP8 weights of ``count`` blocks, one block at a time (per-row e4m3)."""
+    from vflash_b200.native.h3_block_stack import block_shapes
+    from vflash_b200.native.h3_parallel import FP8Weight
+
+    gen = torch.Generator(device=device)
+    for b in range(count):
+        block = {}
+        for j, (name, n, k) in enumerate(block_shapes(STACK_HIDDEN, STACK_FFN)):
+            gen.manual_seed(7000 + 10 * b + j)
+            w = torch.randn(n, k, generator=gen, device=device) * 0.02
+            scale = w.abs().amax(dim=1, keepdim=True) / 448.0
+            block[name] = FP8Weight((w / scale).to(torch.float8_e4m3fn), scale)
+            del w
+        yield block
+
+
+def stack_config(args, device, rank: int, world: int, barrier, max_over_ranks) -> dict:
+    """Config 4: 48 blocks of FP8 linears, M = 65520 tokens sharded over the ranks.
+
+    Weights stream from the pinned arena through the two-slot ring (each rank
+    pins and copies 1/world of every block; NCCL all-gathers the rest) and,
+    for comparison, from a resident copy of the stack.  Every rank runs the
+    same collective steps; times are the max over ranks.
+    """
+    import torch.distributed as dist
+
+    from vflash_b200.native.h3_block_stack import FP8BlockStack, block_flops, block_linears
+    from vflash_b200.native.h3_parallel import partition_rows, shard_rows_count
+    from vflash_b200.native.h3_pinned_arena import FP8BlockRing
+
+    group = dist.group.WORLD if world > 1 else None
+    blocks = args.stack_blocks
+    t0 = time.perf_counter()
+    stack = FP8BlockStack(stack_blocks(blocks, device), STACK_HIDDEN, STACK_FFN, device, group=group)
+    setup_s = time.perf_counter() - t0
+    gen = torch.Generator(device=device).manual_seed(4004)
+    tokens = torch.randn(STACK_TOKENS, STACK_HIDDEN, generator=gen, device=device).to(torch.bfloat16)
+    shard, valid = partition_rows(tokens, rank, world)
+    del tokens
+    shard = shard.reshape(-1, 1, STACK_HIDDEN)
+    gate = torch.full((1, STACK_HIDDEN), 1 / 32, dtype=torch.bfloat16, device=device)
+    stream = torch.cuda.current_stream(device)
+
+    def timed(forward, steps: int) -> tuple[float, torch.Tensor]:
+        out = forward(shard, gate)  # warm-up step
+        barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(steps):
+            out = forward(shard, gate)
+        e1.record(stream)
+        barrier()
+        return max_over_ranks(e0.elapsed_time(e1) / steps), out
+
+    steps = args.stack_steps
+    streamed_ms, out = timed(stack.forward, steps)
+    finite = bool(torch.isfinite(out[:valid].float()).all())
+    resident_ring = FP8BlockRing(stack.layout, stack.host_blocks, device, group=group, resident=True)
+    resident_ms, out2 = timed(
+        lambda h, g: resident_ring.run(h, lambda w, x: block_linears(stack.execution, w, x, g)), steps)
+    same = bool(torch.equal(out, out2))
+    del resident_ring, out, out2
+    torch.cuda.empty_cache()
+    peaks = measured_peaks()
+    fp8_peak = 2.0 * float(peaks.get("bf16_tflops_sustained", peaks.get("bf16_tflops", 1400.0)))
+    rows = shard_rows_count(STACK_TOKENS, world)
+    flop_step = blocks * block_flops(STACK_TOKENS, STACK_HIDDEN, STACK_FFN)
+    per_gpu_tflops = blocks * block_flops(rows, STACK_HIDDEN, STACK_FFN) / (streamed_ms * 1e-3) / 1e12
+    return {
+        "workload": f"c4: {blocks} blocks x FP8 linears (QKV [12288,4096], out [4096,4096], up [16384,4096] "
+                    f"GELU-tanh, down [4096,16384]); M={STACK_TOKENS} tokens, {rows} per rank",
+        "streamed_ms_per_step": round(streamed_ms, 2),
+        "resident_ms_per_step": round(resident_ms, 2),
+        "streaming_overhead": round(streamed_ms / resident_ms - 1.0, 4),
+        "tflops_whole_job": round(flop_step / (streamed_ms * 1e-3) / 1e12, 1),
+        "tflops_per_gpu": round(per_gpu_tflops, 1),
+        "frac_of_sustained_peak": round(per_gpu_tflops / fp8_peak, 4),
+        "weight_bytes_per_block": stack.weight_bytes_per_block,
+        "h2d_bytes_per_rank_per_step": blocks * stack.ring.chunk,
+        "weight_path": "pinned arena -> copy stream (two slots)" + (
+            f", each rank copies 1/{world} of a block and NCCL all-gathers the rest" if world > 1 else ""),
+        "output_finite": finite,
+        "streamed_equals_resident": same,
+        "setup_s": round(setup_s, 1),
+        "steps": steps,
+        "l2": "inputs larger than L2 (201 MB of weights per block)",
+    }
 
 
 def library_fp8_probe(device) -> dict:
@@ -572,6 +676,9 @@ def main() -> None:
     parser.add_argument("--no-cpu-baseline", action="store_true")
     parser.add_argument("--no-library-probe", action="store_true")
     parser.add_argument("--no-e2e", action="store_true")
+    parser.add_argument("--no-stack", action="store_true", help="skip the config 4 block stack")
+    parser.add_argument("--stack-blocks", type=int, default=STACK_BLOCKS)
+    parser.add_argument("--stack-steps", type=int, default=2)
     parser.add_argument("--no-other-configs", action="store_true",
                         help="skip the extra BASELINE config 0/2/3 measurements")
     parser.add_argument("--rows", type=int, default=M,

@@ -3,7 +3,8 @@
 Token-sharded rows must equal the single-GPU result bit for bit (each output
 row depends only on its own input row); the row-parallel (reduce-scatter)
 variant must agree with the unsharded linear within bf16 tolerance
-(rel-L2 <= 1e-2).  Needs two SM100 GPUs; skipped otherwise.  The process
+(rel-L2 <= 1e-2); the block stack whose weights each rank pins half of and
+all-gathers must equal a direct loop over device weights bit for bit.  Needs two SM100 GPUs; skipped otherwise.  The process
 group uses a short timeout, and NVLS is off (NCCL_NVLS_ENABLE=0).
 """
 
@@ -77,9 +78,25 @@ def _worker(rank, world, port, result_path):
         codes_exact = bool(torch.equal(codes.view(torch.uint8),
                                        full_codes.view(torch.uint8)[:, rank * cols:(rank + 1) * cols])
                            and torch.equal(scales, full_scales))
+        # block stack: each rank pins half of every block, the all-gather over
+        # NVLink rebuilds it, and the rank's token shard matches a direct loop
+        from vflash_b200.native.h3_block_stack import FP8BlockStack, block_linears, block_shapes
+
+        hid, ffn = 256, 1024
+        blocks = [{name: weight(nn, kk, 50 + 10 * b + j)
+                   for j, (name, nn, kk) in enumerate(block_shapes(hid, ffn))} for b in range(3)]
+        tokens = torch.randn(333, hid, generator=torch.Generator().manual_seed(6)).to(torch.bfloat16).to(device)
+        shard, _valid = par.partition_rows(tokens, rank, world)
+        shard = shard.reshape(-1, 1, hid)
+        gate = torch.full((1, hid), 1 / 32, dtype=torch.bfloat16, device=device)
+        want = shard
+        for block in blocks:
+            want = block_linears(execution, block, want, gate)
+        stack = FP8BlockStack(blocks, hid, ffn, device, group=dist.group.WORLD, chunk_bytes=1 << 20)
+        stack_exact = all(bool(torch.equal(stack.forward(shard, gate), want)) for _ in range(2))
         torch.cuda.synchronize()
-        torch.save({"token_exact": token_exact, "tp_rel": rel, "codes_exact": codes_exact},
-                   f"{result_path}.{rank}")
+        torch.save({"token_exact": token_exact, "tp_rel": rel, "codes_exact": codes_exact,
+                    "stack_exact": stack_exact}, f"{result_path}.{rank}")
     finally:
         dist.destroy_process_group()
 
@@ -93,3 +110,4 @@ def test_two_gpu_token_sharding_and_tensor_parallel(tmp_path):
         assert res["token_exact"], f"rank {r}: token-sharded rows differ from the single-GPU result"
         assert res["codes_exact"], f"rank {r}: split-row codes differ from the unsplit quantisation"
         assert res["tp_rel"] <= 1e-2, res
+        assert res["stack_exact"], f"rank {r}: the streamed block stack differs from a direct loop"
