@@ -329,6 +329,28 @@ __device__ __forceinline__ uint32_t pack_e2m1x8(const float (&v)[8]) {
   return r;
 }
 
+// ---- warp-wide issue ----------------------------------------------------------
+// The tcgen05 issuer runs as a whole converged warp and one elected lane
+// issues: the operands (descriptors, TMEM addresses, loop state) are then
+// warp-uniform, which a single-lane branch (`if (lane == 0)`) hides from the
+// compiler.  Measured on the block-scaled GEMM: 2.7 -> 4.7 PFLOP/s.
+__device__ __forceinline__ bool elect_one() {
+  uint32_t pred = 0;
+  asm volatile(
+      "{\n\t.reg .pred P;\n\t"
+      "elect.sync _|P, 0xffffffff;\n\t"
+      "selp.b32 %0, 1, 0, P;\n\t}"
+      : "=r"(pred));
+  return pred != 0;
+}
+
+// Every lane waits (bounded); the warp proceeds only if all lanes saw the phase.
+__device__ __forceinline__ bool warp_wait(uint64_t *bar, uint32_t parity, volatile int *abort_flag,
+                                          int *status) {
+  const bool ok = mbar_wait(bar, parity, abort_flag, status);
+  return __all_sync(0xffffffffu, ok);
+}
+
 // ---- CTA pairs (2-CTA clusters) ---------------------------------------------
 __device__ __forceinline__ uint32_t cluster_ctarank() {
   uint32_t r;

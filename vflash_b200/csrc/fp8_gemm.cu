@@ -115,19 +115,6 @@ __device__ __forceinline__ void load_bf16x32(const __nv_bfloat16 *p, float (&r)[
   }
 }
 
-__device__ __forceinline__ void store_bf16x32(__nv_bfloat16 *p, const float (&y)[32]) {
-  uint4 *q = reinterpret_cast<uint4 *>(p);
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    uint4 t;
-    t.x = pack_bf16x2(y[8 * i + 0], y[8 * i + 1]);
-    t.y = pack_bf16x2(y[8 * i + 2], y[8 * i + 3]);
-    t.z = pack_bf16x2(y[8 * i + 4], y[8 * i + 5]);
-    t.w = pack_bf16x2(y[8 * i + 6], y[8 * i + 7]);
-    q[i] = t;
-  }
-}
-
 // Writes one 32 x 32 output box: lane i holds row i of the warp's 32 rows.
 // The rows go to shared memory in the 64-byte swizzle the output tensor map
 // uses (conflict-free 16-byte stores), then lane 0 issues one TMA store.
@@ -277,9 +264,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           if (issued[i]) mbar_wait(&full_bar[i], issued_phase[i], abort_flag, p.status);
     }
   } else if (warp == 1) {
-    if (lane == 0 && rank == 0) {
-      // ---------------- MMA issuer (leader CTA only) ----------------
+    if (rank == 0) {
+      // ---------------- MMA issuer (leader CTA only): whole warp, one elected lane ----------------
       constexpr uint32_t idesc = idesc_e4m3_f32(2 * BM, BN);
+      const bool leader = elect_one();  // the same lane issues and commits every tcgen05 op
       int s = 0;
       uint32_t ph = 0;
       int t = 0;
@@ -287,41 +275,49 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       for (int tile = pair; tile < num_tiles && ok; tile += num_pairs, ++t) {
         const int acc = t & 1;
         const uint32_t acc_ph = (t >> 1) & 1;
-        if (!mbar_wait(&tempty_bar[acc], acc_ph ^ 1, abort_flag, p.status)) break;
+        if (!warp_wait(&tempty_bar[acc], acc_ph ^ 1, abort_flag, p.status)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * BN;
         for (int kb = 0; kb < p.num_kb; ++kb) {
-          if (!mbar_wait(&full_bar[s], ph, abort_flag, p.status)) {
+          if (!warp_wait(&full_bar[s], ph, abort_flag, p.status)) {
             ok = false;
             break;
           }
           tc_fence_after();
           const uint64_t a_desc = sw128_kmajor_desc(smem_u32(sA + s * A_STAGE_BYTES));
           const uint64_t b_desc = sw128_kmajor_desc(smem_u32(sB + s * B_STAGE_BYTES));
+          if (leader) {
 #pragma unroll
-          for (int k = 0; k < BK / UMMA_K; ++k) {
-            // +32 bytes along K inside the swizzled 128-byte row = +2 in 16-byte units.
-            mma_f8f6f4_pair(d_tmem, a_desc + 2 * k, b_desc + 2 * k, idesc, (kb | k) != 0);
+            for (int k = 0; k < BK / UMMA_K; ++k) {
+              // +32 bytes along K inside the swizzled 128-byte row = +2 in 16-byte units.
+              mma_f8f6f4_pair(d_tmem, a_desc + 2 * k, b_desc + 2 * k, idesc, (kb | k) != 0);
+            }
+            tc_commit_pair(smem_u32(&empty_bar[s]));
+            tc_commit_pair(map_to_rank(smem_u32(&empty_bar[s]), 1));
           }
-          tc_commit_pair(smem_u32(&empty_bar[s]));
-          tc_commit_pair(map_to_rank(smem_u32(&empty_bar[s]), 1));
+          __syncwarp();
           if (++s == STAGES) {
             s = 0;
             ph ^= 1;
           }
         }
         if (!ok) break;
-        tc_commit_pair(smem_u32(&tfull_bar[acc]));
-        tc_commit_pair(map_to_rank(smem_u32(&tfull_bar[acc]), 1));
+        if (leader) {
+          tc_commit_pair(smem_u32(&tfull_bar[acc]));
+          tc_commit_pair(map_to_rank(smem_u32(&tfull_bar[acc]), 1));
+        }
+        __syncwarp();
       }
-      // Drain: all MMAs issued by this thread are complete before TMEM is freed.
-      tc_commit_pair(smem_u32(drain_bar));
-      mbar_wait(drain_bar, 0, abort_flag, p.status);
+      // Drain: all MMAs issued by the leader lane are complete before TMEM is freed.
+      if (leader) {
+        tc_commit_pair(smem_u32(drain_bar));
+        mbar_wait(drain_bar, 0, abort_flag, p.status);
+      }
+      __syncwarp();
     }
   } else {
     // ---------------- epilogue (warps 2..5 of both CTAs) ----------------
     const int q = warp & 3;  // TMEM lane quarter this warp may access
-    const int row = q * 32 + lane;
     const EpiParams &ep = p.ep;
     uint8_t *warp_smem = sEpi + q * EPI_BOXES * EPI_BOX_BYTES;
     int box = 0;

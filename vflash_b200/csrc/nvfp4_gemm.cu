@@ -181,19 +181,20 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           if (issued[i]) mbar_wait(&full_bar[i], issued_phase[i], abort_flag, p.status);
     }
   } else if (warp == 1) {
-    if (lane == 0 && rank == 0) {
-      // ---------------- MMA issuer (leader) ----------------
+    if (rank == 0) {
+      // ---------------- MMA issuer (leader CTA only): whole warp, one elected lane ----------------
       constexpr uint32_t idesc = idesc_nvf4_f32(2 * BM, BN);
+      const bool leader = elect_one();  // the same lane issues and commits every tcgen05 op
       int s = 0;
       uint32_t ph = 0;
       int t = 0;
       bool ok = true;
       for (int tile = pair; tile < num_tiles && ok; tile += num_pairs, ++t) {
-        if (t > 0 && !mbar_wait(tfree_bar, (t - 1) & 1, abort_flag, p.status)) break;
+        if (t > 0 && !warp_wait(tfree_bar, (t - 1) & 1, abort_flag, p.status)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + ((t & 1) ? ACC1_COL : 0u);
         for (int ks = 0; ks < kstages; ++ks) {
-          if (!mbar_wait(&full_bar[s], ph, abort_flag, p.status)) {
+          if (!warp_wait(&full_bar[s], ph, abort_flag, p.status)) {
             ok = false;
             break;
           }
@@ -206,42 +207,49 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           const uint64_t b_desc = sw128_kmajor_desc(smem_u32(st + A_STAGE));
           const uint64_t sfa_d = sf_block_desc(sfa_smem);
           const uint64_t sfb_d = sf_block_desc(sfb_smem);
-          if (kb_here == KB_PER_STAGE) {
-            // full stage: fully unrolled issue (one thread issues every tcgen05 op,
-            // so its instruction count bounds the MMA rate)
+          if (leader) {
+            if (kb_here == KB_PER_STAGE) {
 #pragma unroll
-            for (int kb = 0; kb < KB_PER_STAGE; ++kb) {
-              tmem_cp_32x128b_warpx4_pair(tmem_base + SFA_COL + 4 * kb, sfa_d + (kb * 512 >> 4));
-              tmem_cp_32x128b_warpx4_pair(tmem_base + SFB_COL + 8 * kb, sfb_d + (kb * 512 >> 4));
-              tmem_cp_32x128b_warpx4_pair(tmem_base + SFB_COL + 8 * kb + 4, sfb_d + ((KB_PER_STAGE * 512 + kb * 512) >> 4));
-            }
+              for (int kb = 0; kb < KB_PER_STAGE; ++kb) {
+                tmem_cp_32x128b_warpx4_pair(tmem_base + SFA_COL + 4 * kb, sfa_d + (kb * 512 >> 4));
+                tmem_cp_32x128b_warpx4_pair(tmem_base + SFB_COL + 8 * kb, sfb_d + (kb * 512 >> 4));
+                tmem_cp_32x128b_warpx4_pair(tmem_base + SFB_COL + 8 * kb + 4, sfb_d + ((KB_PER_STAGE * 512 + kb * 512) >> 4));
+              }
 #pragma unroll
-            for (int kb = 0; kb < KB_PER_STAGE; ++kb)
-              mma_mxf4nvf4_pair(d_tmem, a_desc + 2 * kb, b_desc + 2 * kb, idesc,
-                                tmem_base + SFA_COL + 4 * kb, tmem_base + SFB_COL + 8 * kb, (ks | kb) != 0);
-          } else {
-            for (int kb = 0; kb < kb_here; ++kb) {
-              tmem_cp_32x128b_warpx4_pair(tmem_base + SFA_COL + 4 * kb, sfa_d + (kb * 512 >> 4));
-              tmem_cp_32x128b_warpx4_pair(tmem_base + SFB_COL + 8 * kb, sfb_d + (kb * 512 >> 4));
-              tmem_cp_32x128b_warpx4_pair(tmem_base + SFB_COL + 8 * kb + 4, sfb_d + ((KB_PER_STAGE * 512 + kb * 512) >> 4));
+              for (int kb = 0; kb < KB_PER_STAGE; ++kb)
+                mma_mxf4nvf4_pair(d_tmem, a_desc + 2 * kb, b_desc + 2 * kb, idesc,
+                                  tmem_base + SFA_COL + 4 * kb, tmem_base + SFB_COL + 8 * kb, (ks | kb) != 0);
+            } else {
+              for (int kb = 0; kb < kb_here; ++kb) {
+                tmem_cp_32x128b_warpx4_pair(tmem_base + SFA_COL + 4 * kb, sfa_d + (kb * 512 >> 4));
+                tmem_cp_32x128b_warpx4_pair(tmem_base + SFB_COL + 8 * kb, sfb_d + (kb * 512 >> 4));
+                tmem_cp_32x128b_warpx4_pair(tmem_base + SFB_COL + 8 * kb + 4, sfb_d + ((KB_PER_STAGE * 512 + kb * 512) >> 4));
+              }
+              for (int kb = 0; kb < kb_here; ++kb)
+                mma_mxf4nvf4_pair(d_tmem, a_desc + 2 * kb, b_desc + 2 * kb, idesc,
+                                  tmem_base + SFA_COL + 4 * kb, tmem_base + SFB_COL + 8 * kb, (ks | kb) != 0);
             }
-            for (int kb = 0; kb < kb_here; ++kb)
-              mma_mxf4nvf4_pair(d_tmem, a_desc + 2 * kb, b_desc + 2 * kb, idesc,
-                                tmem_base + SFA_COL + 4 * kb, tmem_base + SFB_COL + 8 * kb, (ks | kb) != 0);
+            tc_commit_pair(smem_u32(&empty_bar[s]));
+            tc_commit_pair(map_to_rank(smem_u32(&empty_bar[s]), 1));
           }
-          tc_commit_pair(smem_u32(&empty_bar[s]));
-          tc_commit_pair(map_to_rank(smem_u32(&empty_bar[s]), 1));
+          __syncwarp();
           if (++s == STAGES) {
             s = 0;
             ph ^= 1;
           }
         }
         if (!ok) break;
-        tc_commit_pair(smem_u32(tfull_bar));
-        tc_commit_pair(map_to_rank(smem_u32(tfull_bar), 1));
+        if (leader) {
+          tc_commit_pair(smem_u32(tfull_bar));
+          tc_commit_pair(map_to_rank(smem_u32(tfull_bar), 1));
+        }
+        __syncwarp();
       }
-      tc_commit_pair(smem_u32(drain_bar));
-      mbar_wait(drain_bar, 0, abort_flag, p.status);
+      if (leader) {
+        tc_commit_pair(smem_u32(drain_bar));
+        mbar_wait(drain_bar, 0, abort_flag, p.status);
+      }
+      __syncwarp();
     }
   } else {
     // ---------------- epilogue (warps 2..5 of both CTAs) ----------------
