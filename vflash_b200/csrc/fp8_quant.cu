@@ -13,8 +13,9 @@
 //
 // Layout: one group of TPR threads (a multiple of 32) owns one row and keeps
 // the whole row in registers as packed bf16 (4 x 16-byte loads per thread, so
-// K <= 32768 needs at most 1024 threads); the row maximum is reduced with warp
-// shuffles and, across the row's warps, through shared memory.  Each byte of
+// K <= 32768 needs at most 1024 threads); the row maximum is taken on the bf16
+// bit patterns (packed 16-bit max), reduced with redux.sync and, across the
+// row's warps, through shared memory.  Each byte of
 // x is read once and each code written once: 3 bytes of traffic per element.
 #include <cfloat>
 
@@ -25,13 +26,6 @@ namespace {
 
 constexpr int kVecPerThread = 4;     // 16-byte vectors (8 bf16) per thread
 constexpr int kBlockThreads = 256;
-
-__device__ __forceinline__ float clamp448(float q) {
-  // NaN-preserving clamp (torch.clamp keeps NaN).
-  q = q > 448.0f ? 448.0f : q;
-  q = q < -448.0f ? -448.0f : q;
-  return q;
-}
 
 __device__ __forceinline__ float row_scale(float amax, bool nan) {
   if (nan || !(amax > 0.0f)) return 1.0f;
@@ -47,18 +41,23 @@ __device__ __forceinline__ float row_scale(float amax, bool nan) {
 // RN(q + remainder * recip) is the correctly rounded quotient.  Quotients
 // small enough to lose precision to fp32 underflow lie far below half the
 // smallest e4m3 subnormal, so their codes (signed zero) are unaffected.
-// The scale is positive, so the quotient carries the sign of x; copying it
-// back keeps -0 / scale = -0 (the correction step would produce +0).
+// The remainder is formed negated, q * scale - x (exact, the negation of
+// x - q * scale), so the correction -rem_neg * recip + q keeps the sign of a
+// zero quotient: -0 / scale = -0 without a separate sign copy.
 __device__ __forceinline__ float div_rn_by_scale(float x, float scale, float recip) {
   const float q = x * recip;
-  const float rem = fmaf(-q, scale, x);
-  return copysignf(fmaf(rem, recip, q), x);
+  const float rem_neg = fmaf(q, scale, -x);
+  return fmaf(-rem_neg, recip, q);
 }
 
 // Quotient used for the codes: exact division routine for non-finite scales.
 __device__ __forceinline__ float quotient(float x, float scale, float recip, bool fast) {
   return fast ? div_rn_by_scale(x, scale, recip) : __fdiv_rn(x, scale);
 }
+
+// The clamp to [-448, 448] of the reference is the saturation of
+// cvt.rn.satfinite.e4m3x2 (finite values beyond 448 and infinities become
+// +-448, NaN stays NaN), so no separate clamp is applied.
 
 // Codes of 8 bf16 values (one 16-byte vector) for a finite scale.
 __device__ __forceinline__ uint2 quantize8(const uint4 &v, float scale, float recip) {
@@ -67,8 +66,7 @@ __device__ __forceinline__ uint2 quantize8(const uint4 &v, float scale, float re
 #pragma unroll
   for (int j = 0; j < 4; ++j) {
     float2 f = __bfloat1622float2(h[j]);
-    q[j] = pack_e4m3x2(clamp448(div_rn_by_scale(f.x, scale, recip)),
-                       clamp448(div_rn_by_scale(f.y, scale, recip)));
+    q[j] = pack_e4m3x2(div_rn_by_scale(f.x, scale, recip), div_rn_by_scale(f.y, scale, recip));
   }
   return make_uint2(static_cast<uint32_t>(q[0]) | (static_cast<uint32_t>(q[1]) << 16),
                     static_cast<uint32_t>(q[2]) | (static_cast<uint32_t>(q[3]) << 16));
@@ -81,10 +79,25 @@ __device__ __noinline__ uint2 quantize8_ieee(uint4 v, float scale) {
 #pragma unroll
   for (int j = 0; j < 4; ++j) {
     float2 f = __bfloat1622float2(h[j]);
-    q[j] = pack_e4m3x2(clamp448(__fdiv_rn(f.x, scale)), clamp448(__fdiv_rn(f.y, scale)));
+    q[j] = pack_e4m3x2(__fdiv_rn(f.x, scale), __fdiv_rn(f.y, scale));
   }
   return make_uint2(static_cast<uint32_t>(q[0]) | (static_cast<uint32_t>(q[1]) << 16),
                     static_cast<uint32_t>(q[2]) | (static_cast<uint32_t>(q[3]) << 16));
+}
+
+// Row maximum on the bf16 bit patterns: with the sign cleared, |x| orders
+// like the unsigned bits, and every NaN pattern (0x7f81..0x7fff) orders above
+// +inf (0x7f80).  One packed 16-bit max per two values gives both the row's
+// amax (the largest non-NaN magnitude when the maximum is <= 0x7f80) and its
+// NaN flag (maximum > 0x7f80); the amax value is the bf16 with those bits.
+constexpr uint32_t kBf16Inf = 0x7f80u;
+
+__device__ __forceinline__ uint32_t abs_bits_max8(const uint4 &v, uint32_t acc) {
+  acc = __vmaxu2(acc, v.x & 0x7fff7fffu);
+  acc = __vmaxu2(acc, v.y & 0x7fff7fffu);
+  acc = __vmaxu2(acc, v.z & 0x7fff7fffu);
+  acc = __vmaxu2(acc, v.w & 0x7fff7fffu);
+  return acc;
 }
 
 // Vector path: x rows 16-byte aligned, K % 8 == 0.
@@ -95,7 +108,7 @@ __global__ void __launch_bounds__(1024, 1) fp8_quant_rows_vec(
     const __nv_bfloat16 *__restrict__ x, int64_t M, int64_t K, int64_t ldx,
     uint8_t *__restrict__ codes, float *__restrict__ scales, int64_t M_pad, int tpr,
     const float *__restrict__ amax_in, float *__restrict__ amax_out) {
-  extern __shared__ float red[];  // [rows per block][warps per row] maxima + nan flags
+  extern __shared__ uint32_t red[];  // [rows per block][warps per row] maxima (bit patterns)
   const int rows_per_block = blockDim.x / tpr;
   const int r_local = threadIdx.x / tpr;
   const int t = threadIdx.x % tpr;
@@ -107,6 +120,7 @@ __global__ void __launch_bounds__(1024, 1) fp8_quant_rows_vec(
   float amax = 0.0f;
   bool nan = false;
   const bool live = row < M;
+  uint32_t bits = 0;
   if (live) {
     const uint4 *src = reinterpret_cast<const uint4 *>(x + row * ldx);
 #pragma unroll
@@ -115,35 +129,19 @@ __global__ void __launch_bounds__(1024, 1) fp8_quant_rows_vec(
       v[i] = c < nvec ? __ldcs(src + c) : make_uint4(0, 0, 0, 0);
     }
 #pragma unroll
-    for (int i = 0; i < kVecPerThread; ++i) {
-      const __nv_bfloat162 *h = reinterpret_cast<const __nv_bfloat162 *>(&v[i]);
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        float2 f = __bfloat1622float2(h[j]);
-        nan |= (f.x != f.x) | (f.y != f.y);
-        amax = fmaxf(amax, fmaxf(fabsf(f.x), fabsf(f.y)));
-      }
-    }
+    for (int i = 0; i < kVecPerThread; ++i) bits = abs_bits_max8(v[i], bits);
   }
   if (amax_in == nullptr) {  // block-uniform
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
-    nan = __any_sync(0xffffffffu, nan);
+    uint32_t m = __reduce_max_sync(0xffffffffu, max(bits & 0xffffu, bits >> 16));
     if (warps_per_row > 1) {
-      float *row_red = red + r_local * warps_per_row * 2;
-      if ((t & 31) == 0) {
-        row_red[t / 32] = amax;
-        row_red[warps_per_row + t / 32] = nan ? 1.0f : 0.0f;
-      }
+      uint32_t *row_red = red + r_local * warps_per_row;
+      if ((t & 31) == 0) row_red[t / 32] = m;
       __syncthreads();
-      amax = 0.0f;
-      float any_nan = 0.0f;
-      for (int w = 0; w < warps_per_row; ++w) {
-        amax = fmaxf(amax, row_red[w]);
-        any_nan = fmaxf(any_nan, row_red[warps_per_row + w]);
-      }
-      nan = any_nan != 0.0f;
+      m = 0;
+      for (int w = 0; w < warps_per_row; ++w) m = max(m, row_red[w]);
     }
+    nan = m > kBf16Inf;
+    amax = __uint_as_float(m << 16);
   } else {
     amax = live ? amax_in[row] : 0.0f;
     nan = amax != amax;
@@ -217,7 +215,7 @@ __global__ void __launch_bounds__(kBlockThreads) fp8_quant_rows_scalar(
     uint8_t q = 0;
     if (live) {
       float f = __bfloat162float(x[row * ldx + c]);
-      q = static_cast<uint8_t>(pack_e4m3x2(clamp448(quotient(f, scale, recip, fast)), 0.0f) & 0xFF);
+      q = static_cast<uint8_t>(pack_e4m3x2(quotient(f, scale, recip, fast), 0.0f) & 0xFF);
     }
     codes[row * K + c] = q;
   }
@@ -245,7 +243,7 @@ int launch_quant(const char *what, const void *x, int64_t M, int64_t K, int64_t 
     const int rows_per_block = tpr >= kBlockThreads ? 1 : kBlockThreads / tpr;
     const int threads = tpr * rows_per_block;
     const int64_t blocks = (M_pad + rows_per_block - 1) / rows_per_block;
-    const size_t smem = static_cast<size_t>(rows_per_block) * (tpr / 32) * 2 * sizeof(float);
+    const size_t smem = static_cast<size_t>(rows_per_block) * (tpr / 32) * sizeof(uint32_t);
     fp8_quant_rows_vec<<<static_cast<unsigned>(blocks), threads, smem, s>>>(
         static_cast<const __nv_bfloat16 *>(x), M, K, ldx, static_cast<uint8_t *>(codes), scales,
         M_pad, tpr, amax_in, amax_out);
