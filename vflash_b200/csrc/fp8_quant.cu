@@ -12,8 +12,8 @@
 // scale is 1 and NaN inputs stay NaN codes.
 //
 // Layout: one group of TPR threads (a multiple of 32) owns one row and keeps
-// the whole row in registers as packed bf16 (4 x 16-byte loads per thread, so
-// K <= 32768 needs at most 1024 threads); the row maximum is taken on the bf16
+// the whole row in registers as packed bf16 (8 x 16-byte loads per thread, so
+// K <= 32768 needs at most 512 threads); the row maximum is taken on the bf16
 // bit patterns (packed 16-bit max), reduced with redux.sync and, across the
 // row's warps, through shared memory.  Each byte of
 // x is read once and each code written once: 3 bytes of traffic per element.
@@ -24,8 +24,9 @@
 namespace vfb {
 namespace {
 
-constexpr int kVecPerThread = 4;     // 16-byte vectors (8 bf16) per thread
-constexpr int kBlockThreads = 256;
+constexpr int kVecPerThread = 8;     // 16-byte vectors (8 bf16) per thread: 128 bytes in flight
+constexpr int kBlockThreads = 128;   // measured best with 8 vectors per thread (K = 4096 and 16384)
+constexpr int kScalarThreads = 256;  // unaligned rows: one block per row
 
 __device__ __forceinline__ float row_scale(float amax, bool nan) {
   if (nan || !(amax > 0.0f)) return 1.0f;
@@ -104,7 +105,7 @@ __device__ __forceinline__ uint32_t abs_bits_max8(const uint4 &v, uint32_t acc) 
 // amax_in != NULL: use these row maxima instead of reducing (a row split over
 //   several ranks quantised with the full row's scale);
 // amax_out != NULL: only write the row maxima (NaN for a row with a NaN).
-__global__ void __launch_bounds__(1024, 1) fp8_quant_rows_vec(
+__global__ void __launch_bounds__(512) fp8_quant_rows_vec(
     const __nv_bfloat16 *__restrict__ x, int64_t M, int64_t K, int64_t ldx,
     uint8_t *__restrict__ codes, float *__restrict__ scales, int64_t M_pad, int tpr,
     const float *__restrict__ amax_in, float *__restrict__ amax_out) {
@@ -168,11 +169,11 @@ __global__ void __launch_bounds__(1024, 1) fp8_quant_rows_vec(
 
 // Generic path (any K, any alignment): one block per row, two passes over
 // the row (the second from cache).
-__global__ void __launch_bounds__(kBlockThreads) fp8_quant_rows_scalar(
+__global__ void __launch_bounds__(kScalarThreads) fp8_quant_rows_scalar(
     const __nv_bfloat16 *__restrict__ x, int64_t M, int64_t K, int64_t ldx,
     uint8_t *__restrict__ codes, float *__restrict__ scales, int64_t M_pad,
     const float *__restrict__ amax_in, float *__restrict__ amax_out) {
-  __shared__ float red[kBlockThreads / 32 * 2];
+  __shared__ float red[kScalarThreads / 32 * 2];
   const int64_t row = blockIdx.x;
   const bool live = row < M;
   float amax = 0.0f;
@@ -248,7 +249,7 @@ int launch_quant(const char *what, const void *x, int64_t M, int64_t K, int64_t 
         static_cast<const __nv_bfloat16 *>(x), M, K, ldx, static_cast<uint8_t *>(codes), scales,
         M_pad, tpr, amax_in, amax_out);
   } else {
-    fp8_quant_rows_scalar<<<static_cast<unsigned>(M_pad), kBlockThreads, 0, s>>>(
+    fp8_quant_rows_scalar<<<static_cast<unsigned>(M_pad), kScalarThreads, 0, s>>>(
         static_cast<const __nv_bfloat16 *>(x), M, K, ldx, static_cast<uint8_t *>(codes), scales,
         M_pad, amax_in, amax_out);
   }
