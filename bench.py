@@ -14,10 +14,11 @@ region; multi-GPU value uses the max over ranks.  Tokens are independent, so
 at N GPUs every rank runs its own full workload with replicated weights
 (weak scaling, no collective on the data path).
 
-``e2e`` runs the same step through the public drop-in API
-(``RowFP8Execution("w8a8").qkv_linear``) with the input copied from pinned
+``e2e`` runs the same step through the public API with the input in pinned
 host memory and Q, K, V copied back to pinned host memory inside the timed
-region.
+region: ``HostRowPipeline`` around ``RowFP8Execution("w8a8").qkv_linear``
+(row chunks whose copies in, compute and copies out overlap); the
+``unpipelined`` entry is one whole-tensor copy in, the linear, one copy out.
 
 ``stack_c4`` is BASELINE config 4 on every rank: 48 blocks of FP8 linears
 over M=65520 tokens sharded across the ranks, weights streamed from the
@@ -165,32 +166,47 @@ def synthetic_workload(device: torch.device, rank: int, M: int):
 
 
 def run_e2e(args, M, x_host, w_codes, w_scales, bias, device, stream, barrier):
-    """Same step through the public drop-in API, host (pinned) buffers in and out."""
+    """Same step through the public API, pinned host buffers in and out.
+
+    Returns (ms, steps) for the row-chunked pipeline (``HostRowPipeline``:
+    host->device copy, compute and device->host copy of successive row chunks
+    overlap on three streams) and for one whole-tensor copy -> qkv_linear ->
+    copy back.
+    """
     from vflash_b200.native.h3_fp8_linear import RowFP8Execution
+    from vflash_b200.native.h3_host_stream import HostRowPipeline
 
     execution = RowFP8Execution("w8a8", activation_quantizer="triton")
     x_pinned = x_host.pin_memory()
     x_dev = torch.empty(x_host.shape, dtype=x_host.dtype, device=device)
     head_dim = K // HEADS
     outs_host = [torch.empty((M, HEADS, head_dim), dtype=torch.bfloat16).pin_memory() for _ in range(3)]
+    pipeline = HostRowPipeline(lambda xd: execution.qkv_linear(xd, w_codes, w_scales, bias), device,
+                               chunk_rows=args.e2e_chunk_rows)
 
-    def e2e_step():
+    def whole_step():
         x_dev.copy_(x_pinned, non_blocking=True)
         q, k, v = execution.qkv_linear(x_dev, w_codes, w_scales, bias)
         for host, plane in zip(outs_host, (q, k, v)):
             host.copy_(plane.view(M, HEADS, head_dim), non_blocking=True)
 
-    for _ in range(args.warmup):
-        e2e_step()
-    barrier()
+    def pipelined_step():
+        pipeline(x_pinned, outs_host)
+
     steps = max(3, min(args.steps, 10))
-    s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    s0.record(stream)
-    for _ in range(steps):
-        e2e_step()
-    s1.record(stream)
-    barrier()
-    return s0.elapsed_time(s1), steps
+    results = []
+    for fn in (pipelined_step, whole_step):
+        for _ in range(args.warmup):
+            fn()
+        barrier()
+        s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s0.record(stream)
+        for _ in range(steps):
+            fn()
+        s1.record(stream)
+        barrier()
+        results.append((s0.elapsed_time(s1), steps))
+    return results
 
 
 def run_gpu(args) -> None:
@@ -260,10 +276,12 @@ def run_gpu(args) -> None:
     total_ms = max_over_ranks(sum(step_ms))
     status = _lib.device_status(clear=True)
 
-    e2e_ms, e2e_steps = float("nan"), 0
+    e2e_ms, e2e_steps, whole_ms, whole_steps = float("nan"), 0, float("nan"), 0
     if not args.no_e2e:
-        e2e_ms, e2e_steps = run_e2e(args, M, x_host, w_codes, w_scales, bias, device, stream, barrier)
+        (e2e_ms, e2e_steps), (whole_ms, whole_steps) = run_e2e(args, M, x_host, w_codes, w_scales, bias,
+                                                               device, stream, barrier)
         e2e_ms = max_over_ranks(e2e_ms)
+        whole_ms = max_over_ranks(whole_ms)
 
     stack = None
     if not args.no_stack:
@@ -332,8 +350,13 @@ def run_gpu(args) -> None:
         line["e2e"] = {"value": round(world * e2e_steps * flop_per_step / (e2e_ms * 1e-3) / 1e12, 2),
                        "unit": "TFLOP/s", "h2d_bytes_per_step": M * K * 2,
                        "d2h_bytes_per_step": M * N_QKV * 2,
-                       "api": "RowFP8Execution('w8a8').qkv_linear, pinned host in/out",
-                       "ms_per_step": round(e2e_ms / e2e_steps, 3)}
+                       "api": "HostRowPipeline(RowFP8Execution('w8a8').qkv_linear), pinned host in/out, "
+                              f"{args.e2e_chunk_rows}-row chunks overlapping H2D, compute and D2H",
+                       "ms_per_step": round(e2e_ms / e2e_steps, 3),
+                       "unpipelined": {
+                           "value": round(world * whole_steps * flop_per_step / (whole_ms * 1e-3) / 1e12, 2),
+                           "ms_per_step": round(whole_ms / whole_steps, 3),
+                           "api": "one copy in, RowFP8Execution('w8a8').qkv_linear, one copy out"}}
     if stack is not None:
         line["stack_c4"] = stack
     if library is not None:
@@ -677,6 +700,7 @@ def main() -> None:
     parser.add_argument("--no-library-probe", action="store_true")
     parser.add_argument("--no-e2e", action="store_true")
     parser.add_argument("--no-stack", action="store_true", help="skip the config 4 block stack")
+    parser.add_argument("--e2e-chunk-rows", type=int, default=4096)
     parser.add_argument("--stack-blocks", type=int, default=STACK_BLOCKS)
     parser.add_argument("--stack-steps", type=int, default=2)
     parser.add_argument("--no-other-configs", action="store_true",

@@ -147,3 +147,17 @@ def test_injected_failure_is_seen_by_the_peer_before_its_next_collective(tmp_pat
     mp.spawn(_failure_worker, args=(world, _free_port(), str(tmp_path / "f")), nprocs=world)
     assert torch.load(tmp_path / "f.1")["outcome"] == "raised"
     assert torch.load(tmp_path / "f.0")["outcome"] == "refused"
+
+
+def test_host_pipeline_chunk_plan_covers_rows_in_aligned_chunks():
+    from vflash_b200.native.h3_host_stream import plan_chunks
+
+    assert plan_chunks(0, 4096) == []
+    assert plan_chunks(100, 4096) == [(0, 100)]
+    assert plan_chunks(32760, 4096) == [(i, min(32760, i + 4096)) for i in range(0, 32760, 4096)]
+    chunks = plan_chunks(10001, 1000)  # rounded down to a multiple of 16
+    assert chunks[0] == (0, 992) and chunks[-1][1] == 10001
+    assert all(b - a == 992 for a, b in chunks[:-1])
+    assert plan_chunks(40, 5) == [(0, 16), (16, 32), (32, 40)]
+    with pytest.raises(ValueError):
+        plan_chunks(10, 0)
