@@ -117,3 +117,11 @@ def test_constructor_validation():
         RowFP8Execution(activation_quantizer="numpy")
     with pytest.raises(ValueError, match="boolean"):
         RowFP8Execution(fast_accum=1)
+
+
+def test_known_answer_ones_times_ones_is_sixteen():
+    # reference tests/test_fp8_loaders.py:31-47: ones e4m3 codes, unit row scales, K = 16
+    codes = torch.ones(4, 16).to(torch.float8_e4m3fn)
+    scales = torch.ones(4, 1)
+    out = RowFP8Execution("weight-only").linear(torch.ones(2, 16), codes, scales)
+    assert torch.equal(out, torch.full((2, 4), 16.0))

@@ -149,3 +149,15 @@ def test_device_status_stays_clean():
     x, w, ws, b = make_case(m, n, k, seed=29)
     plain(x, w, ws, b)
     assert _lib.device_status(clear=True) == _lib.VFB_OK
+
+
+@pytest.mark.parametrize("k", [16, 32, 4096])
+def test_known_answer_ones_times_ones_is_k(k):
+    # reference tests/test_fp8_loaders.py:31-47 (K = 16 there), on the W8A8 path
+    from vflash_b200.native.h3_fp8_linear import RowFP8Execution
+
+    codes = torch.ones(32, k).to(torch.float8_e4m3fn).to(DEV)  # the GEMM needs N % 32 == 0
+    scales = torch.ones(32, 1, device=DEV)
+    x = torch.ones(2, k, dtype=torch.bfloat16, device=DEV)
+    out = RowFP8Execution("w8a8").linear(x, codes, scales)
+    assert torch.equal(out, torch.full((2, 32), float(k), dtype=torch.bfloat16, device=DEV))

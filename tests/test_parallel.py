@@ -161,3 +161,60 @@ def test_host_pipeline_chunk_plan_covers_rows_in_aligned_chunks():
     assert plan_chunks(40, 5) == [(0, 16), (16, 32), (32, 40)]
     with pytest.raises(ValueError):
         plan_chunks(10, 0)
+
+
+# ---------------------------------------------------------------------------
+# low-rank adapters under tensor parallelism
+# (reference tests/test_native_parallel.py:54-89, float64, 2 and 4 ranks)
+# ---------------------------------------------------------------------------
+def _adapter(inputs, outputs, seed):
+    gen = torch.Generator().manual_seed(seed)
+    return par.LowRankAdapter(torch.randn(2, inputs, generator=gen, dtype=torch.float64),
+                              torch.randn(outputs, 2, generator=gen, dtype=torch.float64), 0.0625)
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_adapter_shards_preserve_branch_order(world):
+    adapters = {"qkv": tuple(_adapter(8, 8, 10 + b) for b in range(3)),
+                "attention_out": _adapter(8, 8, 20), "ffn_in": _adapter(8, 24, 21),
+                "ffn_out": _adapter(12, 8, 22)}
+    shards = [par.shard_block_adapters(adapters, r, world) for r in range(world)]
+    for b in range(3):
+        assert torch.equal(torch.cat([s["qkv"][b].up for s in shards]), adapters["qkv"][b].up)
+        assert all(torch.equal(s["qkv"][b].down, adapters["qkv"][b].down) for s in shards)
+    packed = torch.cat([s["ffn_in"].up.reshape(2, -1, 2) for s in shards], dim=1)
+    assert torch.equal(packed.reshape(-1, 2), adapters["ffn_in"].up)
+    for name in ("attention_out", "ffn_out"):
+        assert torch.equal(torch.cat([s[name].down for s in shards], dim=1), adapters[name].down)
+        assert all(torch.equal(s[name].up, adapters[name].up) for s in shards)
+    assert par.shard_adapter(None, 0, world, mode="row") is None
+
+
+def _adapter_worker(rank, world, port, result_path):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        inputs, outputs, total = 12, 8, 7
+        gen = torch.Generator().manual_seed(18)
+        weight = torch.randn(outputs, inputs, generator=gen, dtype=torch.float64)
+        adapter = _adapter(inputs, outputs, 19)
+        states = torch.arange(inputs * total, dtype=torch.float64).reshape(total, inputs) / 32
+        x_cols = states.chunk(world, dim=1)[rank].contiguous()
+        w_shard = par.split_matrix(weight, rank, world, axis=1)
+        a_shard = par.shard_adapter(adapter, rank, world, mode="row")
+        base, update = par.row_parallel_adapter_linear(
+            x_cols, w_shard, lambda x, w, _b: x @ w.T, a_shard)
+        actual = base + update * adapter.scaling
+        expected = states @ weight.T + ((states @ adapter.down.T) @ adapter.up.T) * adapter.scaling
+        mine, valid = par.partition_rows(expected, rank, world)
+        torch.testing.assert_close(actual[:valid], mine[:valid], rtol=1e-12, atol=1e-12)
+        torch.save({"ok": True}, f"{result_path}.{rank}")
+    finally:
+        dist.destroy_process_group()
+
+
+def test_row_parallel_adapter_reduces_down_before_up_on_gloo(tmp_path):
+    world = 2
+    mp.spawn(_adapter_worker, args=(world, _free_port(), str(tmp_path / "a")), nprocs=world)
+    assert all(torch.load(tmp_path / f"a.{r}")["ok"] for r in range(world))

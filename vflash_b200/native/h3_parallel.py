@@ -12,7 +12,8 @@ in one process to ``world`` ranks, one process per GPU over NCCL:
   ``shard_h3_block``/``_split_matrix`` h3_parallel.py:34-88 and
   ``_TensorBlock`` h3_parallel.py:220-250): QKV and ffn_in are split by output
   rows with the Q/K/V (3) and value/gate (2) branch order kept, attention_out
-  and ffn_out by input features.  A row-parallel linear produces bf16 partial
+  and ffn_out by input features; their low-rank adapters split ``up`` with
+  column projections and ``down`` with row projections.  A row-parallel linear produces bf16 partial
   sums on every rank, as the reference's BF16 TP block does; instead of the
   reference's all-reduce they are combined with one NCCL reduce-scatter over
   the token rows, which leaves the output token-sharded, and the bias /
@@ -89,6 +90,46 @@ def shard_block(weights: dict[str, FP8Weight], rank: int, world: int) -> dict[st
     }
 
 
+@dataclass(frozen=True)
+class LowRankAdapter:
+    """Low-rank residual branch ``x @ down.T @ up.T * scaling``: down ``[r, K]``, up ``[N, r]``."""
+
+    down: torch.Tensor
+    up: torch.Tensor
+    scaling: float
+
+
+def shard_adapter(adapter: LowRankAdapter | None, rank: int, world: int, *, mode: str,
+                  parts: int = 1) -> LowRankAdapter | None:
+    """Shard an adapter with its projection (h3_parallel.py:70-80 generalised to ``world`` ranks).
+
+    Column-parallel projections split ``up`` by output rows (keeping the
+    value/gate branch order for ``parts=2``) and keep ``down`` whole;
+    row-parallel projections split ``down`` by input features and keep ``up``
+    whole, so the rank-r down products are summed before the replicated up.
+    """
+    if adapter is None:
+        return None
+    if mode == "column":
+        return LowRankAdapter(adapter.down, split_matrix(adapter.up, rank, world, axis=0, parts=parts),
+                              adapter.scaling)
+    if mode == "row":
+        if parts != 1:
+            raise ParallelError("row shards have no branches")
+        return LowRankAdapter(split_matrix(adapter.down, rank, world, axis=1), adapter.up, adapter.scaling)
+    raise ParallelError("shard mode must be 'column' or 'row'")
+
+
+def shard_block_adapters(adapters: dict[str, Any], rank: int, world: int) -> dict[str, Any]:
+    """Shard one block's six adapters: three QKV branches, attention_out, ffn_in (packed), ffn_out."""
+    return {
+        "qkv": tuple(shard_adapter(a, rank, world, mode="column") for a in adapters.get("qkv", ())),
+        "attention_out": shard_adapter(adapters.get("attention_out"), rank, world, mode="row"),
+        "ffn_in": shard_adapter(adapters.get("ffn_in"), rank, world, mode="column", parts=2),
+        "ffn_out": shard_adapter(adapters.get("ffn_out"), rank, world, mode="row"),
+    }
+
+
 # ---------------------------------------------------------------------------
 # token sharding
 # ---------------------------------------------------------------------------
@@ -161,6 +202,35 @@ def row_parallel_linear(states_cols: torch.Tensor, weight_shard: FP8Weight, line
     out = torch.empty((rows, partial.shape[1]), dtype=partial.dtype, device=partial.device)
     dist.reduce_scatter_tensor(out, partial.contiguous(), op=dist.ReduceOp.SUM, group=group)
     return out if epilogue is None else epilogue(out)
+
+
+def row_parallel_adapter_linear(states_cols: torch.Tensor, weight_shard, linear: Linear,
+                                adapter: LowRankAdapter, group=None) -> tuple[torch.Tensor, torch.Tensor]:
+    """Row-parallel linear with its low-rank branch: returns this rank's (base, update) rows.
+
+    As the reference's tensor-parallel block (``_TensorBlock``,
+    h3_parallel.py:220-250), the rank-r down products are summed across ranks
+    before the replicated up projection; here the base partials and the down
+    partials travel in ONE reduce-scatter over token rows (a ``[rows, N + r]``
+    buffer), then ``update = down_sum @ up.T`` is formed for the local rows.
+    The caller applies ``triton_strict_bf16_adapter_gate_residual(base,
+    update, residual, gate, scaling=adapter.scaling)`` to its token rows.
+    """
+    import torch.distributed as dist
+
+    world = dist.get_world_size(group)
+    total = states_cols.shape[0]
+    rows = shard_rows_count(total, world)
+    base = linear(states_cols, weight_shard, None)
+    down = torch.nn.functional.linear(states_cols, adapter.down).to(base.dtype)
+    n = base.shape[1]
+    both = torch.cat([base, down], dim=1)
+    if rows * world != total:
+        both = torch.cat([both, both.new_zeros((rows * world - total, both.shape[1]))])
+    local = torch.empty((rows, both.shape[1]), dtype=both.dtype, device=both.device)
+    dist.reduce_scatter_tensor(local, both.contiguous(), op=dist.ReduceOp.SUM, group=group)
+    update = torch.nn.functional.linear(local[:, n:], adapter.up)
+    return local[:, :n], update
 
 
 def row_parallel_fp8_linear(states_cols: torch.Tensor, weight_shard: FP8Weight, group=None,
