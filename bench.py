@@ -292,7 +292,8 @@ def run_gpu(args) -> None:
         library = library_fp8_probe(device)
     other = None
     if rank == 0 and not args.no_other_configs:
-        other = other_configs(device, flush, stream)
+        other = other_configs(device, flush, stream,
+                              0.0 if args.no_cpu_baseline else min(args.cpu_seconds, 10.0))
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu = cpu_baseline(x_host, w_codes.cpu(), w_scales.cpu(), bias.cpu(), args.cpu_seconds)
@@ -368,7 +369,7 @@ def run_gpu(args) -> None:
     print(json.dumps(line), flush=True)
 
 
-def _timed(fn, flush, stream, reps: int = 5, warmup: int = 3) -> list[float]:
+def _timed(fn, flush, stream, reps: int = 50, warmup: int = 10) -> list[float]:
     """Per-call milliseconds of ``fn`` (CUDA events, L2 flushed before each call)."""
     for _ in range(warmup):
         fn()
@@ -384,8 +385,33 @@ def _timed(fn, flush, stream, reps: int = 5, warmup: int = 3) -> list[float]:
     return [a.elapsed_time(b) for a, b in times]
 
 
-def other_configs(device, flush, stream) -> dict:
-    """BASELINE configs 0, 2 and 3 on one GPU (seeded synthetic inputs, same timing rules)."""
+def nvfp4_cpu_baseline(ac, asf, wp, wsc, alpha, seconds: float) -> dict:
+    """NVFP4 has no reference CPU path: the oracle's dequantise-then-fp32-matmul on a row sample."""
+    from oracle.nvfp4 import dequant_matmul_f32
+
+    rows, k = 1024, ac.shape[1] * 2
+    kt = -(-(k // 16) // 4)
+    a = ac[:rows].cpu().numpy()
+    a_sf = asf.reshape(-1)[: rows // 128 * kt * 512].cpu().numpy()
+    w = wp.cpu().numpy()
+    w_sf = wsc.reshape(-1).cpu().numpy()
+    al = float(alpha)
+    reps, elapsed = 0, 0.0
+    while elapsed < seconds or reps < 1:
+        t0 = time.perf_counter()
+        dequant_matmul_f32(a, a_sf, w, w_sf, al)
+        elapsed += time.perf_counter() - t0
+        reps += 1
+    flop = 2.0 * rows * w.shape[0] * k * reps
+    return {"value": round(flop / elapsed / 1e12, 4), "unit": "TFLOP/s", "cores": cpu_threads(),
+            "kind": "port", "sample": f"{reps} x oracle dequantise (e2m1 x e4m3 block scales) + fp32 "
+                                      f"matmul on {rows} rows, N={w.shape[0]}, K={k}: {elapsed:.1f} s "
+                                      "(the reference has no NVFP4 CPU path)"}
+
+
+def other_configs(device, flush, stream, cpu_seconds: float = 0.0) -> dict:
+    """BASELINE configs 0, 2 and 3 on one GPU: seeded synthetic inputs, 10 warm-up calls, median of 50
+    timed calls with L2 flushed before each."""
     from vflash_b200 import _lib
     from vflash_b200.kernels import Epilogue, fp8_gemm, nvfp4_gemm, nvfp4_quantize, quantize_fp8_rows
 
@@ -449,7 +475,24 @@ def other_configs(device, flush, stream) -> dict:
                  "down GEMM + residual epilogue (four launches; intermediate round-trips HBM)",
          "last_step_ms": {"quant_x": round(parts[0], 4), "up_gemm_gelu": round(parts[1], 4),
                           "requant_mid": round(parts[2], 4), "down_gemm_residual": round(parts[3], 4)}})
-    del x, up, ups, down, downs
+    del up, ups
+
+    # c2 SwiGLU variant (the reference model's packed FFN input [2F, H]) through
+    # the public fused entry point RowFP8Execution.ffn
+    from vflash_b200.native.h3_fp8_linear import RowFP8Execution
+
+    packed, packeds = quantize_fp8_rows(seeded(2 * f, h, 2022, std=0.02), pad_to=1)
+    execution = RowFP8Execution("w8a8")
+
+    def c2_swiglu():
+        execution.ffn(x, packed, packeds, down, downs, activation="swiglu", residual=x)
+
+    ms = _timed(c2_swiglu, flush, stream)
+    out["c2_fp8_ffn_swiglu"] = summary(
+        ms, 2.0 * m * (2 * f) * h + 2.0 * m * f * h, fp8_peak,
+        {"step": "RowFP8Execution.ffn(activation='swiglu'): quant X, packed up GEMM [2F,H] with "
+                 "value * bf16(silu(gate)) epilogue, requant, down GEMM + residual"})
+    del x, packed, packeds, down, downs
 
     # c3: NVFP4 linear, M = 32760, K = 4096, N in {4096, 16384}
     x = seeded(32760, 4096, 1003)
@@ -460,22 +503,24 @@ def other_configs(device, flush, stream) -> dict:
         wp, wsc = nvfp4_quantize(w, gsf_w)
         wsc = wsc.view(n, 4096 // 16)
         alpha = ((1.0 / gsf_w) / gsf_x).to(torch.float32)
-        ev2 = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
 
         def c3():
-            ev2[0].record(stream)
             ac, asf = nvfp4_quantize(x, gsf_x)
-            ev2[1].record(stream)
             nvfp4_gemm(ac, asf, wp, wsc, alpha)
-            ev2[2].record(stream)
 
         ms = _timed(c3, flush, stream)
-        gemm_ms = ev2[1].elapsed_time(ev2[2])
+        ac0, asf0 = nvfp4_quantize(x, gsf_x)
+        gemm_ms = statistics.median(_timed(lambda: nvfp4_gemm(ac0, asf0, wp, wsc, alpha), flush, stream))
+        del ac0, asf0
         flop = 2.0 * 32760 * n * 4096
         out[f"c3_nvfp4_n{n}"] = summary(ms, flop, fp4_peak, {
             "step": "NVFP4 quantiser + block-scaled GEMM",
+            "gemm_only_ms": round(gemm_ms, 4),
             "gemm_only_tflops": round(flop / (gemm_ms * 1e-3) / 1e12, 1),
             "gemm_frac_of_peak": round(flop / (gemm_ms * 1e-3) / 1e12 / fp4_peak, 4)})
+        if n == 4096 and cpu_seconds > 0:
+            ac, asf = nvfp4_quantize(x, gsf_x)
+            out["c3_nvfp4_n4096"]["cpu_baseline"] = nvfp4_cpu_baseline(ac, asf, wp, wsc, alpha, cpu_seconds)
     out["peak_note"] = ("fp8 peak = 2 x measured cuBLAS bf16 burst, fp4 peak = 4 x; nominal dense "
                         "fp8 4.5, fp4 9 PFLOP/s")
     return out
