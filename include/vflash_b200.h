@@ -80,6 +80,27 @@ VFB_API int vfb_fp8_quant_rows_amax(const void *x, int64_t M, int64_t K, int64_t
                                     const float *amax, void *codes, float *scales, int64_t M_pad,
                                     void *stream);
 
+/* RMSNorm + AdaLN modulate + per-token e4m3 quantisation of the result, in
+ * one pass.  Replaces the sequence the reference block runs before its QKV and
+ * FFN-input projections (src/vflash/native/h3_native_denoiser.py:534-541 and
+ * 561-568): _rms_norm (231-243, torch's fused rms_norm: fp32 upcast,
+ * rsqrt(mean(x^2) + eps), (x * rstd) * w rounded once to bf16), then
+ * triton_strict_bf16_modulate (src/vflash/native/h3_fused_ops.py:52-122,
+ * 575-611: bf16(bf16(n * bf16(1 + scale)) + shift)), then the quantiser above
+ * applied to the modulated rows.
+ * x: bf16 [M,K], row stride ldx; norm_weight: bf16 [K] or NULL (no weight);
+ * scale / shift: bf16 [tokens, K] with row strides *_token_stride (0 = one
+ * row for all tokens), row r uses row r % tokens.  Outputs as
+ * vfb_fp8_quant_rows.  Requires K % 8 == 0, 8 <= K <= 32768, 16-byte aligned
+ * rows of x, weight, scale and shift, 8-byte aligned codes, eps >= 0.  rstd
+ * is accumulated in fp32 in this kernel's order and rounded from fp64, so it
+ * may differ from torch's by one fp32 ulp. */
+VFB_API int vfb_fp8_norm_modulate_quant(const void *x, int64_t M, int64_t K, int64_t ldx,
+                                        const void *norm_weight, float eps, const void *scale,
+                                        int64_t scale_token_stride, const void *shift,
+                                        int64_t shift_token_stride, int64_t tokens, void *codes,
+                                        float *scales, int64_t M_pad, void *stream);
+
 /* ---- FP8 row-scaled GEMM with fused epilogues ----------------------------
  * Replaces torch._scaled_mm(codes, weight.t(), scale_a, scale_b.t(),
  * out_dtype=bf16) plus the following bias add
@@ -194,6 +215,14 @@ VFB_API int vfb_ffn_adapter_silu(const void *base, const void *adapter, int64_t 
 VFB_API int vfb_gate_residual(const void *residual, const void *gate, int64_t gate_token_stride,
                               const void *projected, int64_t rows, int64_t tokens,
                               int64_t hidden, void *out, void *stream);
+
+/* triton_strict_bf16_modulate (h3_fused_ops.py:52-122, 575-611):
+ * value [rows, hidden] contiguous (rows = batch * tokens), scale / shift
+ * [tokens, hidden] with row strides scale_token_stride / shift_token_stride:
+ * out = bf16(bf16(value * bf16(1 + scale[r % tokens])) + shift[r % tokens]). */
+VFB_API int vfb_modulate(const void *value, const void *scale, int64_t scale_token_stride,
+                         const void *shift, int64_t shift_token_stride, int64_t rows,
+                         int64_t tokens, int64_t hidden, void *out, void *stream);
 
 /* triton_strict_bf16_adapter_gate_residual (h3_fused_ops.py:342-415, 982-1028):
  * out = bf16(residual + bf16(gate * bf16(base + bf16(adapter * scaling)))). */

@@ -109,3 +109,38 @@ def adapter_gate_residual(base_bits, adapter_bits, residual_bits, gate_bits, sca
     gate = bf16_value(gate_bits)
     adapted = bf16_round(base + bf16_round(adapter * np.float32(scaling)))
     return bf16_bits(residual + bf16_round(gate * adapted))
+
+
+def modulate(value_bits, scale_bits, shift_bits) -> np.ndarray:
+    """``strict_modulate_kernel`` (h3_fused_ops.py:52-122): bf16(bf16(x * bf16(1 + scale)) + shift).
+
+    value [B,S,H] (or [S,H]); scale/shift [S,H] broadcast over the batch.
+    All arithmetic in fp32 with the kernel's three bf16 roundings.
+    """
+    value = bf16_value(value_bits)
+    scale = bf16_value(scale_bits)
+    shift = bf16_value(shift_bits)
+    one_plus = bf16_round((np.float32(1.0) + scale).astype(np.float32))
+    scaled = bf16_round((value * one_plus).astype(np.float32))
+    return bf16_bits((scaled + shift).astype(np.float32))
+
+
+def rms_norm(x_bits, weight_bits, eps: float) -> np.ndarray:
+    """torch ``F.rms_norm`` on bf16 (``_rms_norm``, h3_native_denoiser.py:231-243).
+
+    Follows torch's fused decomposition (fp32 upcast, ``rsqrt(mean(x^2) + eps)``,
+    ``(x * rstd) * w`` in fp32, one rounding to bf16).  The mean of squares is
+    summed in float64 and rounded to fp32, and the reciprocal square root is
+    taken in float64 and rounded to fp32: the ideal values that a GPU
+    reduction approximates to within an fp32 ulp.
+    """
+    x = bf16_value(x_bits).astype(np.float32)
+    k = x.shape[-1]
+    ss = np.sum(x.astype(np.float64) ** 2, axis=-1, keepdims=True)
+    mean = (ss.astype(np.float32) / np.float32(k)).astype(np.float32)
+    mean_eps = (mean + np.float32(eps)).astype(np.float32)
+    rstd = (1.0 / np.sqrt(mean_eps.astype(np.float64))).astype(np.float32)
+    y = (x * rstd).astype(np.float32)
+    if weight_bits is not None:
+        y = (y * bf16_value(weight_bits).astype(np.float32)).astype(np.float32)
+    return bf16_bits(y)

@@ -113,3 +113,37 @@ def test_w8a8_emulation_agrees_with_dequantised_matmul(golden):
     y = fp8.w8a8_reference(a_codes[:33], a_scale[:33], golden["wo_mid_codes"], golden["wo_mid_scales"])
     f32 = fp8.dequant_matmul_f32(a_codes[:33], a_scale[:33], golden["wo_mid_codes"], golden["wo_mid_scales"])
     assert fp8.rel_l2(y, f32) < 5e-3
+
+
+def test_oracle_modulate_matches_eager_torch_composition():
+    # the reference kernel reproduces three eager bf16 TensorIterator kernels
+    import torch
+
+    from oracle import epilogues
+    from tests.helpers import bits_of
+
+    gen = torch.Generator().manual_seed(71)
+    x = torch.randn(2, 5, 64, generator=gen).to(torch.bfloat16)
+    scale = (torch.randn(5, 64, generator=gen) * 0.3).to(torch.bfloat16)
+    shift = (torch.randn(5, 64, generator=gen) * 0.3).to(torch.bfloat16)
+    eager = x * (1.0 + scale) + shift
+    got = epilogues.modulate(bits_of(x), bits_of(scale), bits_of(shift))
+    np.testing.assert_array_equal(got, bits_of(eager))
+
+
+def test_oracle_rms_norm_matches_torch_cpu_within_one_ulp():
+    import torch
+
+    from oracle import epilogues
+    from tests.helpers import bits_of
+
+    gen = torch.Generator().manual_seed(72)
+    x = (torch.randn(33, 4096, generator=gen) * 3).to(torch.bfloat16)
+    w = (1 + torch.randn(4096, generator=gen) * 0.1).to(torch.bfloat16)
+    ref = torch.nn.functional.rms_norm(x, (4096,), w, 1e-6)
+    got = fp8.bf16_value(epilogues.rms_norm(bits_of(x), bits_of(w), 1e-6))
+    want = ref.float().numpy()
+    diff = np.abs(got - want)
+    ulp = np.abs(want) * 2.0 ** -7
+    assert (diff <= ulp).all()
+    assert (diff == 0).mean() > 0.99

@@ -68,6 +68,11 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         ctypes.c_int,
         [_vp, _c_int64, _c_int64, _c_int64, _vp, _vp, _vp, _c_int64, _vp],
     ),
+    "vfb_fp8_norm_modulate_quant": (
+        ctypes.c_int,
+        [_vp, _c_int64, _c_int64, _c_int64, _vp, ctypes.c_float, _vp, _c_int64, _vp, _c_int64, _c_int64,
+         _vp, _vp, _c_int64, _vp],
+    ),
     "vfb_fp8_gemm": (
         ctypes.c_int,
         [_vp, _c_int64, _vp, _vp, _c_int64, _vp, _c_int64, _c_int64, _c_int64,
@@ -83,6 +88,8 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         ctypes.c_int, [_vp, _vp, _c_int64, _c_int64, ctypes.c_float, _vp, _c_int64, _vp]),
     "vfb_gate_residual": (
         ctypes.c_int, [_vp, _vp, _c_int64, _vp, _c_int64, _c_int64, _c_int64, _vp, _vp]),
+    "vfb_modulate": (
+        ctypes.c_int, [_vp, _vp, _c_int64, _vp, _c_int64, _c_int64, _c_int64, _c_int64, _vp, _vp]),
     "vfb_adapter_gate_residual": (
         ctypes.c_int,
         [_vp, _vp, _vp, _vp, _c_int64, _c_int64, _c_int64, _c_int64, ctypes.c_float, _vp, _vp]),

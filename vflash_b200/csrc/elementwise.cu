@@ -9,6 +9,7 @@
 //                         out = bf16(v * bf16(silu(g)))                  (254-284)
 //   adapter_merge         out = bf16(base + bf16(a * s_branch))          (298-339)
 //   adapter_gate_residual out = bf16(r + bf16(gate * bf16(base + bf16(a * s)))) (342-415)
+//   modulate              out = bf16(bf16(x * bf16(1 + scale)) + shift)  (52-122, 575-611)
 // Work is split into 8-element groups along the contiguous last dimension;
 // when every pointer and row stride allows, a group is one 16-byte load or
 // store, otherwise the same kernel runs with scalar accesses.  Offsets are
@@ -132,6 +133,30 @@ __global__ void __launch_bounds__(kThreads) gate_residual_kernel(
 #pragma unroll
     for (int j = 0; j < 8; ++j) r.v[j] = r.v[j] + bf16r(g.v[j] * p.v[j]);
     r.store(out + off);
+  }
+}
+
+// value [rows, hidden] contiguous; scale / shift [tokens, hidden] with row
+// strides scale_ts / shift_ts (0 broadcasts one row) and unit column stride.
+template <bool VEC>
+__global__ void __launch_bounds__(kThreads) modulate_kernel(
+    const __nv_bfloat16 *value, const __nv_bfloat16 *scale, int64_t scale_ts,
+    const __nv_bfloat16 *shift, int64_t shift_ts, int64_t rows, int64_t tokens, int64_t hidden,
+    __nv_bfloat16 *out) {
+  const int64_t gpr = hidden / 8;
+  const int64_t total = rows * gpr;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const RowIndex ix = split(i, gpr);
+    const int64_t off = ix.row * hidden + ix.col;
+    const int64_t token = ix.row % tokens;
+    Group<VEC> x, sc, sh;
+    x.load(value + off);
+    sc.load(scale + token * scale_ts + ix.col);
+    sh.load(shift + token * shift_ts + ix.col);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) x.v[j] = bf16r(x.v[j] * bf16r(1.0f + sc.v[j])) + sh.v[j];
+    x.store(out + off);
   }
 }
 
@@ -362,4 +387,28 @@ extern "C" int vfb_qkv_direct_merge(void *base, const void *adapter_q, const voi
     qkv_direct_merge_kernel<false><<<grid, kThreads, 0, s>>>(b, q, k, v, rows, width, scalings[0],
                                                              scalings[1], scalings[2]);
   return finish("vfb_qkv_direct_merge");
+}
+
+extern "C" int vfb_modulate(const void *value, const void *scale, int64_t scale_token_stride,
+                            const void *shift, int64_t shift_token_stride, int64_t rows, int64_t tokens,
+                            int64_t hidden, void *out, void *stream) {
+  using namespace vfb;
+  if (rows < 0 || tokens <= 0 || hidden <= 0 || hidden % 8 || scale_token_stride < 0 ||
+      shift_token_stride < 0 || !value || !scale || !shift || !out)
+    return set_error(VFB_EINVAL, "vfb_modulate: need hidden %% 8 == 0, tokens > 0, strides >= 0");
+  if (rows == 0) return VFB_OK;
+  const int grid = grid_for(rows * (hidden / 8));
+  if (grid < 0) return VFB_EDEVICE;
+  const auto *x = static_cast<const __nv_bfloat16 *>(value);
+  const auto *sc = static_cast<const __nv_bfloat16 *>(scale);
+  const auto *sh = static_cast<const __nv_bfloat16 *>(shift);
+  auto *o = static_cast<__nv_bfloat16 *>(out);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (a16(x) && a16(sc) && a16(sh) && a16(o) && scale_token_stride % 8 == 0 && shift_token_stride % 8 == 0)
+    modulate_kernel<true><<<grid, kThreads, 0, s>>>(x, sc, scale_token_stride, sh, shift_token_stride, rows,
+                                                    tokens, hidden, o);
+  else
+    modulate_kernel<false><<<grid, kThreads, 0, s>>>(x, sc, scale_token_stride, sh, shift_token_stride, rows,
+                                                     tokens, hidden, o);
+  return finish("vfb_modulate");
 }

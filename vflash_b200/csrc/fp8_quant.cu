@@ -223,6 +223,138 @@ __global__ void __launch_bounds__(kScalarThreads) fp8_quant_rows_scalar(
   if (threadIdx.x == 0) scales[row] = scale;
 }
 
+// ---------------------------------------------------------------------------
+// RMSNorm + AdaLN modulate + per-token e4m3 quantisation in one pass.
+//
+// For each token row x (bf16, K values), as the reference block computes it
+// before its QKV and FFN-input projections (src/vflash/native/
+// h3_native_denoiser.py:534-541 and 561-568):
+//   rstd = rsqrt(mean(x^2) + eps)                 fp32 (torch's fused rms_norm:
+//                                                 fp32 upcast, mean, rsqrt)
+//   n    = bf16((x * rstd) * w)                   one rounding (fp32 products)
+//   m    = bf16(bf16(n * bf16(1 + scale)) + shift) strict-BF16 modulate
+//                                                 (h3_fused_ops.py:52-122)
+//   codes, row scale = the per-token quantisation of m (as above)
+// scale / shift are [tokens, K] rows selected by row % tokens.  The sum of
+// squares is accumulated in fp32 in this kernel's order and the reciprocal
+// square root is correctly rounded (computed in fp64), so rstd can differ
+// from another implementation's by an ulp of fp32; n, m and the codes then
+// differ from it only where that ulp crosses a bf16 rounding boundary.
+// x stays in registers between the two row reductions (sum of squares, then
+// max |m|): 2 bytes read per element of x, scale and shift each, 1 written.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ float block_row_sum(float v, uint32_t *red_u32, int r_local, int t,
+                                               int warps_per_row) {
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+  if (warps_per_row > 1) {
+    float *row_red = reinterpret_cast<float *>(red_u32) + r_local * warps_per_row;
+    if ((t & 31) == 0) row_red[t / 32] = v;
+    __syncthreads();
+    v = 0.0f;
+    for (int w = 0; w < warps_per_row; ++w) v += row_red[w];
+    __syncthreads();  // the buffer is reused by the maximum that follows
+  }
+  return v;
+}
+
+__global__ void __launch_bounds__(512) fp8_norm_modulate_quant_vec(
+    const __nv_bfloat16 *__restrict__ x, int64_t M, int64_t K, int64_t ldx,
+    const __nv_bfloat16 *__restrict__ norm_w, float eps, const __nv_bfloat16 *__restrict__ mod_scale,
+    int64_t scale_ts, const __nv_bfloat16 *__restrict__ mod_shift, int64_t shift_ts, int64_t tokens,
+    uint8_t *__restrict__ codes, float *__restrict__ scales, int64_t M_pad, int tpr) {
+  extern __shared__ uint32_t red[];
+  const int rows_per_block = blockDim.x / tpr;
+  const int r_local = threadIdx.x / tpr;
+  const int t = threadIdx.x % tpr;
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * rows_per_block + r_local;
+  const int warps_per_row = tpr / 32;
+  const int64_t nvec = K / 8;
+  const bool live = row < M;
+
+  uint4 v[kVecPerThread];
+  float ss = 0.0f;
+  if (live) {
+    const uint4 *src = reinterpret_cast<const uint4 *>(x + row * ldx);
+#pragma unroll
+    for (int i = 0; i < kVecPerThread; ++i) {
+      const int64_t c = static_cast<int64_t>(i) * tpr + t;
+      v[i] = c < nvec ? __ldcs(src + c) : make_uint4(0, 0, 0, 0);
+    }
+#pragma unroll
+    for (int i = 0; i < kVecPerThread; ++i) {
+      const __nv_bfloat162 *h = reinterpret_cast<const __nv_bfloat162 *>(&v[i]);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float2 f = __bfloat1622float2(h[j]);
+        ss = fmaf(f.x, f.x, ss);
+        ss = fmaf(f.y, f.y, ss);
+      }
+    }
+  }
+  ss = block_row_sum(ss, red, r_local, t, warps_per_row);  // block-uniform call
+  uint32_t bits = 0;
+  if (live) {
+    const float mean_eps = __fadd_rn(__fdiv_rn(ss, static_cast<float>(K)), eps);
+    const float rstd = static_cast<float>(1.0 / sqrt(static_cast<double>(mean_eps)));
+    const int64_t token = row % tokens;
+    const uint4 *wq = reinterpret_cast<const uint4 *>(norm_w);
+    const uint4 *scq = reinterpret_cast<const uint4 *>(mod_scale + token * scale_ts);
+    const uint4 *shq = reinterpret_cast<const uint4 *>(mod_shift + token * shift_ts);
+#pragma unroll
+    for (int i = 0; i < kVecPerThread; ++i) {
+      const int64_t c = static_cast<int64_t>(i) * tpr + t;
+      if (c >= nvec) continue;
+      const uint4 wv = norm_w != nullptr ? __ldg(wq + c) : make_uint4(0x3f803f80u, 0x3f803f80u,
+                                                                       0x3f803f80u, 0x3f803f80u);
+      const uint4 scv = __ldg(scq + c);
+      const uint4 shv = __ldg(shq + c);
+      const __nv_bfloat162 *hx = reinterpret_cast<const __nv_bfloat162 *>(&v[i]);
+      const __nv_bfloat162 *hw = reinterpret_cast<const __nv_bfloat162 *>(&wv);
+      const __nv_bfloat162 *hs = reinterpret_cast<const __nv_bfloat162 *>(&scv);
+      const __nv_bfloat162 *hb = reinterpret_cast<const __nv_bfloat162 *>(&shv);
+      uint32_t out[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float2 fx = __bfloat1622float2(hx[j]);
+        const float2 fw = __bfloat1622float2(hw[j]);
+        const float2 fs = __bfloat1622float2(hs[j]);
+        const float2 fb = __bfloat1622float2(hb[j]);
+        const float n0 = bf16r((fx.x * rstd) * fw.x);
+        const float n1 = bf16r((fx.y * rstd) * fw.y);
+        const float m0 = bf16r(n0 * bf16r(1.0f + fs.x)) + fb.x;
+        const float m1 = bf16r(n1 * bf16r(1.0f + fs.y)) + fb.y;
+        out[j] = pack_bf16x2(m0, m1);
+      }
+      v[i] = make_uint4(out[0], out[1], out[2], out[3]);
+      bits = abs_bits_max8(v[i], bits);
+    }
+  }
+  uint32_t m = __reduce_max_sync(0xffffffffu, max(bits & 0xffffu, bits >> 16));
+  if (warps_per_row > 1) {
+    uint32_t *row_red = red + r_local * warps_per_row;
+    if ((t & 31) == 0) row_red[t / 32] = m;
+    __syncthreads();
+    m = 0;
+    for (int w = 0; w < warps_per_row; ++w) m = max(m, row_red[w]);
+  }
+  if (row >= M_pad) return;
+  const float amax = __uint_as_float(m << 16);
+  const float scale = live ? row_scale(amax, m > kBf16Inf) : 1.0f;
+  const bool fast = isfinite(scale);
+  const float recip = fast ? __frcp_rn(scale) : 0.0f;
+  uint2 *dst = reinterpret_cast<uint2 *>(codes + row * K);
+#pragma unroll
+  for (int i = 0; i < kVecPerThread; ++i) {
+    const int64_t c = static_cast<int64_t>(i) * tpr + t;
+    if (c >= nvec) continue;
+    uint2 q = make_uint2(0, 0);
+    if (live) q = fast ? quantize8(v[i], scale, recip) : quantize8_ieee(v[i], scale);
+    dst[c] = q;
+  }
+  if (t == 0) scales[row] = scale;
+}
+
 int launch_quant(const char *what, const void *x, int64_t M, int64_t K, int64_t ldx, void *codes,
                  float *scales, int64_t M_pad, const float *amax_in, float *amax_out,
                  cudaStream_t s) {
@@ -283,4 +415,45 @@ extern "C" int vfb_fp8_quant_rows_amax(const void *x, int64_t M, int64_t K, int6
     return vfb::set_error(VFB_EINVAL, "vfb_fp8_quant_rows_amax: NULL pointer");
   return vfb::launch_quant("vfb_fp8_quant_rows_amax", x, M, K, ldx, codes, scales, M_pad, amax,
                            nullptr, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int vfb_fp8_norm_modulate_quant(const void *x, int64_t M, int64_t K, int64_t ldx,
+                                           const void *norm_weight, float eps, const void *scale,
+                                           int64_t scale_token_stride, const void *shift,
+                                           int64_t shift_token_stride, int64_t tokens, void *codes,
+                                           float *scales, int64_t M_pad, void *stream) {
+  using namespace vfb;
+  if (M < 0 || K < 8 || K > 32768 || K % 8 || ldx < K || M_pad < M || tokens <= 0 ||
+      scale_token_stride < 0 || shift_token_stride < 0 || !(eps >= 0.0f))
+    return set_error(VFB_EINVAL,
+                     "vfb_fp8_norm_modulate_quant: need 8 <= K <= 32768, K %% 8 == 0, ldx >= K, "
+                     "M_pad >= M, tokens > 0, strides >= 0, eps >= 0");
+  if (M_pad == 0) return VFB_OK;
+  if ((M > 0 && (!x || !scale || !shift)) || !codes || !scales)
+    return set_error(VFB_EINVAL, "vfb_fp8_norm_modulate_quant: NULL pointer");
+  const auto al16 = [](const void *p) { return reinterpret_cast<uintptr_t>(p) % 16 == 0; };
+  if (!al16(x) || ldx % 8 || (norm_weight && !al16(norm_weight)) || !al16(scale) || !al16(shift) ||
+      scale_token_stride % 8 || shift_token_stride % 8 || reinterpret_cast<uintptr_t>(codes) % 8)
+    return set_error(VFB_EINVAL,
+                     "vfb_fp8_norm_modulate_quant: rows of x, weight, scale and shift must be "
+                     "16-byte aligned (strides %% 8 == 0) and codes 8-byte aligned");
+  int rc = check_device(nullptr);
+  if (rc != VFB_OK) return rc;
+  const int64_t nvec = K / 8;
+  int tpr = static_cast<int>((nvec + kVecPerThread - 1) / kVecPerThread);
+  tpr = (tpr + 31) / 32 * 32;
+  const int rows_per_block = tpr >= kBlockThreads ? 1 : kBlockThreads / tpr;
+  const int threads = tpr * rows_per_block;
+  const int64_t blocks = (M_pad + rows_per_block - 1) / rows_per_block;
+  const size_t smem = static_cast<size_t>(rows_per_block) * (tpr / 32) * sizeof(uint32_t);
+  fp8_norm_modulate_quant_vec<<<static_cast<unsigned>(blocks), threads, smem,
+                                static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const __nv_bfloat16 *>(x), M, K, ldx, static_cast<const __nv_bfloat16 *>(norm_weight),
+      eps, static_cast<const __nv_bfloat16 *>(scale), scale_token_stride,
+      static_cast<const __nv_bfloat16 *>(shift), shift_token_stride, tokens, static_cast<uint8_t *>(codes),
+      scales, M_pad, tpr);
+  cudaError_t err = cudaGetLastError();
+  if (err != cudaSuccess)
+    return set_error(VFB_ECUDA, "vfb_fp8_norm_modulate_quant launch: %s", cudaGetErrorString(err));
+  return VFB_OK;
 }

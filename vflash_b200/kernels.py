@@ -75,6 +75,46 @@ def quantize_fp8_rows(matrix: torch.Tensor, *, pad_to: int = 16, amax: torch.Ten
     return codes, scales
 
 
+def _check_modifier(t: torch.Tensor, cols: int, device, name: str) -> None:
+    if (t.dtype != BF16 or t.ndim != 2 or t.shape[1] != cols or t.stride(1) != 1 or t.device != device
+            or t.shape[0] < 1):
+        raise KernelInputError(f"{name} must be bf16 [tokens, K] with unit column stride")
+
+
+def quantize_fp8_norm_modulate(matrix: torch.Tensor, norm_weight: torch.Tensor | None, eps: float,
+                               scale: torch.Tensor, shift: torch.Tensor, *, pad_to: int = 16):
+    """RMSNorm + AdaLN modulate + per-token e4m3 quantisation of ``matrix`` in one pass.
+
+    ``matrix`` bf16 ``[M, K]`` (unit column stride), ``norm_weight`` bf16
+    ``[K]`` or None, ``scale``/``shift`` bf16 ``[tokens, K]`` (row ``r`` of
+    ``matrix`` uses row ``r % tokens``; a ``[1, K]`` row serves every token).
+    Returns the codes and scales the quantiser would produce for
+    ``bf16(bf16(rms_norm(x) * bf16(1 + scale)) + shift)``.
+    """
+    rows, cols = _check_fp8_input(matrix)
+    device = matrix.device
+    _check_modifier(scale, cols, device, "modulate scale")
+    _check_modifier(shift, cols, device, "modulate shift")
+    tokens = scale.shape[0]
+    if shift.shape[0] != tokens:
+        raise KernelInputError("modulate scale and shift cover different token counts")
+    if norm_weight is not None and (norm_weight.dtype != BF16 or norm_weight.shape != (cols,)
+                                    or not norm_weight.is_contiguous() or norm_weight.device != device):
+        raise KernelInputError("norm weight must be contiguous bf16 [K]")
+    padded = padded_rows(rows, pad_to)
+    codes = torch.empty((padded, cols), device=device, dtype=FP8)
+    scales = torch.empty((padded, 1), device=device, dtype=torch.float32)
+    lib = _lib.load()
+    with torch.cuda.device(device):
+        rc = lib.vfb_fp8_norm_modulate_quant(
+            matrix.data_ptr() if rows else None, rows, cols, max(matrix.stride(0), cols),
+            None if norm_weight is None else norm_weight.data_ptr(), float(eps), scale.data_ptr(),
+            scale.stride(0) if tokens > 1 else 0, shift.data_ptr(), shift.stride(0) if tokens > 1 else 0,
+            tokens, codes.data_ptr(), scales.data_ptr(), padded, _lib.stream_handle(device))
+    _lib.check(rc, "vfb_fp8_norm_modulate_quant")
+    return codes, scales
+
+
 def row_absmax(matrix: torch.Tensor) -> torch.Tensor:
     """fp32 ``[M]`` row maxima of |x| (NaN for rows holding a NaN), as the quantiser computes them."""
     rows, cols = _check_fp8_input(matrix)

@@ -20,19 +20,41 @@ and error messages, same weight layout (e4m3 ``[N, K]`` + fp32 ``row_scale``
 New fused entry points (``qkv_linear``, ``gelu_linear``, ``swiglu_linear``,
 ``gate_residual_linear``, ``ffn``) run the same GEMM with the elementwise step
 that the H3 block performs next fused into the epilogue; each keeps the BF16
-rounding boundaries of the reference's separate launch.
+rounding boundaries of the reference's separate launch.  ``linear``,
+``qkv_linear``, ``gelu_linear``, ``swiglu_linear`` and ``ffn`` also take a
+``prologue=NormModulate(...)``: the block's RMSNorm + AdaLN modulate
+(src/vflash/native/h3_native_denoiser.py:534-541, 561-568) then runs inside
+the activation quantiser (``vfb_fp8_norm_modulate_quant``) and ``value`` is
+the un-normalised hidden state.
 """
 
 from __future__ import annotations
 
 from collections.abc import Callable
 from contextlib import AbstractContextManager, nullcontext
+from dataclasses import dataclass
 from typing import Any
 
 import torch
 
 from .. import _lib
-from ..kernels import Epilogue, fp8_gemm, quantize_fp8_rows
+from ..kernels import Epilogue, fp8_gemm, quantize_fp8_norm_modulate, quantize_fp8_rows
+
+
+@dataclass(frozen=True)
+class NormModulate:
+    """RMSNorm + AdaLN modulate applied to a linear's input inside its quantiser.
+
+    ``norm_weight`` bf16 ``[K]`` (or None), ``scale``/``shift`` bf16 ``[S, K]``
+    indexed by token (``[1, K]`` for one modulation of every token), ``eps``
+    the norm epsilon.  The quantised activation is that of
+    ``bf16(bf16(rms_norm(value) * bf16(1 + scale)) + shift)``.
+    """
+
+    norm_weight: torch.Tensor | None
+    scale: torch.Tensor
+    shift: torch.Tensor
+    eps: float = 1e-6
 
 
 def _on_sm100(device: torch.device) -> bool:
@@ -103,13 +125,23 @@ class RowFP8Execution:
         if self.observer is not None and sum(self.calls.values()) % 200 == 0:
             self.observer()
 
-    def _quantize(self, matrix):
+    def _quantize(self, matrix, prologue: NormModulate | None = None, shape=None):
         with self.measure("linear.activation_quantize"):
-            return quantize_fp8_rows(matrix, pad_to=16)
+            if prologue is None:
+                return quantize_fp8_rows(matrix, pad_to=16)
+            tokens = prologue.scale.shape[0] if prologue.scale.ndim == 2 else 0
+            if shape is not None and len(shape) >= 3 and tokens not in (1, shape[-2]):
+                raise ValueError("FP8 prologue modulation tokens differ from the activation")
+            if tokens < 1 or matrix.shape[0] % tokens:
+                raise ValueError("FP8 prologue modulation tokens differ from the activation")
+            return quantize_fp8_norm_modulate(matrix, prologue.norm_weight, prologue.eps, prologue.scale,
+                                              prologue.shift, pad_to=16)
 
-    def linear(self, value, weight, scale, bias=None):
+    def linear(self, value, weight, scale, bias=None, *, prologue: NormModulate | None = None):
         self._observe()
         self._validate(value, weight, scale, bias)
+        if prologue is not None and self.mode != "w8a8":
+            raise ValueError("fused FP8 prologues require the w8a8 mode")
         if self.mode == "weight-only":
             self.calls["weight_only"] += 1
             restored = (weight.float() * scale).to(value.dtype)
@@ -119,7 +151,7 @@ class RowFP8Execution:
         shape = value.shape
         matrix = value.reshape(-1, shape[-1])
         rows = matrix.shape[0]
-        codes, act_scale = self._quantize(matrix)
+        codes, act_scale = self._quantize(matrix, prologue, shape)
         with self.measure("linear.fp8_gemm"):
             output = fp8_gemm(codes, act_scale, rows, weight, scale, Epilogue(bias=bias))
         return output.reshape(*shape[:-1], weight.shape[0])
@@ -135,7 +167,8 @@ class RowFP8Execution:
         matrix = value.reshape(-1, value.shape[-1])
         return value.shape, matrix, matrix.shape[0]
 
-    def qkv_linear(self, value, weight, scale, bias=None, *, adapters=None, scalings=None):
+    def qkv_linear(self, value, weight, scale, bias=None, *, adapters=None, scalings=None,
+                   prologue: NormModulate | None = None):
         """Merged QKV projection writing Q, K and V planes directly.
 
         Equivalent to ``linear(value, weight, scale, bias).chunk(3, -1)``
@@ -158,22 +191,22 @@ class RowFP8Execution:
                 raise ValueError("QKV merge requires three adapters and three scalings")
             flat_adapters = tuple(a.reshape(rows, width) for a in adapters)
             scales = tuple(float(s) for s in scalings)
-        codes, act_scale = self._quantize(matrix)
+        codes, act_scale = self._quantize(matrix, prologue, shape)
         with self.measure("linear.fp8_gemm"):
             planes = fp8_gemm(codes, act_scale, rows, weight, scale,
                               Epilogue(bias=bias, planes=3, adapters=flat_adapters, scalings=scales))
         return tuple(planes[i].reshape(*shape[:-1], width) for i in range(3))
 
-    def gelu_linear(self, value, weight, scale, bias=None):
+    def gelu_linear(self, value, weight, scale, bias=None, *, prologue: NormModulate | None = None):
         """``F.gelu(linear(...), approximate="tanh")`` with the GELU in the epilogue."""
         shape, matrix, rows = self._fused_prologue(value, weight, scale, bias)
-        codes, act_scale = self._quantize(matrix)
+        codes, act_scale = self._quantize(matrix, prologue, shape)
         with self.measure("linear.fp8_gemm"):
             out = fp8_gemm(codes, act_scale, rows, weight, scale,
                            Epilogue(kind=_lib.EPI_GELU_TANH, bias=bias))
         return out.reshape(*shape[:-1], weight.shape[0])
 
-    def swiglu_linear(self, value, weight, scale, bias=None):
+    def swiglu_linear(self, value, weight, scale, bias=None, *, prologue: NormModulate | None = None):
         """Packed FFN input projection with ``value * bf16(silu(gate))`` fused.
 
         ``weight`` is the packed ``[2F, K]`` ffn_in matrix (value rows first,
@@ -183,7 +216,7 @@ class RowFP8Execution:
         shape, matrix, rows = self._fused_prologue(value, weight, scale, bias)
         if weight.shape[0] % 64:
             raise ValueError("packed SwiGLU weight needs 2F rows with F % 32 == 0")
-        codes, act_scale = self._quantize(matrix)
+        codes, act_scale = self._quantize(matrix, prologue, shape)
         with self.measure("linear.fp8_gemm"):
             out = fp8_gemm(codes, act_scale, rows, weight, scale,
                            Epilogue(kind=_lib.EPI_SWIGLU, bias=bias))
@@ -217,7 +250,7 @@ class RowFP8Execution:
         return out.reshape(*shape[:-1], n)
 
     def ffn(self, value, up_weight, up_scale, down_weight, down_scale, *, activation="gelu_tanh",
-            up_bias=None, down_bias=None, residual=None, gate=None):
+            up_bias=None, down_bias=None, residual=None, gate=None, prologue: NormModulate | None = None):
         """Fused FFN: up GEMM + activation epilogue -> per-token e4m3 requant -> down GEMM.
 
         ``activation`` is ``"gelu_tanh"`` (up weight ``[F, H]``) or ``"swiglu"``
@@ -244,7 +277,7 @@ class RowFP8Execution:
             raise ValueError("FP8 bias differs from the declared output")
         shape, matrix, rows = self._fused_prologue(value, up_weight, up_scale, up_bias)
         hidden = down_weight.shape[0]
-        codes, act_scale = self._quantize(matrix)
+        codes, act_scale = self._quantize(matrix, prologue, shape)
         with self.measure("linear.fp8_gemm"):
             if activation == "gelu_tanh":
                 mid = fp8_gemm(codes, act_scale, rows, up_weight, up_scale,

@@ -129,6 +129,27 @@ def triton_strict_bf16_gate_residual(residual: Any, gate: Any, projected: Any, *
     return output
 
 
+def triton_strict_bf16_modulate(value: Any, scale: Any, shift: Any, *, block_size: int = 256) -> Any:
+    """Compute ``value * (1 + scale) + shift`` with eager BF16 rounding.
+
+    Replaces src/vflash/native/h3_fused_ops.py:575-611 (kernel 52-122):
+    ``bf16(bf16(value * bf16(1 + scale)) + shift)``, scale and shift ``[S,H]``
+    indexed per token.
+    """
+    batch, tokens, hidden_size = _validate_common(value, scale, modifier_name="scale",
+                                                  block_size=block_size)
+    _validate_common(value, shift, modifier_name="shift", block_size=block_size)
+    torch = _torch()
+    _require_launchable(value)
+    output = torch.empty_like(value)
+    with torch.cuda.device(value.device):
+        rc = _lib.load().vfb_modulate(
+            value.data_ptr(), scale.data_ptr(), scale.stride(0), shift.data_ptr(), shift.stride(0),
+            batch * tokens, tokens, hidden_size, output.data_ptr(), _stream(value.device))
+    _check(rc, "vfb_modulate")
+    return output
+
+
 def triton_strict_bf16_silu_mul(packed: Any, *, block_size: int = 256) -> Any:
     """Fuse H3 ``value * silu(gate)`` while retaining the eager BF16 round."""
     torch = _torch()
