@@ -449,6 +449,36 @@ def other_configs(device, flush, stream, cpu_seconds: float = 0.0) -> dict:
                                         {"step": "quantiser + GEMM + bias"})
     del x, wc, ws, b
 
+    # next-row prologue at config 1's shape: RMSNorm + AdaLN modulate (per-token
+    # scale / shift) + per-token e4m3 quantisation, fused vs the three launches
+    from vflash_b200.kernels import quantize_fp8_norm_modulate
+    from vflash_b200.native.h3_fused_ops import triton_strict_bf16_modulate
+
+    m1 = 32760
+    xp = seeded(m1, 4096, 1005)
+    nw = (1 + seeded(1, 4096, 1006, std=0.1)).view(-1)
+    sc = seeded(m1, 4096, 1007, std=0.3)
+    sh = seeded(m1, 4096, 1008, std=0.3)
+
+    def fused_prologue():
+        quantize_fp8_norm_modulate(xp, nw, 1e-6, sc, sh)
+
+    def unfused_prologue():
+        normed = torch.nn.functional.rms_norm(xp, (4096,), nw, 1e-6)
+        quantize_fp8_rows(triton_strict_bf16_modulate(normed.view(1, m1, 4096), sc, sh).view(m1, 4096))
+
+    fused_ms = statistics.median(_timed(fused_prologue, flush, stream))
+    unfused_ms = statistics.median(_timed(unfused_prologue, flush, stream))
+    pbytes = m1 * 4096 * (2 + 2 + 2 + 1) + m1 * 4 + 4096 * 2
+    hbm = float(peaks.get("hbm_gbs", 6650.0))
+    out["prologue_norm_modulate_quant"] = {
+        "ms": round(fused_ms, 4), "gb_per_s": round(pbytes / (fused_ms * 1e-3) / 1e9, 1),
+        "frac_of_measured_hbm": round(pbytes / (fused_ms * 1e-3) / 1e9 / hbm, 4),
+        "unfused_ms": round(unfused_ms, 4),
+        "step": "x [32760,4096] bf16, per-token scale/shift [32760,4096]: one pass (x, scale, shift "
+                "read, codes written) vs torch rms_norm + vfb_modulate + vfb_fp8_quant_rows"}
+    del xp, nw, sc, sh
+
     # c2: fused FFN, GELU-tanh, per-token requant of the intermediate, residual
     m, h, f = 32760, 4096, 16384
     x = seeded(m, h, 1002)
