@@ -462,6 +462,18 @@ __device__ __forceinline__ float bf16r(float x) {
   return __bfloat162float(__float2bfloat16_rn(x));
 }
 
+// Rounds 32 floats to bf16 values in place, two per cvt.rn.bf16x2.f32: the same
+// per-element rounding as bf16r with half the conversion instructions (the
+// conversions share the XU pipe, which the GEMM epilogues otherwise saturate).
+__device__ __forceinline__ void bf16r_x32(float (&v)[32]) {
+#pragma unroll
+  for (int j = 0; j < 32; j += 2) {
+    const float2 f = __bfloat1622float2(__floats2bfloat162_rn(v[j], v[j + 1]));
+    v[j] = f.x;
+    v[j + 1] = f.y;
+  }
+}
+
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
   return *reinterpret_cast<uint32_t *>(&h);

@@ -154,12 +154,14 @@ __device__ __forceinline__ void scale_bias(float (&v)[32], float sa, const float
   float w[32];
   load_f32x32(sw, w);
 #pragma unroll
-  for (int j = 0; j < 32; ++j) v[j] = bf16r(v[j] * sa * w[j]);
+  for (int j = 0; j < 32; ++j) v[j] = v[j] * sa * w[j];
+  bf16r_x32(v);
   if (bias != nullptr) {
     float b[32];
     load_bf16x32(bias, b);
 #pragma unroll
-    for (int j = 0; j < 32; ++j) v[j] = bf16r(v[j] + b[j]);
+    for (int j = 0; j < 32; ++j) v[j] = v[j] + b[j];
+    bf16r_x32(v);
   }
 }
 
@@ -374,7 +376,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 load_bf16x32(ad + m * ep.adapter_ld + col, a);
                 const float sc = ep.scaling[plane];
 #pragma unroll
-                for (int j = 0; j < 32; ++j) v[j] = v[j] + bf16r(a[j] * sc);
+                for (int j = 0; j < 32; ++j) a[j] = a[j] * sc;
+                bf16r_x32(a);
+#pragma unroll
+                for (int j = 0; j < 32; ++j) v[j] = v[j] + a[j];
               }
             } else if (EPI == VFB_EPI_GELU_TANH) {
 #pragma unroll
@@ -383,8 +388,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
               if (ep.gate != nullptr) {
                 const __nv_bfloat16 *gp = ep.gate + (m % ep.tokens) * ep.gate_ts + n * ep.gate_hs;
 #pragma unroll
-                for (int j = 0; j < 32; ++j)
-                  v[j] = bf16r(__bfloat162float(gp[j * ep.gate_hs]) * v[j]);
+                for (int j = 0; j < 32; ++j) v[j] = __bfloat162float(gp[j * ep.gate_hs]) * v[j];
+                bf16r_x32(v);
               }
               float r[32];
               load_bf16x32(ep.residual + m * ep.ldr + n, r);

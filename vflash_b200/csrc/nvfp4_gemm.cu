@@ -285,7 +285,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         const int32_t col = n - plane * p.plane_width;
         if (live) {
 #pragma unroll
-          for (int j = 0; j < 32; ++j) v[j] = bf16r(alpha * v[j]);
+          for (int j = 0; j < 32; ++j) v[j] = alpha * v[j];
+          bf16r_x32(v);
           if (p.bias != nullptr) {
             const uint4 *bq = reinterpret_cast<const uint4 *>(p.bias + n);
 #pragma unroll
@@ -295,10 +296,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 #pragma unroll
               for (int e = 0; e < 4; ++e) {
                 float2 f = __bfloat1622float2(h[e]);
-                v[8 * g + 2 * e] = bf16r(v[8 * g + 2 * e] + f.x);
-                v[8 * g + 2 * e + 1] = bf16r(v[8 * g + 2 * e + 1] + f.y);
+                v[8 * g + 2 * e] += f.x;
+                v[8 * g + 2 * e + 1] += f.y;
               }
             }
+            bf16r_x32(v);
           }
         } else {
 #pragma unroll
