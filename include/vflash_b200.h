@@ -122,6 +122,17 @@ VFB_API int vfb_fp8_norm_modulate_quant(const void *x, int64_t M, int64_t K, int
  *                     t = m % tokens, or bf16(residual + y) when gate == NULL
  *                     (triton_strict_bf16_gate_residual,
  *                     src/vflash/native/h3_fused_ops.py:125-170,614-657)
+ *   VFB_EPI_QKV_NORM_ROPE  STORE into three planes (Q, K, V; adapters as
+ *                     STORE), then on every 128-column head of the Q and K
+ *                     planes the block's QK-norm and rotary embedding
+ *                     (_qk_norm_rotary, src/vflash/native/h3_native_denoiser.py:
+ *                     409-419): n = bf16((q * rstd) * norm_w) with rstd =
+ *                     rsqrt(mean(q^2) + qk_eps) over the head (fp32 sum, rounded
+ *                     from fp64), then out = bf16(bf16(n * cos[t,d]) +
+ *                     bf16(partner * sin[t,d])), partner = -n[d+64] for d < 64,
+ *                     n[d-64] otherwise (triton_strict_bf16_rotary,
+ *                     src/vflash/native/h3_fused_ops.py:421-510), t = m % tokens;
+ *                     rotary over the whole head (cos/sin [tokens, 128]).
  * Output column n of a STORE/GELU/RESIDUAL epilogue goes to plane
  * p = n / plane_width (plane_width = 0: one plane of width N) at
  *   out + p * plane_stride + m * ldo + (n % plane_width),
@@ -134,6 +145,7 @@ VFB_API int vfb_fp8_norm_modulate_quant(const void *x, int64_t M, int64_t K, int
 #define VFB_EPI_GELU_TANH 1
 #define VFB_EPI_SWIGLU 2
 #define VFB_EPI_RESIDUAL 3
+#define VFB_EPI_QKV_NORM_ROPE 4
 
 typedef struct vfb_epilogue {
   int32_t kind;              /* VFB_EPI_*                                   */
@@ -154,7 +166,15 @@ typedef struct vfb_epilogue {
   const void *gate;          /* bf16 [tokens, N] strided, or NULL           */
   int64_t gate_token_stride; /* elements                                    */
   int64_t gate_hidden_stride;/* elements                                    */
-  int64_t tokens;            /* gate row = m % tokens                       */
+  int64_t tokens;            /* gate / rotary row = m % tokens              */
+  /* QKV_NORM_ROPE (head_dim 128, rotary over the whole head)               */
+  const void *q_norm;        /* bf16 [128] or NULL (no weight)              */
+  const void *k_norm;        /* bf16 [128] or NULL                          */
+  const void *rope_cos;      /* bf16 [tokens, 128], row stride rope_token_stride */
+  const void *rope_sin;      /* bf16 [tokens, 128], same stride             */
+  int64_t rope_token_stride; /* elements, multiple of 8                     */
+  float qk_eps;              /* > 0                                         */
+  int32_t reserved2;
 } vfb_epilogue;
 
 VFB_API int vfb_fp8_gemm(const void *A, int64_t lda, const float *sa,
@@ -223,6 +243,17 @@ VFB_API int vfb_gate_residual(const void *residual, const void *gate, int64_t ga
 VFB_API int vfb_modulate(const void *value, const void *scale, int64_t scale_token_stride,
                          const void *shift, int64_t shift_token_stride, int64_t rows,
                          int64_t tokens, int64_t hidden, void *out, void *stream);
+
+/* triton_strict_bf16_rotary (h3_fused_ops.py:421-510, 1031-1085), split-half
+ * RoPE on value [rows, heads, head_dim] contiguous (rows = batch * tokens) with
+ * cos / sin [tokens, rotary_dim] (row strides *_token_stride, unit column
+ * stride): for d < rotary_dim,
+ *   out[d] = bf16(bf16(x[d] * cos[d]) + bf16(partner[d] * sin[d])),
+ *   partner[d] = d < rotary_dim/2 ? -x[d + rotary_dim/2] : x[d - rotary_dim/2];
+ * out[d] = x[d] for d >= rotary_dim.  rotary_dim even, <= head_dim. */
+VFB_API int vfb_rotary(const void *value, const void *cos, int64_t cos_token_stride, const void *sin,
+                       int64_t sin_token_stride, int64_t rows, int64_t tokens, int64_t heads,
+                       int64_t head_dim, int64_t rotary_dim, void *out, void *stream);
 
 /* triton_strict_bf16_adapter_gate_residual (h3_fused_ops.py:342-415, 982-1028):
  * out = bf16(residual + bf16(gate * bf16(base + bf16(adapter * scaling)))). */

@@ -144,3 +144,22 @@ def rms_norm(x_bits, weight_bits, eps: float) -> np.ndarray:
     if weight_bits is not None:
         y = (y * bf16_value(weight_bits).astype(np.float32)).astype(np.float32)
     return bf16_bits(y)
+
+
+def rotary(value_bits, cos_bits, sin_bits) -> np.ndarray:
+    """``strict_rotary_kernel`` (h3_fused_ops.py:421-510) / ``_apply_rotary`` (h3_native_denoiser.py:246-256).
+
+    value [B,S,heads,head_dim]; cos/sin [S,rotary_dim].  On the first
+    rotary_dim values of each head: bf16(bf16(x * cos) + bf16(partner * sin))
+    with partner = cat(-second_half, first_half); the rest is copied.
+    """
+    value = bf16_value(value_bits)
+    cos = bf16_value(cos_bits)[None, :, None, :]
+    sin = bf16_value(sin_bits)[None, :, None, :]
+    rd = cos.shape[-1]
+    rot = value[..., :rd]
+    first, second = rot[..., : rd // 2], rot[..., rd // 2:]
+    partner = np.concatenate([-second, first], axis=-1)
+    out = value.copy()
+    out[..., :rd] = bf16_round(rot * cos) + bf16_round(partner * sin)
+    return bf16_bits(out.astype(np.float32))

@@ -52,9 +52,10 @@ def test_version_and_error_strings():
 
 def test_epilogue_struct_layout_matches_header():
     # 8-byte aligned fields as declared in vfb_epilogue
-    assert ctypes.sizeof(_lib.Epilogue) == 4 + 4 + 8 * 5 + 8 * 3 + 8 + 4 * 3 + 4 + 8 * 6
+    assert ctypes.sizeof(_lib.Epilogue) == 4 + 4 + 8 * 5 + 8 * 3 + 8 + 4 * 3 + 4 + 8 * 6 + 8 * 5 + 4 + 4
     assert _lib.Epilogue.adapter.offset == 48
     assert _lib.Epilogue.residual.offset == 96
+    assert _lib.Epilogue.q_norm.offset == 144
 
 
 @pytest.mark.parametrize(

@@ -147,3 +147,23 @@ def test_oracle_rms_norm_matches_torch_cpu_within_one_ulp():
     ulp = np.abs(want) * 2.0 ** -7
     assert (diff <= ulp).all()
     assert (diff == 0).mean() > 0.99
+
+
+def test_oracle_rotary_matches_the_reference_eager_expression():
+    # _apply_rotary (h3_native_denoiser.py:246-256) in eager bf16 torch, written out here
+    import torch
+
+    from oracle import epilogues
+    from tests.helpers import bits_of
+
+    gen = torch.Generator().manual_seed(73)
+    for rd in (128, 64):
+        x = torch.randn(2, 7, 3, 128, generator=gen).to(torch.bfloat16)
+        cos = torch.randn(7, rd, generator=gen).to(torch.bfloat16)
+        sin = torch.randn(7, rd, generator=gen).to(torch.bfloat16)
+        rot, passthrough = x[..., :rd], x[..., rd:]
+        first, second = rot.chunk(2, dim=-1)
+        rotated = torch.cat((-second, first), dim=-1)
+        c, s = cos[None, :, None, :], sin[None, :, None, :]
+        eager = torch.cat((rot * c + rotated * s, passthrough), dim=-1)
+        np.testing.assert_array_equal(epilogues.rotary(bits_of(x), bits_of(cos), bits_of(sin)), bits_of(eager))

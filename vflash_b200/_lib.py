@@ -25,6 +25,7 @@ EPI_STORE = 0
 EPI_GELU_TANH = 1
 EPI_SWIGLU = 2
 EPI_RESIDUAL = 3
+EPI_QKV_NORM_ROPE = 4
 
 # Every symbol include/vflash_b200.h declares, with its ctypes signature.
 _c_int64 = ctypes.c_int64
@@ -52,6 +53,13 @@ class Epilogue(ctypes.Structure):
         ("gate_token_stride", _c_int64),
         ("gate_hidden_stride", _c_int64),
         ("tokens", _c_int64),
+        ("q_norm", _vp),
+        ("k_norm", _vp),
+        ("rope_cos", _vp),
+        ("rope_sin", _vp),
+        ("rope_token_stride", _c_int64),
+        ("qk_eps", ctypes.c_float),
+        ("reserved2", ctypes.c_int32),
     ]
 
 
@@ -90,6 +98,9 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         ctypes.c_int, [_vp, _vp, _c_int64, _vp, _c_int64, _c_int64, _c_int64, _vp, _vp]),
     "vfb_modulate": (
         ctypes.c_int, [_vp, _vp, _c_int64, _vp, _c_int64, _c_int64, _c_int64, _c_int64, _vp, _vp]),
+    "vfb_rotary": (
+        ctypes.c_int, [_vp, _vp, _c_int64, _vp, _c_int64, _c_int64, _c_int64, _c_int64, _c_int64, _c_int64,
+                       _vp, _vp]),
     "vfb_adapter_gate_residual": (
         ctypes.c_int,
         [_vp, _vp, _vp, _vp, _c_int64, _c_int64, _c_int64, _c_int64, ctypes.c_float, _vp, _vp]),

@@ -10,6 +10,8 @@
 //   adapter_merge         out = bf16(base + bf16(a * s_branch))          (298-339)
 //   adapter_gate_residual out = bf16(r + bf16(gate * bf16(base + bf16(a * s)))) (342-415)
 //   modulate              out = bf16(bf16(x * bf16(1 + scale)) + shift)  (52-122, 575-611)
+//   rotary                out = bf16(bf16(x * cos) + bf16(partner * sin)) on the first
+//                         rotary_dim values of each head (split-half)   (421-510, 1031-1085)
 // Work is split into 8-element groups along the contiguous last dimension;
 // when every pointer and row stride allows, a group is one 16-byte load or
 // store, otherwise the same kernel runs with scalar accesses.  Offsets are
@@ -157,6 +159,31 @@ __global__ void __launch_bounds__(kThreads) modulate_kernel(
 #pragma unroll
     for (int j = 0; j < 8; ++j) x.v[j] = bf16r(x.v[j] * bf16r(1.0f + sc.v[j])) + sh.v[j];
     x.store(out + off);
+  }
+}
+
+// value [rows, heads, head_dim] contiguous; cos / sin [tokens, rotary_dim]
+// with row strides cos_ts / sin_ts and unit column stride.  For d < half the
+// partner is -x[d + half], otherwise x[d - half]; d >= rotary_dim is copied.
+__global__ void __launch_bounds__(kThreads) rotary_kernel(
+    const __nv_bfloat16 *value, const __nv_bfloat16 *cos, int64_t cos_ts, const __nv_bfloat16 *sin,
+    int64_t sin_ts, int64_t rows, int64_t tokens, int64_t heads, int64_t head_dim, int64_t rotary_dim,
+    __nv_bfloat16 *out) {
+  const int64_t total = rows * heads * head_dim;
+  const int64_t half = rotary_dim / 2;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t d = i % head_dim;
+    const float x = __bfloat162float(value[i]);
+    if (d >= rotary_dim) {
+      out[i] = value[i];
+      continue;
+    }
+    const int64_t token = (i / (heads * head_dim)) % tokens;
+    const float partner = d < half ? -__bfloat162float(value[i + half]) : __bfloat162float(value[i - half]);
+    const float c = __bfloat162float(cos[token * cos_ts + d]);
+    const float s = __bfloat162float(sin[token * sin_ts + d]);
+    out[i] = __float2bfloat16_rn(bf16r(x * c) + bf16r(partner * s));
   }
 }
 
@@ -411,4 +438,22 @@ extern "C" int vfb_modulate(const void *value, const void *scale, int64_t scale_
     modulate_kernel<false><<<grid, kThreads, 0, s>>>(x, sc, scale_token_stride, sh, shift_token_stride, rows,
                                                      tokens, hidden, o);
   return finish("vfb_modulate");
+}
+
+extern "C" int vfb_rotary(const void *value, const void *cos, int64_t cos_token_stride, const void *sin,
+                          int64_t sin_token_stride, int64_t rows, int64_t tokens, int64_t heads,
+                          int64_t head_dim, int64_t rotary_dim, void *out, void *stream) {
+  using namespace vfb;
+  if (rows < 0 || tokens <= 0 || heads <= 0 || head_dim <= 0 || rotary_dim <= 0 ||
+      rotary_dim > head_dim || rotary_dim % 2 || cos_token_stride < 0 || sin_token_stride < 0 ||
+      !value || !cos || !sin || !out)
+    return set_error(VFB_EINVAL, "vfb_rotary: need 0 < rotary_dim <= head_dim, rotary_dim even, tokens > 0");
+  if (rows == 0) return VFB_OK;
+  const int grid = grid_for(rows * heads * head_dim);
+  if (grid < 0) return VFB_EDEVICE;
+  rotary_kernel<<<grid, kThreads, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const __nv_bfloat16 *>(value), static_cast<const __nv_bfloat16 *>(cos), cos_token_stride,
+      static_cast<const __nv_bfloat16 *>(sin), sin_token_stride, rows, tokens, heads, head_dim, rotary_dim,
+      static_cast<__nv_bfloat16 *>(out));
+  return finish("vfb_rotary");
 }

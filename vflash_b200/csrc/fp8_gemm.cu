@@ -62,6 +62,13 @@ struct EpiParams {
   int64_t gate_ts;
   int64_t gate_hs;
   int64_t tokens;
+  // QKV_NORM_ROPE
+  const __nv_bfloat16 *q_norm;
+  const __nv_bfloat16 *k_norm;
+  const __nv_bfloat16 *rope_cos;
+  const __nv_bfloat16 *rope_sin;
+  int64_t rope_ts;
+  float qk_eps;
 };
 
 struct GemmParams {
@@ -162,6 +169,79 @@ __device__ __forceinline__ void scale_bias(float (&v)[32], float sa, const float
 #pragma unroll
     for (int j = 0; j < 32; ++j) v[j] = v[j] + b[j];
     bf16r_x32(v);
+  }
+}
+
+// STORE value of 32 columns: scale_bias, then the plane's LoRA branch if any.
+__device__ __forceinline__ void store_value(float (&v)[32], float sa, const float *sw, const EpiParams &ep,
+                                            int32_t n, int32_t plane, int32_t col, int64_t m) {
+  scale_bias(v, sa, sw + n, ep.bias ? ep.bias + n : nullptr);
+  const __nv_bfloat16 *ad = plane < 3 ? ep.adapter[plane] : nullptr;
+  if (ad != nullptr) {
+    float a[32];
+    load_bf16x32(ad + m * ep.adapter_ld + col, a);
+    const float sc = ep.scaling[plane];
+#pragma unroll
+    for (int j = 0; j < 32; ++j) a[j] = a[j] * sc;
+    bf16r_x32(a);
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] = v[j] + a[j];
+  }
+}
+
+__device__ __forceinline__ void unpack8(const uint4 &u, float (&f)[8]) {
+  const __nv_bfloat162 *h = reinterpret_cast<const __nv_bfloat162 *>(&u);
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    const float2 t = __bfloat1622float2(h[e]);
+    f[2 * e] = t.x;
+    f[2 * e + 1] = t.y;
+  }
+}
+
+__device__ __forceinline__ void bf16r_pair(float &x, float &y) {
+  const float2 f = __bfloat1622float2(__floats2bfloat162_rn(x, y));
+  x = f.x;
+  y = f.y;
+}
+
+// QK-norm + rotary of one head held as two 32-column halves of each rotary
+// half: a = columns [32k, 32k+32), b = columns [64+32k, 64+32k+32) of the
+// head, k in {0, 1}.  w / cos / sin point at the head's column 0.
+__device__ __forceinline__ void qk_norm_rope_pair(float (&a)[32], float (&b)[32], float rstd, int k,
+                                                  const __nv_bfloat16 *w, const __nv_bfloat16 *cs,
+                                                  const __nv_bfloat16 *sn) {
+  const uint4 one = make_uint4(0x3f803f80u, 0x3f803f80u, 0x3f803f80u, 0x3f803f80u);
+#pragma unroll
+  for (int g = 0; g < 4; ++g) {
+    const int da = 32 * k + 8 * g;  // column of a[8g] in the head
+    const int db = da + 64;
+    float wa[8], wb[8], ca[8], sa[8], cb[8], sb[8];
+    unpack8(w ? __ldg(reinterpret_cast<const uint4 *>(w + da)) : one, wa);
+    unpack8(w ? __ldg(reinterpret_cast<const uint4 *>(w + db)) : one, wb);
+    unpack8(__ldg(reinterpret_cast<const uint4 *>(cs + da)), ca);
+    unpack8(__ldg(reinterpret_cast<const uint4 *>(sn + da)), sa);
+    unpack8(__ldg(reinterpret_cast<const uint4 *>(cs + db)), cb);
+    unpack8(__ldg(reinterpret_cast<const uint4 *>(sn + db)), sb);
+#pragma unroll
+    for (int e = 0; e < 8; e += 2) {
+      // n = bf16((x * rstd) * w)
+      float na0 = (a[8 * g + e] * rstd) * wa[e], na1 = (a[8 * g + e + 1] * rstd) * wa[e + 1];
+      float nb0 = (b[8 * g + e] * rstd) * wb[e], nb1 = (b[8 * g + e + 1] * rstd) * wb[e + 1];
+      bf16r_pair(na0, na1);
+      bf16r_pair(nb0, nb1);
+      // first half: n*cos + (-n[d+64])*sin; second half: n*cos + n[d-64]*sin
+      float ac0 = na0 * ca[e], ac1 = na1 * ca[e + 1], as0 = -nb0 * sa[e], as1 = -nb1 * sa[e + 1];
+      float bc0 = nb0 * cb[e], bc1 = nb1 * cb[e + 1], bs0 = na0 * sb[e], bs1 = na1 * sb[e + 1];
+      bf16r_pair(ac0, ac1);
+      bf16r_pair(as0, as1);
+      bf16r_pair(bc0, bc1);
+      bf16r_pair(bs0, bs1);
+      a[8 * g + e] = ac0 + as0;
+      a[8 * g + e + 1] = ac1 + as1;
+      b[8 * g + e] = bc0 + bs0;
+      b[8 * g + e + 1] = bc1 + bs1;
+    }
   }
 }
 
@@ -338,7 +418,69 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       const float sa = live ? __ldg(p.sa + m) : 0.0f;
       const uint32_t t_row = tmem_base + acc * BN + (static_cast<uint32_t>(q * 32) << 16);
 
-      if (EPI == VFB_EPI_SWIGLU) {
+      if (EPI == VFB_EPI_QKV_NORM_ROPE) {
+#pragma unroll 1
+        for (int hh = 0; hh < BN / 128; ++hh) {
+          const int32_t n0 = n_tile * BN + hh * 128;
+          if (n0 >= p.N) break;  // warp-uniform
+          const int32_t plane = n0 / ep.plane_width;
+          const int32_t col0 = n0 - plane * ep.plane_width;
+          const uint32_t t_head = t_row + hh * 128;
+          if (plane == 2) {  // V: plain store
+#pragma unroll 1
+            for (int k = 0; k < 4; ++k) {
+              float v[32];
+              tmem_ld_32x32b_x32(t_head + k * 32, v);
+              if (live) {
+                store_value(v, sa, p.sw, ep, n0 + 32 * k, plane, col0 + 32 * k, m);
+              } else {
+#pragma unroll
+                for (int j = 0; j < 32; ++j) v[j] = 0.0f;
+              }
+              store_box(warp_smem, box, &tmOut, v, lane, col0 + 32 * k, static_cast<int32_t>(row0), plane,
+                        any_row);
+            }
+            continue;
+          }
+          // pass 1: this thread's row of the head, sum of squares in fp32
+          float ss = 0.0f;
+#pragma unroll 1
+          for (int k = 0; k < 4; ++k) {
+            float v[32];
+            tmem_ld_32x32b_x32(t_head + k * 32, v);
+            if (live) {
+              store_value(v, sa, p.sw, ep, n0 + 32 * k, plane, col0 + 32 * k, m);
+#pragma unroll
+              for (int j = 0; j < 32; ++j) ss = fmaf(v[j], v[j], ss);
+            }
+          }
+          const float mean_eps = __fadd_rn(__fdiv_rn(ss, 128.0f), ep.qk_eps);
+          const float rstd = static_cast<float>(1.0 / sqrt(static_cast<double>(mean_eps)));
+          const __nv_bfloat16 *w = plane == 0 ? ep.q_norm : ep.k_norm;
+          const int64_t token = live ? m % ep.tokens : 0;
+          const __nv_bfloat16 *cs = ep.rope_cos + token * ep.rope_ts;
+          const __nv_bfloat16 *sn = ep.rope_sin + token * ep.rope_ts;
+          // pass 2: the two rotary halves of the head, 32 columns at a time
+#pragma unroll 1
+          for (int k = 0; k < 2; ++k) {
+            float a[32], b[32];
+            tmem_ld_32x32b_x32(t_head + k * 32, a);
+            tmem_ld_32x32b_x32(t_head + (k + 2) * 32, b);
+            if (live) {
+              store_value(a, sa, p.sw, ep, n0 + 32 * k, plane, col0 + 32 * k, m);
+              store_value(b, sa, p.sw, ep, n0 + 32 * (k + 2), plane, col0 + 32 * (k + 2), m);
+              qk_norm_rope_pair(a, b, rstd, k, w, cs, sn);
+            } else {
+#pragma unroll
+              for (int j = 0; j < 32; ++j) a[j] = b[j] = 0.0f;
+            }
+            store_box(warp_smem, box, &tmOut, a, lane, col0 + 32 * k, static_cast<int32_t>(row0), plane,
+                      any_row);
+            store_box(warp_smem, box, &tmOut, b, lane, col0 + 32 * (k + 2), static_cast<int32_t>(row0), plane,
+                      any_row);
+          }
+        }
+      } else if (EPI == VFB_EPI_SWIGLU) {
         const int32_t F = ep.plane_width;
 #pragma unroll 1
         for (int c = 0; c < BN_HALF / 32; ++c) {
@@ -368,23 +510,14 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           const int32_t plane = n / ep.plane_width;
           const int32_t col = n - plane * ep.plane_width;
           if (live) {
-            scale_bias(v, sa, p.sw + n, ep.bias ? ep.bias + n : nullptr);
             if (EPI == VFB_EPI_STORE) {
-              const __nv_bfloat16 *ad = plane < 3 ? ep.adapter[plane] : nullptr;
-              if (ad != nullptr) {
-                float a[32];
-                load_bf16x32(ad + m * ep.adapter_ld + col, a);
-                const float sc = ep.scaling[plane];
-#pragma unroll
-                for (int j = 0; j < 32; ++j) a[j] = a[j] * sc;
-                bf16r_x32(a);
-#pragma unroll
-                for (int j = 0; j < 32; ++j) v[j] = v[j] + a[j];
-              }
+              store_value(v, sa, p.sw, ep, n, plane, col, m);
             } else if (EPI == VFB_EPI_GELU_TANH) {
+              scale_bias(v, sa, p.sw + n, ep.bias ? ep.bias + n : nullptr);
 #pragma unroll
               for (int j = 0; j < 32; ++j) v[j] = gelu_tanh(v[j]);
             } else if (EPI == VFB_EPI_RESIDUAL) {
+              scale_bias(v, sa, p.sw + n, ep.bias ? ep.bias + n : nullptr);
               if (ep.gate != nullptr) {
                 const __nv_bfloat16 *gp = ep.gate + (m % ep.tokens) * ep.gate_ts + n * ep.gate_hs;
 #pragma unroll
@@ -502,7 +635,7 @@ extern "C" int vfb_fp8_gemm(const void *A, int64_t lda, const float *sa, const v
   using namespace vfb;
   if (ep == nullptr) return set_error(VFB_EINVAL, "vfb_fp8_gemm: epilogue is NULL");
   const int kind = ep->kind;
-  if (kind < VFB_EPI_STORE || kind > VFB_EPI_RESIDUAL)
+  if (kind < VFB_EPI_STORE || kind > VFB_EPI_QKV_NORM_ROPE)
     return set_error(VFB_EINVAL, "vfb_fp8_gemm: unknown epilogue kind %d", kind);
   if (M < 0 || N <= 0 || K <= 0 || K % 16 || N % 32)
     return set_error(VFB_EINVAL, "vfb_fp8_gemm: need M >= 0, N > 0 with N %% 32 == 0, K > 0 with "
@@ -565,7 +698,26 @@ extern "C" int vfb_fp8_gemm(const void *A, int64_t lda, const float *sa, const v
     p.num_n_tiles = static_cast<int>((N + BN - 1) / BN);
     if ((rc = make_map_u8(&tb, W, N, K, ldw, BN_HALF)) != VFB_OK) return rc;
     tb2 = tb;
-    if (kind == VFB_EPI_STORE) {
+    if (kind == VFB_EPI_QKV_NORM_ROPE) {
+      const auto a16p = [](const void *q) { return q == nullptr || aligned16(q); };
+      if (planes != 3 || width % 128)
+        return set_error(VFB_EINVAL, "vfb_fp8_gemm: QKV_NORM_ROPE needs three planes of 128-column heads");
+      if (ep->rope_cos == nullptr || ep->rope_sin == nullptr || !aligned16(ep->rope_cos) ||
+          !aligned16(ep->rope_sin) || ep->rope_token_stride < 0 || ep->rope_token_stride % 8 ||
+          (ep->tokens > 1 && ep->rope_token_stride < 128) || ep->tokens <= 0)
+        return set_error(VFB_EINVAL,
+                         "vfb_fp8_gemm: rotary cos/sin need 16-byte aligned [tokens, 128] rows, tokens > 0");
+      if (!a16p(ep->q_norm) || !a16p(ep->k_norm) || !(ep->qk_eps > 0.0f))
+        return set_error(VFB_EINVAL, "vfb_fp8_gemm: QK-norm weights need 16-byte alignment, qk_eps > 0");
+      e.q_norm = static_cast<const __nv_bfloat16 *>(ep->q_norm);
+      e.k_norm = static_cast<const __nv_bfloat16 *>(ep->k_norm);
+      e.rope_cos = static_cast<const __nv_bfloat16 *>(ep->rope_cos);
+      e.rope_sin = static_cast<const __nv_bfloat16 *>(ep->rope_sin);
+      e.rope_ts = ep->rope_token_stride;
+      e.qk_eps = ep->qk_eps;
+      e.tokens = ep->tokens;
+    }
+    if (kind == VFB_EPI_STORE || kind == VFB_EPI_QKV_NORM_ROPE) {
       for (int i = 0; i < 3; ++i) {
         e.adapter[i] = static_cast<const __nv_bfloat16 *>(ep->adapter[i]);
         e.scaling[i] = ep->scaling[i];
@@ -602,6 +754,8 @@ extern "C" int vfb_fp8_gemm(const void *A, int64_t lda, const float *sa, const v
       return launch<VFB_EPI_GELU_TANH>(ta, tb, tb2, to, p, sm_count, s);
     case VFB_EPI_SWIGLU:
       return launch<VFB_EPI_SWIGLU>(ta, tb, tb2, to, p, sm_count, s);
+    case VFB_EPI_QKV_NORM_ROPE:
+      return launch<VFB_EPI_QKV_NORM_ROPE>(ta, tb, tb2, to, p, sm_count, s);
     default:
       return launch<VFB_EPI_RESIDUAL>(ta, tb, tb2, to, p, sm_count, s);
   }

@@ -141,6 +141,12 @@ class Epilogue:
     residual: torch.Tensor | None = None # RESIDUAL: bf16 [M, N]
     gate: torch.Tensor | None = None     # RESIDUAL: bf16 [tokens, N] with unit hidden stride
     tokens: int = 0
+    # QKV_NORM_ROPE (planes = 3, 128-column heads, rotary over the whole head)
+    q_norm: torch.Tensor | None = None   # bf16 [128] or None
+    k_norm: torch.Tensor | None = None   # bf16 [128] or None
+    rope_cos: torch.Tensor | None = None # bf16 [tokens, 128], unit column stride
+    rope_sin: torch.Tensor | None = None # bf16 [tokens, 128], same layout as rope_cos
+    qk_eps: float = 1e-5
 
 
 def fp8_gemm(a_codes: torch.Tensor, a_scales: torch.Tensor, rows: int, weight: torch.Tensor,
@@ -206,6 +212,26 @@ def fp8_gemm(a_codes: torch.Tensor, a_scales: torch.Tensor, rows: int, weight: t
         e.adapter_ld = width
         for i, s in enumerate(ep.scalings):
             e.scaling[i] = float(s)
+    if ep.kind == _lib.EPI_QKV_NORM_ROPE:
+        cos, sin = ep.rope_cos, ep.rope_sin
+        if (cos is None or sin is None or cos.dtype != BF16 or sin.dtype != BF16 or cos.ndim != 2
+                or cos.shape != sin.shape or cos.shape[1] != 128 or cos.stride(1) != 1 or sin.stride(1) != 1
+                or cos.stride(0) != sin.stride(0) or cos.device != device or sin.device != device):
+            raise KernelInputError("rotary cos/sin must be bf16 [tokens, 128] with one row stride")
+        for name, w in (("q_norm", ep.q_norm), ("k_norm", ep.k_norm)):
+            if w is not None and (w.dtype != BF16 or w.shape != (128,) or not w.is_contiguous()
+                                  or w.device != device):
+                raise KernelInputError(f"{name} must be contiguous bf16 [128]")
+        if ep.planes != 3:
+            raise KernelInputError("QK-norm + rotary writes the three Q, K, V planes")
+        tokens = cos.shape[0]
+        e.q_norm = None if ep.q_norm is None else ep.q_norm.data_ptr()
+        e.k_norm = None if ep.k_norm is None else ep.k_norm.data_ptr()
+        e.rope_cos = cos.data_ptr()
+        e.rope_sin = sin.data_ptr()
+        e.rope_token_stride = cos.stride(0) if tokens > 1 else 0
+        e.qk_eps = float(ep.qk_eps)
+        e.tokens = tokens
     if ep.kind == _lib.EPI_RESIDUAL:
         r = ep.residual
         if r is None or r.dtype != BF16 or r.shape != (rows, n) or r.stride(1) != 1:

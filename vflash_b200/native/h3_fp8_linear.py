@@ -57,6 +57,22 @@ class NormModulate:
     eps: float = 1e-6
 
 
+@dataclass(frozen=True)
+class QKNormRope:
+    """The block's QK-norm + rotary (h3_native_denoiser.py:409-419) fused into ``qkv_linear``.
+
+    ``q_norm``/``k_norm`` bf16 ``[128]`` (or None), ``cos``/``sin`` bf16
+    ``[S, 128]`` indexed by token (rotary over the whole 128-wide head), ``eps``
+    the QK-norm epsilon.
+    """
+
+    q_norm: torch.Tensor | None
+    k_norm: torch.Tensor | None
+    cos: torch.Tensor
+    sin: torch.Tensor
+    eps: float = 1e-5
+
+
 def _on_sm100(device: torch.device) -> bool:
     return device.type == "cuda" and torch.cuda.get_device_capability(device) == (10, 0)
 
@@ -168,8 +184,12 @@ class RowFP8Execution:
         return value.shape, matrix, matrix.shape[0]
 
     def qkv_linear(self, value, weight, scale, bias=None, *, adapters=None, scalings=None,
-                   prologue: NormModulate | None = None):
+                   prologue: NormModulate | None = None, qk_norm_rope: QKNormRope | None = None):
         """Merged QKV projection writing Q, K and V planes directly.
+
+        With ``qk_norm_rope`` the Q and K planes also get the block's per-head
+        RMSNorm and rotary embedding in the epilogue (one pass instead of
+        ``_qk_norm_rotary``'s four launches).
 
         Equivalent to ``linear(value, weight, scale, bias).chunk(3, -1)``
         (src/vflash/native/h3_native_denoiser.py:541) followed, when
@@ -191,10 +211,18 @@ class RowFP8Execution:
                 raise ValueError("QKV merge requires three adapters and three scalings")
             flat_adapters = tuple(a.reshape(rows, width) for a in adapters)
             scales = tuple(float(s) for s in scalings)
+        epilogue = Epilogue(bias=bias, planes=3, adapters=flat_adapters, scalings=scales)
+        if qk_norm_rope is not None:
+            tokens = qk_norm_rope.cos.shape[0] if qk_norm_rope.cos.ndim == 2 else 0
+            if width % 128 or tokens < 1 or rows % tokens or (len(shape) >= 3 and tokens not in (1, shape[-2])):
+                raise ValueError("FP8 QK-norm rotary needs 128-wide heads and cos/sin rows per token")
+            epilogue.kind = _lib.EPI_QKV_NORM_ROPE
+            epilogue.q_norm, epilogue.k_norm = qk_norm_rope.q_norm, qk_norm_rope.k_norm
+            epilogue.rope_cos, epilogue.rope_sin = qk_norm_rope.cos, qk_norm_rope.sin
+            epilogue.qk_eps = qk_norm_rope.eps
         codes, act_scale = self._quantize(matrix, prologue, shape)
         with self.measure("linear.fp8_gemm"):
-            planes = fp8_gemm(codes, act_scale, rows, weight, scale,
-                              Epilogue(bias=bias, planes=3, adapters=flat_adapters, scalings=scales))
+            planes = fp8_gemm(codes, act_scale, rows, weight, scale, epilogue)
         return tuple(planes[i].reshape(*shape[:-1], width) for i in range(3))
 
     def gelu_linear(self, value, weight, scale, bias=None, *, prologue: NormModulate | None = None):

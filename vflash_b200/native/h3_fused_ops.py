@@ -150,6 +150,39 @@ def triton_strict_bf16_modulate(value: Any, scale: Any, shift: Any, *, block_siz
     return output
 
 
+def triton_strict_bf16_rotary(value: Any, cos: Any, sin: Any, *, block_size: int = 256) -> Any:
+    """Apply H3 split-half RoPE while preserving eager BF16 products.
+
+    Replaces src/vflash/native/h3_fused_ops.py:1031-1085 (kernel 421-510):
+    value ``[B,S,heads,head_dim]``, cos/sin ``[S,rotary_dim]``.
+    """
+    torch = _torch()
+    if block_size not in _BLOCK_SIZES:
+        raise H3FusedOpsError(f"unsupported fused H3 block size: {block_size}")
+    if not all(isinstance(item, torch.Tensor) for item in (value, cos, sin)):
+        raise H3FusedOpsError("fused H3 rotary inputs must be tensors")
+    if value.device.type != "cuda" or cos.device != value.device or sin.device != value.device:
+        raise H3FusedOpsError("fused H3 rotary inputs must share one CUDA device")
+    if value.dtype != torch.bfloat16 or cos.dtype != value.dtype or sin.dtype != value.dtype:
+        raise H3FusedOpsError("fused H3 rotary inputs must use BF16")
+    if value.ndim != 4 or cos.ndim != 2 or tuple(sin.shape) != tuple(cos.shape):
+        raise H3FusedOpsError("fused H3 rotary shapes are invalid")
+    batch, tokens, heads, head_dim = (int(item) for item in value.shape)
+    rotary_dim = int(cos.shape[1])
+    if int(cos.shape[0]) != tokens or rotary_dim <= 0 or rotary_dim > head_dim or rotary_dim % 2:
+        raise H3FusedOpsError("fused H3 rotary dimension is invalid")
+    if not value.is_contiguous() or cos.stride(-1) != 1 or sin.stride(-1) != 1:
+        raise H3FusedOpsError("fused H3 rotary inputs require contiguous hidden dimensions")
+    _require_launchable(value)
+    output = torch.empty_like(value)
+    with torch.cuda.device(value.device):
+        rc = _lib.load().vfb_rotary(
+            value.data_ptr(), cos.data_ptr(), cos.stride(0), sin.data_ptr(), sin.stride(0), batch * tokens,
+            tokens, heads, head_dim, rotary_dim, output.data_ptr(), _stream(value.device))
+    _check(rc, "vfb_rotary")
+    return output
+
+
 def triton_strict_bf16_silu_mul(packed: Any, *, block_size: int = 256) -> Any:
     """Fuse H3 ``value * silu(gate)`` while retaining the eager BF16 round."""
     torch = _torch()
