@@ -479,6 +479,41 @@ def other_configs(device, flush, stream, cpu_seconds: float = 0.0) -> dict:
                 "read, codes written) vs torch rms_norm + vfb_modulate + vfb_fp8_quant_rows"}
     del xp, nw, sc, sh
 
+    # next-row epilogue at config 1's shape: QKV projection + per-head QK-norm +
+    # rotary, fused vs the GEMM followed by rms_norm and the strict rotary on Q and K
+    from vflash_b200.native.h3_fp8_linear import QKNormRope, RowFP8Execution as _Exec
+    from vflash_b200.native.h3_fused_ops import triton_strict_bf16_rotary
+
+    xq = seeded(m1, 4096, 1009, outliers=True)
+    wq, wqs = quantize_fp8_rows(seeded(12288, 4096, 2011, std=0.02), pad_to=1)
+    qn = (1 + seeded(1, 128, 1010, std=0.1)).view(-1)
+    kn = (1 + seeded(1, 128, 1011, std=0.1)).view(-1)
+    pos = torch.arange(m1, device=device, dtype=torch.float32)[:, None]
+    freq = 1.0 / (10000 ** (torch.arange(64, device=device, dtype=torch.float32) / 64))
+    ang = torch.cat([pos * freq, pos * freq], dim=1)
+    rc, rs = ang.cos().to(torch.bfloat16), ang.sin().to(torch.bfloat16)
+    ex = _Exec("w8a8")
+    rope = QKNormRope(qn, kn, rc, rs, 1e-5)
+    x3 = xq.view(1, m1, 4096)
+
+    def fused_qkv():
+        ex.qkv_linear(x3, wq, wqs, qk_norm_rope=rope)
+
+    def unfused_qkv():
+        q, k, _v = ex.qkv_linear(x3, wq, wqs)
+        for t, w in ((q, qn), (k, kn)):
+            h = torch.nn.functional.rms_norm(t.view(1, m1, 32, 128), (128,), w, 1e-5)
+            triton_strict_bf16_rotary(h, rc, rs)
+
+    fq = statistics.median(_timed(fused_qkv, flush, stream))
+    uq = statistics.median(_timed(unfused_qkv, flush, stream))
+    qflop = 2.0 * m1 * 12288 * 4096
+    out["qkv_qk_norm_rope"] = {
+        "ms": round(fq, 4), "tflops": round(qflop / (fq * 1e-3) / 1e12, 1), "unfused_ms": round(uq, 4),
+        "step": "quantiser + QKV GEMM with per-head QK-norm + rotary on Q and K in the epilogue, vs the "
+                "same GEMM then torch rms_norm and vfb_rotary on Q and K"}
+    del xq, wq, wqs, rc, rs, ang
+
     # c2: fused FFN, GELU-tanh, per-token requant of the intermediate, residual
     m, h, f = 32760, 4096, 16384
     x = seeded(m, h, 1002)

@@ -40,13 +40,23 @@ constexpr int UMMA_K = 32;
 constexpr int STAGES = 5;
 constexpr int A_STAGE_BYTES = BM * BK;       // 16 KB
 constexpr int B_STAGE_BYTES = BN_HALF * BK;  // 16 KB
-constexpr int NUM_THREADS = 192;
+// Warps 0 (TMA) and 1 (MMA) plus the epilogue warps: four (one per TMEM lane
+// quarter) for the light epilogues, eight for QK-norm + rotary, where each
+// 256-column tile is two 128-column heads and each head gets its own four
+// warps.
+template <int EPI>
+__host__ __device__ constexpr int epi_warps() { return EPI == VFB_EPI_QKV_NORM_ROPE ? 8 : 4; }
+template <int EPI>
+__host__ __device__ constexpr int num_threads() { return 64 + 32 * epi_warps<EPI>(); }
 constexpr int TMEM_COLS = 512;
 // Epilogue staging: per epilogue warp a ring of EPI_BOXES 32 x 32 bf16 boxes
 // (2 KB each), so TMA stores drain while the warp fills the next boxes.
-constexpr int EPI_BOXES = 4;
+constexpr int EPI_BOXES = 4;  // with four epilogue warps; two with eight (same shared memory)
+template <int EPI>
+__host__ __device__ constexpr int epi_boxes() { return 16 / epi_warps<EPI>(); }
 constexpr int EPI_BOX_BYTES = 32 * 32 * 2;
 constexpr int EPI_SMEM_BYTES = 4 * EPI_BOXES * EPI_BOX_BYTES;
+static_assert(8 * 2 * EPI_BOX_BYTES == EPI_SMEM_BYTES, "eight-warp epilogue staging must fit");
 constexpr size_t SMEM_BYTES =
     1024 + STAGES * (A_STAGE_BYTES + B_STAGE_BYTES) + EPI_SMEM_BYTES + 256;
 
@@ -127,11 +137,12 @@ __device__ __forceinline__ void load_bf16x32(const __nv_bfloat16 *p, float (&r)[
 // uses (conflict-free 16-byte stores), then lane 0 issues one TMA store.
 // Each warp cycles through EPI_BOXES staging boxes; a box is rewritten only
 // after the store issued from it EPI_BOXES chunks earlier has read it.
+template <int BOXES = EPI_BOXES>
 __device__ __forceinline__ void store_box(uint8_t *warp_smem, int &box, const CUtensorMap *map,
                                           const float (&y)[32], int lane, int32_t col, int32_t row0,
                                           int32_t plane, bool any_row) {
   uint8_t *buf = warp_smem + box * EPI_BOX_BYTES;
-  if (lane == 0) bulk_wait_group_read<EPI_BOXES - 1>();
+  if (lane == 0) bulk_wait_group_read<BOXES - 1>();
   __syncwarp();
   uint4 *row = reinterpret_cast<uint4 *>(buf + lane * 64);
   const int sw = (lane >> 1) & 3;
@@ -151,7 +162,7 @@ __device__ __forceinline__ void store_box(uint8_t *warp_smem, int &box, const CU
     tma_store_3d_hint(map, buf, col, row0, plane, l2_policy_evict_first());
     bulk_commit_group();
   }
-  box = box + 1 == EPI_BOXES ? 0 : box + 1;
+  box = box + 1 == BOXES ? 0 : box + 1;
 }
 
 // y = bf16(acc * sa * sw) then bf16(y + bias): the _scaled_mm output followed
@@ -189,16 +200,6 @@ __device__ __forceinline__ void store_value(float (&v)[32], float sa, const floa
   }
 }
 
-__device__ __forceinline__ void unpack8(const uint4 &u, float (&f)[8]) {
-  const __nv_bfloat162 *h = reinterpret_cast<const __nv_bfloat162 *>(&u);
-#pragma unroll
-  for (int e = 0; e < 4; ++e) {
-    const float2 t = __bfloat1622float2(h[e]);
-    f[2 * e] = t.x;
-    f[2 * e + 1] = t.y;
-  }
-}
-
 __device__ __forceinline__ void bf16r_pair(float &x, float &y) {
   const float2 f = __bfloat1622float2(__floats2bfloat162_rn(x, y));
   x = f.x;
@@ -208,26 +209,42 @@ __device__ __forceinline__ void bf16r_pair(float &x, float &y) {
 // QK-norm + rotary of one head held as two 32-column halves of each rotary
 // half: a = columns [32k, 32k+32), b = columns [64+32k, 64+32k+32) of the
 // head, k in {0, 1}.  w / cos / sin point at the head's column 0.
+__device__ __forceinline__ void unpack4(const uint2 &u, float (&f)[4]) {
+  const __nv_bfloat162 *h = reinterpret_cast<const __nv_bfloat162 *>(&u);
+  const float2 t0 = __bfloat1622float2(h[0]);
+  const float2 t1 = __bfloat1622float2(h[1]);
+  f[0] = t0.x;
+  f[1] = t0.y;
+  f[2] = t1.x;
+  f[3] = t1.y;
+}
+
+__device__ __forceinline__ uint2 ld4(const __nv_bfloat16 *p) { return __ldg(reinterpret_cast<const uint2 *>(p)); }
+
+// QK-norm + rotary of one head held as two 32-column halves of each rotary
+// half: a = columns [32k, 32k+32), b = columns [64+32k, 64+32k+32) of the
+// head, k in {0, 1}.  w / cos / sin point at the head's column 0.  Works four
+// columns at a time to bound the live registers.
 __device__ __forceinline__ void qk_norm_rope_pair(float (&a)[32], float (&b)[32], float rstd, int k,
                                                   const __nv_bfloat16 *w, const __nv_bfloat16 *cs,
                                                   const __nv_bfloat16 *sn) {
-  const uint4 one = make_uint4(0x3f803f80u, 0x3f803f80u, 0x3f803f80u, 0x3f803f80u);
+  const uint2 one = make_uint2(0x3f803f80u, 0x3f803f80u);
 #pragma unroll
-  for (int g = 0; g < 4; ++g) {
-    const int da = 32 * k + 8 * g;  // column of a[8g] in the head
+  for (int g = 0; g < 8; ++g) {
+    const int da = 32 * k + 4 * g;  // column of a[4g] in the head
     const int db = da + 64;
-    float wa[8], wb[8], ca[8], sa[8], cb[8], sb[8];
-    unpack8(w ? __ldg(reinterpret_cast<const uint4 *>(w + da)) : one, wa);
-    unpack8(w ? __ldg(reinterpret_cast<const uint4 *>(w + db)) : one, wb);
-    unpack8(__ldg(reinterpret_cast<const uint4 *>(cs + da)), ca);
-    unpack8(__ldg(reinterpret_cast<const uint4 *>(sn + da)), sa);
-    unpack8(__ldg(reinterpret_cast<const uint4 *>(cs + db)), cb);
-    unpack8(__ldg(reinterpret_cast<const uint4 *>(sn + db)), sb);
+    float wa[4], wb[4], ca[4], sa[4], cb[4], sb[4];
+    unpack4(w ? ld4(w + da) : one, wa);
+    unpack4(w ? ld4(w + db) : one, wb);
+    unpack4(ld4(cs + da), ca);
+    unpack4(ld4(sn + da), sa);
+    unpack4(ld4(cs + db), cb);
+    unpack4(ld4(sn + db), sb);
 #pragma unroll
-    for (int e = 0; e < 8; e += 2) {
+    for (int e = 0; e < 4; e += 2) {
       // n = bf16((x * rstd) * w)
-      float na0 = (a[8 * g + e] * rstd) * wa[e], na1 = (a[8 * g + e + 1] * rstd) * wa[e + 1];
-      float nb0 = (b[8 * g + e] * rstd) * wb[e], nb1 = (b[8 * g + e + 1] * rstd) * wb[e + 1];
+      float na0 = (a[4 * g + e] * rstd) * wa[e], na1 = (a[4 * g + e + 1] * rstd) * wa[e + 1];
+      float nb0 = (b[4 * g + e] * rstd) * wb[e], nb1 = (b[4 * g + e + 1] * rstd) * wb[e + 1];
       bf16r_pair(na0, na1);
       bf16r_pair(nb0, nb1);
       // first half: n*cos + (-n[d+64])*sin; second half: n*cos + n[d-64]*sin
@@ -237,16 +254,16 @@ __device__ __forceinline__ void qk_norm_rope_pair(float (&a)[32], float (&b)[32]
       bf16r_pair(as0, as1);
       bf16r_pair(bc0, bc1);
       bf16r_pair(bs0, bs1);
-      a[8 * g + e] = ac0 + as0;
-      a[8 * g + e + 1] = ac1 + as1;
-      b[8 * g + e] = bc0 + bs0;
-      b[8 * g + e + 1] = bc1 + bs1;
+      a[4 * g + e] = ac0 + as0;
+      a[4 * g + e + 1] = ac1 + as1;
+      b[4 * g + e] = bc0 + bs0;
+      b[4 * g + e + 1] = bc1 + bs1;
     }
   }
 }
 
 template <int EPI>
-__global__ void __launch_bounds__(NUM_THREADS, 1)
+__global__ void __launch_bounds__(num_threads<EPI>(), 1)
     fp8_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                     const __grid_constant__ CUtensorMap tmB2, const __grid_constant__ CUtensorMap tmOut,
                     const GemmParams p) {
@@ -277,7 +294,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tfull_bar[a], 1);
-      mbar_init(&tempty_bar[a], 2 * 128);  // leader: every epilogue thread of both CTAs
+      mbar_init(&tempty_bar[a], 2 * 32 * epi_warps<EPI>());  // leader: every epilogue thread of both CTAs
     }
     mbar_init(drain_bar, 1);
     *abort_flag = 0;
@@ -401,7 +418,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     // ---------------- epilogue (warps 2..5 of both CTAs) ----------------
     const int q = warp & 3;  // TMEM lane quarter this warp may access
     const EpiParams &ep = p.ep;
-    uint8_t *warp_smem = sEpi + q * EPI_BOXES * EPI_BOX_BYTES;
+    constexpr int kBoxes = epi_boxes<EPI>();
+    const int group = (warp - 2) >> 2;  // QKV_NORM_ROPE: the head of the tile this warp handles
+    uint8_t *warp_smem = sEpi + (q + 4 * group) * kBoxes * EPI_BOX_BYTES;
     int box = 0;
     int t = 0;
     for (int tile = pair; tile < num_tiles; tile += num_pairs, ++t) {
@@ -419,14 +438,14 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       const uint32_t t_row = tmem_base + acc * BN + (static_cast<uint32_t>(q * 32) << 16);
 
       if (EPI == VFB_EPI_QKV_NORM_ROPE) {
-#pragma unroll 1
-        for (int hh = 0; hh < BN / 128; ++hh) {
-          const int32_t n0 = n_tile * BN + hh * 128;
-          if (n0 >= p.N) break;  // warp-uniform
-          const int32_t plane = n0 / ep.plane_width;
-          const int32_t col0 = n0 - plane * ep.plane_width;
-          const uint32_t t_head = t_row + hh * 128;
-          if (plane == 2) {  // V: plain store
+        const int hh = group;
+        const int32_t n0 = n_tile * BN + hh * 128;
+        const int32_t plane = n0 / ep.plane_width;
+        const int32_t col0 = n0 - plane * ep.plane_width;
+        const uint32_t t_head = t_row + hh * 128;
+        if (n0 >= p.N) {
+          // past the last head (warp-uniform): nothing to store
+        } else if (plane == 2) {  // V: plain store
 #pragma unroll 1
             for (int k = 0; k < 4; ++k) {
               float v[32];
@@ -437,11 +456,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 #pragma unroll
                 for (int j = 0; j < 32; ++j) v[j] = 0.0f;
               }
-              store_box(warp_smem, box, &tmOut, v, lane, col0 + 32 * k, static_cast<int32_t>(row0), plane,
-                        any_row);
+              store_box<kBoxes>(warp_smem, box, &tmOut, v, lane, col0 + 32 * k, static_cast<int32_t>(row0),
+                                plane, any_row);
             }
-            continue;
-          }
+        } else {
           // pass 1: this thread's row of the head, sum of squares in fp32
           float ss = 0.0f;
 #pragma unroll 1
@@ -474,9 +492,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 #pragma unroll
               for (int j = 0; j < 32; ++j) a[j] = b[j] = 0.0f;
             }
-            store_box(warp_smem, box, &tmOut, a, lane, col0 + 32 * k, static_cast<int32_t>(row0), plane,
+            store_box<kBoxes>(warp_smem, box, &tmOut, a, lane, col0 + 32 * k, static_cast<int32_t>(row0), plane,
                       any_row);
-            store_box(warp_smem, box, &tmOut, b, lane, col0 + 32 * (k + 2), static_cast<int32_t>(row0), plane,
+            store_box<kBoxes>(warp_smem, box, &tmOut, b, lane, col0 + 32 * (k + 2), static_cast<int32_t>(row0), plane,
                       any_row);
           }
         }
@@ -498,7 +516,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 #pragma unroll
             for (int j = 0; j < 32; ++j) v[j] = 0.0f;
           }
-          store_box(warp_smem, box, &tmOut, v, lane, f, static_cast<int32_t>(row0), 0, any_row);
+          store_box<kBoxes>(warp_smem, box, &tmOut, v, lane, f, static_cast<int32_t>(row0), 0, any_row);
         }
       } else {
 #pragma unroll 1
@@ -533,7 +551,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 #pragma unroll
             for (int j = 0; j < 32; ++j) v[j] = 0.0f;
           }
-          store_box(warp_smem, box, &tmOut, v, lane, col, static_cast<int32_t>(row0), plane, any_row);
+          store_box<kBoxes>(warp_smem, box, &tmOut, v, lane, col, static_cast<int32_t>(row0), plane, any_row);
         }
       }
       tc_fence_before();
@@ -610,7 +628,7 @@ int launch(const CUtensorMap &a, const CUtensorMap &b, const CUtensorMap &b2, co
   const int pairs = tiles < max_pairs ? tiles : max_pairs;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(2 * pairs, 1, 1);
-  cfg.blockDim = dim3(NUM_THREADS, 1, 1);
+  cfg.blockDim = dim3(num_threads<EPI>(), 1, 1);
   cfg.dynamicSmemBytes = SMEM_BYTES;
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
