@@ -94,3 +94,24 @@ def test_rejects_inputs_of_the_wrong_shape():
     hidden, gate = inputs(16)
     with pytest.raises(ValueError, match="rows, 1, hidden"):
         stack.forward(hidden.reshape(16, H), gate)
+
+
+def test_stack_from_block_files_equals_in_memory(tmp_path):
+    safetensors_torch = pytest.importorskip("safetensors.torch")
+    from vflash_b200.native.h3_weight_files import FP8_BLOCK_KEYS
+
+    blocks = make_blocks(3, seed=300)
+    paths = []
+    for i, block in enumerate(blocks):
+        tensors = {}
+        for name, w in block.items():
+            tensors[FP8_BLOCK_KEYS[name]] = w.codes.cpu().contiguous()
+            tensors[FP8_BLOCK_KEYS[name] + ".row_scale"] = w.row_scale.cpu().contiguous()
+        paths.append(tmp_path / f"block_{i}.safetensors")
+        safetensors_torch.save_file(tensors, str(paths[-1]))
+    hidden, gate = inputs(256)
+    want = direct(blocks, hidden, gate)
+    stack = FP8BlockStack.from_files(paths, H, F, DEV, chunk_bytes=1 << 20)
+    for host in stack.host_blocks:
+        assert host.is_pinned()
+    assert torch.equal(stack.forward(hidden, gate), want)

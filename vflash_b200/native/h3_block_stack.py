@@ -83,6 +83,31 @@ class FP8BlockStack:
         self.ring = FP8BlockRing(self.layout, self.host_blocks, device, group=group, resident=resident)
         self.execution = execution or RowFP8Execution("w8a8")
 
+    @classmethod
+    def from_files(cls, paths, hidden: int, ffn: int, device, *, group=None, resident: bool = False,
+                   chunk_bytes: int = 2 * 1024**3, execution: RowFP8Execution | None = None) -> FP8BlockStack:
+        """A stack whose blocks are read from the reference's per-block safetensors files.
+
+        Each rank reads only its share of every block, straight into pinned
+        memory (``h3_weight_files.pin_fp8_block_files``).
+        """
+        import torch.distributed as dist
+
+        from .h3_weight_files import pin_fp8_block_files
+
+        self = cls.__new__(cls)
+        world = dist.get_world_size(group) if group is not None else 1
+        rank = dist.get_rank(group) if group is not None else 0
+        self.hidden, self.ffn = hidden, ffn
+        self.layout = BlockLayout.for_shapes(block_shapes(hidden, ffn), multiple=ALIGN * world)
+        chunk = self.layout.nbytes // world
+        self.arena = PinnedHostArena(max(chunk_bytes, 1 << (chunk - 1).bit_length()))
+        self.host_blocks = pin_fp8_block_files(paths, self.layout, self.arena, rank=rank, world=world)
+        self.arena.close()
+        self.ring = FP8BlockRing(self.layout, self.host_blocks, device, group=group, resident=resident)
+        self.execution = execution or RowFP8Execution("w8a8")
+        return self
+
     @property
     def weight_bytes_per_block(self) -> int:
         return self.layout.nbytes
