@@ -227,6 +227,11 @@ def run_gpu(args) -> None:
                                 device_id=torch.device("cuda", local_rank))
     device = torch.device("cuda", local_rank)
     torch.cuda.set_device(device)
+    # host buffers (pinned inputs/outputs of e2e, the weight arena) on this GPU's own socket
+    from vflash_b200.native.h3_host_stream import bind_host_to_device
+
+    all_cpus = os.sched_getaffinity(0)
+    host_cpus = bind_host_to_device(device)
 
     def barrier():
         if distributed:
@@ -294,6 +299,7 @@ def run_gpu(args) -> None:
     if rank == 0 and not args.no_other_configs:
         other = other_configs(device, flush, stream,
                               0.0 if args.no_cpu_baseline else min(args.cpu_seconds, 10.0))
+    os.sched_setaffinity(0, all_cpus)  # the CPU baseline may use every host thread
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu = cpu_baseline(x_host, w_codes.cpu(), w_scales.cpu(), bias.cpu(), args.cpu_seconds)
@@ -346,6 +352,7 @@ def run_gpu(args) -> None:
         "clocks": clocks.summary(),
         "wall_s_timed_region": round(wall, 3),
         "device_status": status,
+        "host_cpus_bound": len(host_cpus),
     }
     if e2e_steps:
         line["e2e"] = {"value": round(world * e2e_steps * flop_per_step / (e2e_ms * 1e-3) / 1e12, 2),

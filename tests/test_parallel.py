@@ -218,3 +218,33 @@ def test_row_parallel_adapter_reduces_down_before_up_on_gloo(tmp_path):
     world = 2
     mp.spawn(_adapter_worker, args=(world, _free_port(), str(tmp_path / "a")), nprocs=world)
     assert all(torch.load(tmp_path / f"a.{r}")["ok"] for r in range(world))
+
+
+def test_cpu_set_for_bus_id_decodes_nvml_affinity_masks():
+    from vflash_b200.native.h3_host_stream import cpu_set_for_bus_id
+
+    calls = []
+
+    class FakeNVML:
+        def nvmlInit(self):
+            calls.append("init")
+
+        def nvmlShutdown(self):
+            calls.append("shutdown")
+
+        def nvmlDeviceGetHandleByPciBusId(self, bus_id):
+            calls.append(bus_id)
+            return "handle"
+
+        def nvmlDeviceGetCpuAffinity(self, handle, words):
+            assert handle == "handle" and words >= 1
+            return [0b1011, 1 << 3]
+
+    assert cpu_set_for_bus_id("00000000:1B:00.0", FakeNVML()) == {0, 1, 3, 67}
+    assert calls == ["init", "00000000:1B:00.0", "shutdown"]
+
+    class Failing(FakeNVML):
+        def nvmlDeviceGetHandleByPciBusId(self, bus_id):
+            raise RuntimeError("no such device")
+
+    assert cpu_set_for_bus_id("x", Failing()) == set()

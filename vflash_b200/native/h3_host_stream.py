@@ -14,9 +14,52 @@ device->host copy alone instead of by the sum of both copies and the compute.
 
 from __future__ import annotations
 
+import os
 from collections.abc import Callable, Sequence
 
 import torch
+
+
+def device_bus_id(device) -> str:
+    """NVML-style PCI address (``DDDDDDDD:BB:DD.0``) of a CUDA device."""
+    props = torch.cuda.get_device_properties(torch.device(device))
+    return f"{props.pci_domain_id:08X}:{props.pci_bus_id:02X}:{props.pci_device_id:02X}.0"
+
+
+def cpu_set_for_bus_id(bus_id: str, nvml=None) -> set[int]:
+    """CPUs local to the GPU at ``bus_id`` (NVML's CPU affinity), or an empty set if unknown.
+
+    ``nvml`` defaults to the ``pynvml`` module; finding the device by PCI
+    address keeps the mapping right under any ``CUDA_VISIBLE_DEVICES``.
+    """
+    if nvml is None:
+        try:
+            import pynvml as nvml
+        except ImportError:
+            return set()
+    try:
+        nvml.nvmlInit()
+        try:
+            handle = nvml.nvmlDeviceGetHandleByPciBusId(bus_id)
+            masks = nvml.nvmlDeviceGetCpuAffinity(handle, (os.cpu_count() + 63) // 64)
+        finally:
+            nvml.nvmlShutdown()
+    except Exception:
+        return set()
+    return {64 * w + b for w, mask in enumerate(masks) for b in range(64) if (int(mask) >> b) & 1}
+
+
+def bind_host_to_device(device, nvml=None) -> set[int]:
+    """Run this process on the CPUs local to ``device`` (returns them; no-op if unknown).
+
+    Pinned buffers allocated afterwards are first touched by a thread on the
+    GPU's own socket, so host<->device copies do not cross the socket link.
+    Only this process's CPU affinity changes.
+    """
+    cpus = cpu_set_for_bus_id(device_bus_id(device), nvml) & set(os.sched_getaffinity(0))
+    if cpus:
+        os.sched_setaffinity(0, cpus)
+    return cpus
 
 
 def plan_chunks(rows: int, chunk_rows: int, align: int = 16) -> list[tuple[int, int]]:
