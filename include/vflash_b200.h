@@ -50,6 +50,14 @@ VFB_API const char *vfb_version(void);
  * return instead of hanging.  Synchronises the device. */
 VFB_API int vfb_device_status(int *status, int clear);
 
+/* Bounded-wait self-test: launches one thread that waits on a barrier nothing
+ * completes; the wait gives up after timeout_ns (1 ms .. 10 s), records
+ * VFB_ETIMEOUT in the device status word (read it with vfb_device_status) and
+ * the kernel ends normally, leaving the context usable.  No reference
+ * counterpart: it exercises the failure path every pipeline wait of the GEMMs
+ * takes (their limit is 4 s) without stalling a real kernel. */
+VFB_API int vfb_wait_selftest(int64_t timeout_ns, void *stream);
+
 /* ---- FP8 per-token activation quantisation -------------------------------
  * Replaces quantize_activation / _rows_fp8
  * (src/vflash/native/h3_fp8_activation.py:13-55) and the portable expression

@@ -67,6 +67,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "vfb_last_error": (ctypes.c_char_p, []),
     "vfb_version": (ctypes.c_char_p, []),
     "vfb_device_status": (ctypes.c_int, [ctypes.POINTER(ctypes.c_int), ctypes.c_int]),
+    "vfb_wait_selftest": (ctypes.c_int, [_c_int64, _vp]),
     "vfb_fp8_quant_rows": (
         ctypes.c_int,
         [_vp, _c_int64, _c_int64, _c_int64, _vp, _vp, _c_int64, _vp],

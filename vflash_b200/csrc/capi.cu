@@ -110,3 +110,38 @@ extern "C" int vfb_device_status(int *status, int clear) {
   }
   return VFB_OK;
 }
+
+// ---------------------------------------------------------------------------
+// Bounded-wait self-test: one thread waits on an mbarrier that nothing ever
+// arrives at.  The wait gives up after timeout_ns, records VFB_ETIMEOUT in the
+// device status word and the kernel returns normally (no trap, no fault), so
+// the context stays usable; this is the path every pipeline wait in the GEMMs
+// takes when a peer role stops making progress.
+// ---------------------------------------------------------------------------
+namespace vfb {
+namespace {
+__global__ void wait_selftest_kernel(uint64_t timeout_ns, int *status) {
+  __shared__ __align__(8) uint64_t bar;
+  __shared__ int abort_flag;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    abort_flag = 0;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) mbar_wait_for(&bar, 0, &abort_flag, status, timeout_ns);
+}
+}  // namespace
+}  // namespace vfb
+
+extern "C" int vfb_wait_selftest(int64_t timeout_ns, void *stream) {
+  using namespace vfb;
+  if (timeout_ns < 1000000 || timeout_ns > 10000000000ll)
+    return set_error(VFB_EINVAL, "vfb_wait_selftest: timeout must be 1 ms .. 10 s");
+  int rc = check_device(nullptr);
+  if (rc != VFB_OK) return rc;
+  wait_selftest_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(static_cast<uint64_t>(timeout_ns),
+                                                                       device_status_ptr());
+  cudaError_t err = cudaGetLastError();
+  if (err != cudaSuccess) return set_error(VFB_ECUDA, "vfb_wait_selftest launch: %s", cudaGetErrorString(err));
+  return VFB_OK;
+}

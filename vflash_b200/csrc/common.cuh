@@ -69,21 +69,26 @@ __device__ __forceinline__ void record_status(int *status, int code) {
 
 // Wait until the phase with the given parity has completed.  Returns false if
 // the wait expired or another role of this CTA already gave up (`abort_flag`).
-__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, volatile int *abort_flag,
-                                          int *status) {
+__device__ __forceinline__ bool mbar_wait_for(uint64_t *bar, uint32_t parity, volatile int *abort_flag,
+                                              int *status, uint64_t timeout_ns) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t start = global_timer_ns();
   for (uint32_t spin = 1;; ++spin) {
     if (mbar_try_wait(bar, parity)) return true;
     if ((spin & 255u) == 0) {
       if (*abort_flag) return false;
-      if (global_timer_ns() - start > VFB_WAIT_TIMEOUT_NS) {
+      if (global_timer_ns() - start > timeout_ns) {
         *abort_flag = 1;
         record_status(status, VFB_ETIMEOUT);
         return false;
       }
     }
   }
+}
+
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, volatile int *abort_flag,
+                                          int *status) {
+  return mbar_wait_for(bar, parity, abort_flag, status, VFB_WAIT_TIMEOUT_NS);
 }
 
 // ---- TMA ------------------------------------------------------------------
