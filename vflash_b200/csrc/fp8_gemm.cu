@@ -200,64 +200,50 @@ __device__ __forceinline__ void store_value(float (&v)[32], float sa, const floa
   }
 }
 
-__device__ __forceinline__ void bf16r_pair(float &x, float &y) {
-  const float2 f = __bfloat1622float2(__floats2bfloat162_rn(x, y));
-  x = f.x;
-  y = f.y;
-}
-
-// QK-norm + rotary of one head held as two 32-column halves of each rotary
-// half: a = columns [32k, 32k+32), b = columns [64+32k, 64+32k+32) of the
-// head, k in {0, 1}.  w / cos / sin point at the head's column 0.
-__device__ __forceinline__ void unpack4(const uint2 &u, float (&f)[4]) {
-  const __nv_bfloat162 *h = reinterpret_cast<const __nv_bfloat162 *>(&u);
-  const float2 t0 = __bfloat1622float2(h[0]);
-  const float2 t1 = __bfloat1622float2(h[1]);
-  f[0] = t0.x;
-  f[1] = t0.y;
-  f[2] = t1.x;
-  f[3] = t1.y;
-}
 
 __device__ __forceinline__ uint2 ld4(const __nv_bfloat16 *p) { return __ldg(reinterpret_cast<const uint2 *>(p)); }
 
-// QK-norm + rotary of one head held as two 32-column halves of each rotary
-// half: a = columns [32k, 32k+32), b = columns [64+32k, 64+32k+32) of the
-// head, k in {0, 1}.  w / cos / sin point at the head's column 0.  Works four
-// columns at a time to bound the live registers.
-__device__ __forceinline__ void qk_norm_rope_pair(float (&a)[32], float (&b)[32], float rstd, int k,
-                                                  const __nv_bfloat16 *w, const __nv_bfloat16 *cs,
-                                                  const __nv_bfloat16 *sn) {
+__device__ __forceinline__ __nv_bfloat162 as_bf162(uint32_t u) { return *reinterpret_cast<__nv_bfloat162 *>(&u); }
+
+// Exact packing of two bf16-representable floats (their low 16 bits are zero).
+__device__ __forceinline__ uint32_t pack_exact_bf16x2(float lo, float hi) {
+  return __byte_perm(__float_as_uint(lo), __float_as_uint(hi), 0x7632);
+}
+
+// QK-norm + rotary output of one 32-column chunk of a head (k in 0..3) from
+// the head's 128 bf16 values packed in hp[64] (hp[i] = columns 2i, 2i+1):
+//   n = bf16((x * rstd) * w)                      fp32 products, one rounding
+//   out[d] = bf16(bf16(n[d] * cos[d]) + bf16(partner[d] * sin[d]))
+//   partner[d] = -n[d + 64] for d < 64, n[d - 64] otherwise.
+// The rotary products are bf16 x bf16, exact in fp32, so rounding the fp32
+// product equals one mul.rn.bf16x2 of the packed operands; the sum stays fp32
+// and is rounded at the store, as in the reference.
+__device__ __forceinline__ void qk_norm_rope_chunk(const uint32_t (&hp)[64], float rstd, int k,
+                                                   const __nv_bfloat16 *w, const __nv_bfloat16 *cs,
+                                                   const __nv_bfloat16 *sn, float (&out)[32]) {
   const uint2 one = make_uint2(0x3f803f80u, 0x3f803f80u);
+  const int kp = k ^ 2;  // the partner chunk (64 columns away)
+  const bool first = k < 2;
 #pragma unroll
   for (int g = 0; g < 8; ++g) {
-    const int da = 32 * k + 4 * g;  // column of a[4g] in the head
-    const int db = da + 64;
-    float wa[4], wb[4], ca[4], sa[4], cb[4], sb[4];
-    unpack4(w ? ld4(w + da) : one, wa);
-    unpack4(w ? ld4(w + db) : one, wb);
-    unpack4(ld4(cs + da), ca);
-    unpack4(ld4(sn + da), sa);
-    unpack4(ld4(cs + db), cb);
-    unpack4(ld4(sn + db), sb);
+    const int d = 32 * k + 4 * g;   // this chunk's columns d .. d+3
+    const int dp = 32 * kp + 4 * g;  // partner columns
+    const uint2 wv = w ? ld4(w + d) : one, wp = w ? ld4(w + dp) : one;
+    const uint2 cv = ld4(cs + d), sv = ld4(sn + d);
+    const uint32_t ww[2] = {wv.x, wv.y}, wpw[2] = {wp.x, wp.y}, cw[2] = {cv.x, cv.y}, sw[2] = {sv.x, sv.y};
 #pragma unroll
-    for (int e = 0; e < 4; e += 2) {
-      // n = bf16((x * rstd) * w)
-      float na0 = (a[4 * g + e] * rstd) * wa[e], na1 = (a[4 * g + e + 1] * rstd) * wa[e + 1];
-      float nb0 = (b[4 * g + e] * rstd) * wb[e], nb1 = (b[4 * g + e + 1] * rstd) * wb[e + 1];
-      bf16r_pair(na0, na1);
-      bf16r_pair(nb0, nb1);
-      // first half: n*cos + (-n[d+64])*sin; second half: n*cos + n[d-64]*sin
-      float ac0 = na0 * ca[e], ac1 = na1 * ca[e + 1], as0 = -nb0 * sa[e], as1 = -nb1 * sa[e + 1];
-      float bc0 = nb0 * cb[e], bc1 = nb1 * cb[e + 1], bs0 = na0 * sb[e], bs1 = na1 * sb[e + 1];
-      bf16r_pair(ac0, ac1);
-      bf16r_pair(as0, as1);
-      bf16r_pair(bc0, bc1);
-      bf16r_pair(bs0, bs1);
-      a[4 * g + e] = ac0 + as0;
-      a[4 * g + e + 1] = ac1 + as1;
-      b[4 * g + e] = bc0 + bs0;
-      b[4 * g + e + 1] = bc1 + bs1;
+    for (int h = 0; h < 2; ++h) {
+      const float2 x = __bfloat1622float2(as_bf162(hp[16 * k + 2 * g + h]));
+      const float2 xp = __bfloat1622float2(as_bf162(hp[16 * kp + 2 * g + h]));
+      const float2 fw = __bfloat1622float2(as_bf162(ww[h]));
+      const float2 fwp = __bfloat1622float2(as_bf162(wpw[h]));
+      const __nv_bfloat162 n = __floats2bfloat162_rn((x.x * rstd) * fw.x, (x.y * rstd) * fw.y);
+      __nv_bfloat162 np = __floats2bfloat162_rn((xp.x * rstd) * fwp.x, (xp.y * rstd) * fwp.y);
+      if (first) np = __hneg2(np);
+      const float2 c = __bfloat1622float2(__hmul2(n, as_bf162(cw[h])));
+      const float2 sp = __bfloat1622float2(__hmul2(np, as_bf162(sw[h])));
+      out[4 * g + 2 * h] = c.x + sp.x;
+      out[4 * g + 2 * h + 1] = c.y + sp.y;
     }
   }
 }
@@ -460,16 +446,24 @@ __global__ void __launch_bounds__(num_threads<EPI>(), 1)
                                 plane, any_row);
             }
         } else {
-          // pass 1: this thread's row of the head, sum of squares in fp32
+          // pass 1: this thread's row of the head (bf16 values, packed), sum of squares in fp32
+          uint32_t hp[64];
           float ss = 0.0f;
-#pragma unroll 1
+#pragma unroll
           for (int k = 0; k < 4; ++k) {
             float v[32];
             tmem_ld_32x32b_x32(t_head + k * 32, v);
             if (live) {
               store_value(v, sa, p.sw, ep, n0 + 32 * k, plane, col0 + 32 * k, m);
+            } else {
 #pragma unroll
-              for (int j = 0; j < 32; ++j) ss = fmaf(v[j], v[j], ss);
+              for (int j = 0; j < 32; ++j) v[j] = 0.0f;
+            }
+#pragma unroll
+            for (int j = 0; j < 32; j += 2) {
+              ss = fmaf(v[j], v[j], ss);
+              ss = fmaf(v[j + 1], v[j + 1], ss);
+              hp[16 * k + j / 2] = pack_exact_bf16x2(v[j], v[j + 1]);
             }
           }
           const float mean_eps = __fadd_rn(__fdiv_rn(ss, 128.0f), ep.qk_eps);
@@ -478,24 +472,19 @@ __global__ void __launch_bounds__(num_threads<EPI>(), 1)
           const int64_t token = live ? m % ep.tokens : 0;
           const __nv_bfloat16 *cs = ep.rope_cos + token * ep.rope_ts;
           const __nv_bfloat16 *sn = ep.rope_sin + token * ep.rope_ts;
-          // pass 2: the two rotary halves of the head, 32 columns at a time
-#pragma unroll 1
-          for (int k = 0; k < 2; ++k) {
-            float a[32], b[32];
-            tmem_ld_32x32b_x32(t_head + k * 32, a);
-            tmem_ld_32x32b_x32(t_head + (k + 2) * 32, b);
+          // pass 2: norm + rotary from registers, one 32-column chunk at a time
+          // (unrolled: hp is indexed with compile-time positions only)
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            float o[32];
             if (live) {
-              store_value(a, sa, p.sw, ep, n0 + 32 * k, plane, col0 + 32 * k, m);
-              store_value(b, sa, p.sw, ep, n0 + 32 * (k + 2), plane, col0 + 32 * (k + 2), m);
-              qk_norm_rope_pair(a, b, rstd, k, w, cs, sn);
+              qk_norm_rope_chunk(hp, rstd, k, w, cs, sn, o);
             } else {
 #pragma unroll
-              for (int j = 0; j < 32; ++j) a[j] = b[j] = 0.0f;
+              for (int j = 0; j < 32; ++j) o[j] = 0.0f;
             }
-            store_box<kBoxes>(warp_smem, box, &tmOut, a, lane, col0 + 32 * k, static_cast<int32_t>(row0), plane,
-                      any_row);
-            store_box<kBoxes>(warp_smem, box, &tmOut, b, lane, col0 + 32 * (k + 2), static_cast<int32_t>(row0), plane,
-                      any_row);
+            store_box<kBoxes>(warp_smem, box, &tmOut, o, lane, col0 + 32 * k, static_cast<int32_t>(row0), plane,
+                              any_row);
           }
         }
       } else if (EPI == VFB_EPI_SWIGLU) {
