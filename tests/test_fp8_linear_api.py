@@ -125,3 +125,10 @@ def test_known_answer_ones_times_ones_is_sixteen():
     scales = torch.ones(4, 1)
     out = RowFP8Execution("weight-only").linear(torch.ones(2, 16), codes, scales)
     assert torch.equal(out, torch.full((2, 4), 16.0))
+
+
+def test_reference_named_torch_quantiser_refuses_the_host():
+    from vflash_b200.native.h3_fp8_linear import _quantize_activation_torch
+
+    with pytest.raises(ValueError, match="SM100"):
+        _quantize_activation_torch(torch.zeros(4, 16, dtype=torch.bfloat16))

@@ -124,3 +124,13 @@ def test_drop_in_refuses_unbounded_widths():
         quantize_activation(torch.zeros(4, 8, dtype=torch.bfloat16, device=DEV))
     with pytest.raises(ValueError, match="SM100"):
         quantize_activation(torch.zeros(4, 64, dtype=torch.float32, device=DEV))
+
+
+def test_reference_named_torch_quantiser_matches_the_oracle():
+    from vflash_b200.native.h3_fp8_linear import _quantize_activation_torch
+
+    x = outlier_activations(37, 320, 21).to(DEV)
+    codes, scales = _quantize_activation_torch(x)
+    want_codes, want_scales = fp8.quantize_activation(bits_of(x))
+    np.testing.assert_array_equal(codes_of(codes), want_codes)
+    np.testing.assert_array_equal(scales.cpu().numpy().view(np.uint32), want_scales.view(np.uint32))

@@ -73,6 +73,18 @@ class QKNormRope:
     eps: float = 1e-5
 
 
+def _quantize_activation_torch(matrix):
+    """The reference's per-token quantiser (h3_fp8_linear.py:18-31), same outputs, on SM100.
+
+    Codes e4m3 ``[ceil16(M), K]`` and fp32 scales ``[ceil16(M), 1]`` of a bf16
+    ``[M, K]`` matrix, computed by the native quantiser, which reproduces the
+    reference expression bit for bit.  Raises for other devices (no host path).
+    """
+    if not isinstance(matrix, torch.Tensor) or not _on_sm100(matrix.device) or matrix.dtype != torch.bfloat16:
+        raise ValueError("the FP8 activation quantiser requires an SM100 (B200) BF16 matrix")
+    return quantize_fp8_rows(matrix, pad_to=16)
+
+
 def _on_sm100(device: torch.device) -> bool:
     return device.type == "cuda" and torch.cuda.get_device_capability(device) == (10, 0)
 
