@@ -90,3 +90,29 @@ def test_missing_library_fails_loudly(monkeypatch, tmp_path):
     monkeypatch.setattr(_lib, "_handle", None)
     with pytest.raises(_lib.NativeLibraryError, match="missing"):
         _lib.load()
+
+
+def test_new_entry_points_reject_bad_arguments_before_any_launch():
+    lib = _lib.load()
+    # fused norm + modulate + quantise: K % 8, tokens, eps, M_pad
+    assert lib.vfb_fp8_norm_modulate_quant(None, 4, 12, 12, None, 1e-6, None, 0, None, 0, 1, None, None, 16,
+                                           None) == _lib.VFB_EINVAL
+    assert "vfb_fp8_norm_modulate_quant" in _lib.last_error()
+    assert lib.vfb_fp8_norm_modulate_quant(None, 4, 64, 64, None, 1e-6, None, 0, None, 0, 0, None, None, 16,
+                                           None) == _lib.VFB_EINVAL
+    assert lib.vfb_fp8_norm_modulate_quant(None, 4, 64, 64, None, -1.0, None, 0, None, 0, 1, None, None, 16,
+                                           None) == _lib.VFB_EINVAL
+    assert lib.vfb_fp8_norm_modulate_quant(None, 20, 64, 64, None, 1e-6, None, 0, None, 0, 1, None, None, 16,
+                                           None) == _lib.VFB_EINVAL
+    # modulate / rotary: widths, tokens, rotary dimension
+    assert lib.vfb_modulate(None, None, 0, None, 0, 4, 1, 12, None, None) == _lib.VFB_EINVAL
+    assert lib.vfb_modulate(None, None, 0, None, 0, 4, 0, 16, None, None) == _lib.VFB_EINVAL
+    assert lib.vfb_rotary(None, None, 0, None, 0, 4, 1, 2, 128, 130, None, None) == _lib.VFB_EINVAL
+    assert lib.vfb_rotary(None, None, 0, None, 0, 4, 1, 2, 128, 63, None, None) == _lib.VFB_EINVAL
+    assert "rotary_dim" in _lib.last_error()
+    # bounded-wait self-test: limit range
+    assert lib.vfb_wait_selftest(10, None) == _lib.VFB_EINVAL
+    # QKV + QK-norm + rotary epilogue needs its tables
+    ep = _lib.Epilogue()
+    ep.kind = _lib.EPI_QKV_NORM_ROPE
+    assert lib.vfb_fp8_gemm(None, 64, None, None, 64, None, 4, 384, 64, ctypes.byref(ep), None) == _lib.VFB_EINVAL
