@@ -231,7 +231,7 @@ def run_gpu(args) -> None:
     from vflash_b200.native.h3_host_stream import bind_host_to_device
 
     all_cpus = os.sched_getaffinity(0)
-    host_cpus = bind_host_to_device(device)
+    host_cpus = set() if args.no_numa_bind else bind_host_to_device(device)
 
     def barrier():
         if distributed:
@@ -818,6 +818,8 @@ def main() -> None:
     parser.add_argument("--no-e2e", action="store_true")
     parser.add_argument("--no-stack", action="store_true", help="skip the config 4 block stack")
     parser.add_argument("--e2e-chunk-rows", type=int, default=4096)
+    parser.add_argument("--no-numa-bind", action="store_true",
+                        help="keep the process on all host CPUs (default: the GPU's local CPUs)")
     parser.add_argument("--stack-blocks", type=int, default=STACK_BLOCKS)
     parser.add_argument("--stack-steps", type=int, default=2)
     parser.add_argument("--no-other-configs", action="store_true",
