@@ -8,19 +8,26 @@
 // eager/Triton sequences is kept: the GEMM result is rounded to BF16 first,
 // then each elementwise step rounds where the reference rounds.
 //
-// Structure (one persistent CTA per SM, 192 threads):
-//   warp 0      TMA producer: A tile 128x128 B and B tile 256x128 B per stage
-//               (128-byte swizzle) into a STAGES-deep shared-memory ring.
-//   warp 1      allocates 512 TMEM columns (two 128x256 fp32 accumulators) and
-//               one elected lane issues tcgen05.mma kind::f8f6f4 (M=128,
-//               N=256, K=32; four per stage), committing each stage back to
-//               the producer and each finished tile to the epilogue.
-//   warps 2-5   epilogue: tcgen05.ld 32 columns at a time (warp w reads TMEM
-//               lanes 32*(w%4)..+31 = tile rows), apply scales / bias /
-//               activation / residual in registers and store BF16 rows with
-//               16-byte stores.  The second accumulator lets the epilogue of
-//               tile i overlap the main loop of tile i+1.
-// Tiles are visited with the N index fastest so that the CTAs running at the
+// Structure: persistent CTA pairs (2-CTA clusters, one CTA per SM), one
+// 256 x 256 output tile per pair at a time, K staged 128 bytes per stage.
+//   warp 0      TMA producer in both CTAs: its own 128 A rows and 128 of the
+//               tile's 256 weight rows per stage (128-byte swizzle, weights with
+//               an evict_last L2 policy) into a 5-deep shared-memory ring; the
+//               bytes of both CTAs complete on the leader's full barrier.
+//   warp 1      allocates 512 TMEM columns per CTA (two 256-column fp32
+//               accumulators); in the leader CTA the whole warp runs the issue
+//               loop and one elected lane issues tcgen05.mma.cta_group::2
+//               kind::f8f6f4 (M=256, N=256, K=32; four per stage), committing
+//               each stage to both CTAs' empty barriers and each finished tile to
+//               both CTAs' epilogues.
+//   warps 2-5   epilogue (2-9 for QKV_NORM_ROPE, one group of four per head):
+//               tcgen05.ld 32 columns at a time (warp w reads TMEM lanes
+//               32*(w%4)..+31 = tile rows), scales / bias / activation /
+//               residual / QK-norm + rotary in registers, 32 x 32 bf16 boxes
+//               staged in 64-byte-swizzled shared memory and written by TMA
+//               stores (evict_first).  The second accumulator lets the epilogue
+//               of tile i overlap the main loop of tile i+1.
+// Tiles are visited with the N index fastest so that the pairs running at the
 // same time share one A row-block and stream the weight through L2.
 // No TMA multicast is used: every CTA loads its own operands.
 #include <cudaTypedefs.h>

@@ -12,8 +12,9 @@
 // loads its own 128 A rows and 128 of the tile's 256 weight rows (128-byte
 // swizzle, no multicast), its A rows' scale blocks and the scale blocks of all
 // 256 weight rows (512-byte blocks in the 128x4 layout, loaded through 2-D
-// tensor maps over those blocks so that rows past the end read as zero).  The
-// leader's MMA thread moves each K = 64 block's scales into both CTAs' TMEM
+// tensor maps over those blocks so that rows past the end read as zero).  One
+// elected lane of the leader's converged MMA warp moves each K = 64 block's
+// scales into both CTAs' TMEM
 // with tcgen05.cp.cta_group::2.32x128b.warpx4 and issues
 // tcgen05.mma.cta_group::2.kind::mxf4nvf4.block_scale.block16 (M = 256,
 // N = 256, K = 64).  TMEM per CTA: two 256-column accumulators overlapping by
