@@ -663,7 +663,15 @@ def stack_config(args, device, rank: int, world: int, barrier, max_over_ranks) -
     resident_ms, out2 = timed(
         lambda h, g: resident_ring.run(h, lambda w, x: block_linears(stack.execution, w, x, g)), steps)
     same = bool(torch.equal(out, out2))
-    del resident_ring, out, out2
+    # the same resident stack replayed from one CUDA graph (no per-block host work)
+    import copy
+
+    graphed = copy.copy(stack)
+    graphed.ring = resident_ring
+    replay = graphed.capture(shard, gate)
+    graph_ms, out3 = timed(lambda h, g: replay(), steps)
+    graph_same = bool(torch.equal(out3, out2))
+    del resident_ring, out, out2, out3, replay, graphed
     torch.cuda.empty_cache()
     peaks = measured_peaks()
     fp8_peak = 2.0 * float(peaks.get("bf16_tflops_sustained", peaks.get("bf16_tflops", 1400.0)))
@@ -675,6 +683,8 @@ def stack_config(args, device, rank: int, world: int, barrier, max_over_ranks) -
                     f"GELU-tanh, down [4096,16384]); M={STACK_TOKENS} tokens, {rows} per rank",
         "streamed_ms_per_step": round(streamed_ms, 2),
         "resident_ms_per_step": round(resident_ms, 2),
+        "resident_graph_ms_per_step": round(graph_ms, 2),
+        "graph_equals_eager": graph_same,
         "streaming_overhead": round(streamed_ms / resident_ms - 1.0, 4),
         "tflops_whole_job": round(flop_step / (streamed_ms * 1e-3) / 1e12, 1),
         "tflops_per_gpu": round(per_gpu_tflops, 1),

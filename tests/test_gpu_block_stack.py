@@ -115,3 +115,19 @@ def test_stack_from_block_files_equals_in_memory(tmp_path):
     for host in stack.host_blocks:
         assert host.is_pinned()
     assert torch.equal(stack.forward(hidden, gate), want)
+
+
+def test_graph_replay_of_a_resident_stack_equals_eager():
+    blocks = make_blocks(3, seed=400)
+    hidden, gate = inputs(512)
+    want = direct(blocks, hidden, gate)
+    stack = FP8BlockStack(blocks, H, F, DEV, resident=True, chunk_bytes=1 << 20)
+    replay = stack.capture(hidden, gate)
+    assert torch.equal(replay(), want)
+    # a replay reads the current input: new values give the new eager result
+    hidden.copy_(inputs(512)[0] * 0.5)
+    want2 = direct(blocks, hidden, gate)
+    assert torch.equal(replay(), want2)
+    streamed = FP8BlockStack(blocks, H, F, DEV, chunk_bytes=1 << 20)
+    with pytest.raises(ValueError, match="resident"):
+        streamed.capture(hidden, gate)

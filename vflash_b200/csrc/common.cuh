@@ -494,6 +494,9 @@ __device__ __forceinline__ uint16_t pack_e4m3x2(float lo, float hi) {
 
 }  // namespace vfb
 
+// Devices whose per-device kernel attributes are cached (others set them per launch).
+constexpr int kMaxAttrDevices = 64;
+
 // Host-side helpers implemented in capi.cu.
 #include <cudaTypedefs.h>
 namespace vfb {

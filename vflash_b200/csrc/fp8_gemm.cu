@@ -32,6 +32,8 @@
 // No TMA multicast is used: every CTA loads its own operands.
 #include <cudaTypedefs.h>
 
+#include <atomic>
+
 #include <mutex>
 
 #include "common.cuh"
@@ -614,10 +616,17 @@ template <int EPI>
 int launch(const CUtensorMap &a, const CUtensorMap &b, const CUtensorMap &b2, const CUtensorMap &o,
            const GemmParams &p, int sm_count, cudaStream_t stream) {
   auto kernel = fp8_gemm_kernel<EPI>;
-  cudaError_t err =
-      cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
-  if (err != cudaSuccess)
-    return set_error(VFB_ECUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(err));
+  // the shared-memory opt-in is a per-device function attribute: set it once
+  static std::atomic<bool> smem_set[kMaxAttrDevices];
+  int dev = 0;
+  cudaError_t err = cudaGetDevice(&dev);
+  if (err != cudaSuccess) return set_error(VFB_ECUDA, "cudaGetDevice: %s", cudaGetErrorString(err));
+  if (dev < 0 || dev >= kMaxAttrDevices || !smem_set[dev].load(std::memory_order_acquire)) {
+    err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+    if (err != cudaSuccess)
+      return set_error(VFB_ECUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(err));
+    if (dev >= 0 && dev < kMaxAttrDevices) smem_set[dev].store(true, std::memory_order_release);
+  }
   // Persistent grid of CTA pairs, one CTA per SM.
   const int tiles = p.num_m_tiles * p.num_n_tiles;
   const int max_pairs = sm_count / 2;

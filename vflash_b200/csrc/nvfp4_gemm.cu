@@ -23,6 +23,8 @@
 // for even tiles, forward for odd) and then lets the next tile's MMAs start.
 #include <cudaTypedefs.h>
 
+#include <atomic>
+
 #include "common.cuh"
 
 namespace vfb {
@@ -398,9 +400,16 @@ extern "C" int vfb_nvfp4_gemm(const void *A, const void *sfa, const void *W, con
                    CU_TENSOR_MAP_SWIZZLE_NONE)) != VFB_OK)
     return rc;
   if ((rc = map_out(&to, out, N / planes, M, planes)) != VFB_OK) return rc;
-  cudaError_t err =
-      cudaFuncSetAttribute(nvfp4_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
-  if (err != cudaSuccess) return set_error(VFB_ECUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(err));
+  // the shared-memory opt-in is a per-device function attribute: set it once
+  static std::atomic<bool> smem_set[kMaxAttrDevices];
+  int dev = 0;
+  cudaError_t err = cudaGetDevice(&dev);
+  if (err != cudaSuccess) return set_error(VFB_ECUDA, "cudaGetDevice: %s", cudaGetErrorString(err));
+  if (dev < 0 || dev >= kMaxAttrDevices || !smem_set[dev].load(std::memory_order_acquire)) {
+    err = cudaFuncSetAttribute(nvfp4_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+    if (err != cudaSuccess) return set_error(VFB_ECUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(err));
+    if (dev >= 0 && dev < kMaxAttrDevices) smem_set[dev].store(true, std::memory_order_release);
+  }
   const int tiles = p.num_m_tiles * p.num_n_tiles;
   const int max_pairs = sms / 2;
   const int pairs = tiles < max_pairs ? tiles : max_pairs;

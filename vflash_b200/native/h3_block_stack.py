@@ -112,6 +112,30 @@ class FP8BlockStack:
     def weight_bytes_per_block(self) -> int:
         return self.layout.nbytes
 
+    def capture(self, hidden: torch.Tensor, gate: torch.Tensor):
+        """CUDA graph of ``forward`` over a resident stack; returns ``replay() -> output``.
+
+        The stack runs once eagerly first (loading every block and setting up
+        the kernels), then the block loop is captured; a replay reads the
+        current contents of ``hidden`` and ``gate`` and rewrites the returned
+        output tensor.  One graph launch replaces the per-block host work of
+        issuing 8 kernels per block.
+        """
+        if not self.ring.resident:
+            raise ValueError("graph capture needs a resident stack")
+        self.forward(hidden, gate)
+        torch.cuda.synchronize(self.ring.device)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            out = self.ring.run(hidden, lambda w, h: block_linears(self.execution, w, h, gate), wait_ready=False)
+
+        def replay() -> torch.Tensor:
+            graph.replay()
+            return out
+
+        replay.graph = graph
+        return replay
+
     def forward(self, hidden: torch.Tensor, gate: torch.Tensor) -> torch.Tensor:
         if hidden.ndim != 3 or hidden.shape[1] != 1 or hidden.shape[2] != self.hidden:
             raise ValueError("block stack input must be bf16 [rows, 1, hidden]")

@@ -208,18 +208,26 @@ class FP8BlockRing:
             self.h2d_bytes += self.chunk
             self.ready[slot].record(self.copy_stream)
 
-    def run(self, hidden: torch.Tensor, block_fn: Callable[[dict[str, FP8Weight], torch.Tensor], torch.Tensor]):
+    def run(self, hidden: torch.Tensor, block_fn: Callable[[dict[str, FP8Weight], torch.Tensor], torch.Tensor],
+            *, wait_ready: bool = True):
+        """Apply ``block_fn`` block by block; ``wait_ready=False`` (resident and already loaded
+        and synchronised only) skips the copy-stream events, as a CUDA graph capture needs."""
         compute = torch.cuda.current_stream(self.device)
         n = len(self.host_blocks)
         if self.resident:
+            if not wait_ready and not all(self.loaded):
+                raise ValueError("skipping the ready events needs every resident block loaded")
             for i in range(n):
                 if not self.loaded[i]:
                     self._fetch(i, i)
                     self.loaded[i] = True
             for i in range(n):
-                compute.wait_event(self.ready[i])
+                if wait_ready:
+                    compute.wait_event(self.ready[i])
                 hidden = block_fn(self.slot_views[i], hidden)
             return hidden
+        if not wait_ready:
+            raise ValueError("a streamed stack always orders its copies with events")
         for i in range(min(2, n)):
             self._fetch(i, i)
         for i in range(n):
