@@ -131,3 +131,16 @@ def test_graph_replay_of_a_resident_stack_equals_eager():
     streamed = FP8BlockStack(blocks, H, F, DEV, chunk_bytes=1 << 20)
     with pytest.raises(ValueError, match="resident"):
         streamed.capture(hidden, gate)
+
+
+@pytest.mark.parametrize("count,resident_blocks", [(5, 2), (4, 3), (3, 1), (2, 2)])
+def test_partially_resident_stack_equals_direct(count, resident_blocks):
+    blocks = make_blocks(count, seed=500)
+    hidden, gate = inputs(300)
+    want = direct(blocks, hidden, gate)
+    stack = FP8BlockStack(blocks, H, F, DEV, resident_blocks=resident_blocks, chunk_bytes=1 << 20)
+    for _ in range(3):
+        assert torch.equal(stack.forward(hidden, gate), want)
+    torch.cuda.synchronize()
+    streamed = count - resident_blocks
+    assert stack.ring.h2d_bytes == (resident_blocks + 3 * streamed) * stack.weight_bytes_per_block

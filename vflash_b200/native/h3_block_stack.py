@@ -66,7 +66,7 @@ class FP8BlockStack:
     """
 
     def __init__(self, blocks: Iterable[dict[str, FP8Weight]], hidden: int, ffn: int, device, *,
-                 group=None, resident: bool = False, chunk_bytes: int = 2 * 1024**3,
+                 group=None, resident: bool = False, resident_blocks: int = 0, chunk_bytes: int = 2 * 1024**3,
                  execution: RowFP8Execution | None = None) -> None:
         import torch.distributed as dist
 
@@ -80,7 +80,8 @@ class FP8BlockStack:
         self.arena = PinnedHostArena(slab)
         self.host_blocks = pin_blocks(self.layout, blocks, self.arena, rank=rank, world=world)
         self.arena.close()  # the views keep their slabs; no further allocations
-        self.ring = FP8BlockRing(self.layout, self.host_blocks, device, group=group, resident=resident)
+        self.ring = FP8BlockRing(self.layout, self.host_blocks, device, group=group, resident=resident,
+                                 resident_blocks=resident_blocks)
         self.execution = execution or RowFP8Execution("w8a8")
 
     @classmethod

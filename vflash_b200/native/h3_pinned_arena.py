@@ -21,7 +21,9 @@ choices:
   together holds one copy of the weights.
 
 ``resident=True`` instead keeps every block on the device after its first
-copy (a stack of 48 H3 blocks is 9.7 GB of FP8 weights; B200 has 180 GB).
+copy (a stack of 48 H3 blocks is 9.7 GB of FP8 weights; B200 has 180 GB), and
+``resident_blocks=R`` keeps the first R resident and streams the rest, which
+lowers the host bandwidth the ring needs when several GPUs share the host.
 """
 
 from __future__ import annotations
@@ -173,7 +175,7 @@ class FP8BlockRing:
     """
 
     def __init__(self, layout: BlockLayout, host_blocks: list[torch.Tensor], device: torch.device, *,
-                 group=None, resident: bool = False) -> None:
+                 group=None, resident: bool = False, resident_blocks: int = 0) -> None:
         import torch.distributed as dist
 
         self.layout = layout
@@ -188,8 +190,12 @@ class FP8BlockRing:
         for b in host_blocks:
             if b.dtype != torch.uint8 or b.numel() != self.chunk:
                 raise ValueError("host block buffers differ from the packed layout")
-        self.resident = resident
-        count = len(host_blocks) if resident else min(2, len(host_blocks))
+        n = len(host_blocks)
+        # blocks [0, resident_count) stay on the device after their first copy;
+        # the rest stream through two slots
+        self.resident_count = n if resident else max(0, min(int(resident_blocks), n))
+        self.resident = self.resident_count == n
+        count = self.resident_count + min(2, n - self.resident_count)
         self.slots = [torch.empty(layout.nbytes, dtype=torch.uint8, device=self.device)
                       for _ in range(count)]
         self.slot_views = [layout.views(s) for s in self.slots]
@@ -214,24 +220,22 @@ class FP8BlockRing:
         and synchronised only) skips the copy-stream events, as a CUDA graph capture needs."""
         compute = torch.cuda.current_stream(self.device)
         n = len(self.host_blocks)
-        if self.resident:
-            if not wait_ready and not all(self.loaded):
-                raise ValueError("skipping the ready events needs every resident block loaded")
-            for i in range(n):
-                if not self.loaded[i]:
-                    self._fetch(i, i)
-                    self.loaded[i] = True
-            for i in range(n):
-                if wait_ready:
-                    compute.wait_event(self.ready[i])
-                hidden = block_fn(self.slot_views[i], hidden)
-            return hidden
-        if not wait_ready:
-            raise ValueError("a streamed stack always orders its copies with events")
-        for i in range(min(2, n)):
-            self._fetch(i, i)
-        for i in range(n):
-            slot = i % 2
+        r = self.resident_count
+        if not wait_ready and (r != n or not all(self.loaded)):
+            raise ValueError("skipping the ready events needs every block resident and loaded")
+        for i in range(r):
+            if not self.loaded[i]:
+                self._fetch(i, i)
+                self.loaded[i] = True
+        # the first streamed blocks load while the resident ones compute
+        for j in range(min(2, n - r)):
+            self._fetch(r + j, r + j)
+        for i in range(r):
+            if wait_ready:
+                compute.wait_event(self.ready[i])
+            hidden = block_fn(self.slot_views[i], hidden)
+        for i in range(r, n):
+            slot = r + (i - r) % 2
             compute.wait_event(self.ready[slot])
             hidden = block_fn(self.slot_views[slot], hidden)
             self.done[slot].record(compute)
