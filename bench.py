@@ -671,16 +671,7 @@ def stack_config(args, device, rank: int, world: int, barrier, max_over_ranks) -
     replay = graphed.capture(shard, gate)
     graph_ms, out3 = timed(lambda h, g: replay(), steps)
     graph_same = bool(torch.equal(out3, out2))
-    del resident_ring, out, out3, replay, graphed
-    torch.cuda.empty_cache()
-    # a quarter of the blocks resident, the rest streamed: lowers the host
-    # bandwidth the ring needs when several GPUs share the host
-    partial_ring = FP8BlockRing(stack.layout, stack.host_blocks, device, group=group,
-                                resident_blocks=blocks // 4)
-    partial_ms, out4 = timed(
-        lambda h, g: partial_ring.run(h, lambda w, x: block_linears(stack.execution, w, x, g)), steps)
-    partial_same = bool(torch.equal(out4, out2))
-    del partial_ring, out2, out4
+    del resident_ring, out, out2, out3, replay, graphed
     torch.cuda.empty_cache()
     peaks = measured_peaks()
     fp8_peak = 2.0 * float(peaks.get("bf16_tflops_sustained", peaks.get("bf16_tflops", 1400.0)))
@@ -694,8 +685,6 @@ def stack_config(args, device, rank: int, world: int, barrier, max_over_ranks) -
         "resident_ms_per_step": round(resident_ms, 2),
         "resident_graph_ms_per_step": round(graph_ms, 2),
         "graph_equals_eager": graph_same,
-        "quarter_resident_ms_per_step": round(partial_ms, 2),
-        "quarter_resident_equals_resident": partial_same,
         "streaming_overhead": round(streamed_ms / resident_ms - 1.0, 4),
         "tflops_whole_job": round(flop_step / (streamed_ms * 1e-3) / 1e12, 1),
         "tflops_per_gpu": round(per_gpu_tflops, 1),

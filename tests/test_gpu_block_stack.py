@@ -144,3 +144,14 @@ def test_partially_resident_stack_equals_direct(count, resident_blocks):
     torch.cuda.synchronize()
     streamed = count - resident_blocks
     assert stack.ring.h2d_bytes == (resident_blocks + 3 * streamed) * stack.weight_bytes_per_block
+
+
+@pytest.mark.parametrize("count,slots,resident_blocks", [(6, 3, 0), (5, 4, 1), (3, 4, 0)])
+def test_deeper_ring_equals_direct(count, slots, resident_blocks):
+    blocks = make_blocks(count, seed=600)
+    hidden, gate = inputs(200)
+    want = direct(blocks, hidden, gate)
+    stack = FP8BlockStack(blocks, H, F, DEV, slots=slots, resident_blocks=resident_blocks, chunk_bytes=1 << 20)
+    for _ in range(3):
+        assert torch.equal(stack.forward(hidden, gate), want)
+    assert len(stack.ring.slots) == resident_blocks + min(slots, count - resident_blocks)

@@ -66,8 +66,8 @@ class FP8BlockStack:
     """
 
     def __init__(self, blocks: Iterable[dict[str, FP8Weight]], hidden: int, ffn: int, device, *,
-                 group=None, resident: bool = False, resident_blocks: int = 0, chunk_bytes: int = 2 * 1024**3,
-                 execution: RowFP8Execution | None = None) -> None:
+                 group=None, resident: bool = False, resident_blocks: int = 0, slots: int = 2,
+                 chunk_bytes: int = 2 * 1024**3, execution: RowFP8Execution | None = None) -> None:
         import torch.distributed as dist
 
         world = dist.get_world_size(group) if group is not None else 1
@@ -81,7 +81,7 @@ class FP8BlockStack:
         self.host_blocks = pin_blocks(self.layout, blocks, self.arena, rank=rank, world=world)
         self.arena.close()  # the views keep their slabs; no further allocations
         self.ring = FP8BlockRing(self.layout, self.host_blocks, device, group=group, resident=resident,
-                                 resident_blocks=resident_blocks)
+                                 resident_blocks=resident_blocks, slots=slots)
         self.execution = execution or RowFP8Execution("w8a8")
 
     @classmethod

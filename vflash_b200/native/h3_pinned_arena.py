@@ -22,8 +22,9 @@ choices:
 
 ``resident=True`` instead keeps every block on the device after its first
 copy (a stack of 48 H3 blocks is 9.7 GB of FP8 weights; B200 has 180 GB), and
-``resident_blocks=R`` keeps the first R resident and streams the rest, which
-lowers the host bandwidth the ring needs when several GPUs share the host.
+``resident_blocks=R`` keeps the first R resident and streams the rest, and
+``slots=S`` (default 2, as the reference) rotates the streamed blocks through
+S device buffers, so each block's copy has S - 1 blocks of compute to land.
 """
 
 from __future__ import annotations
@@ -175,7 +176,7 @@ class FP8BlockRing:
     """
 
     def __init__(self, layout: BlockLayout, host_blocks: list[torch.Tensor], device: torch.device, *,
-                 group=None, resident: bool = False, resident_blocks: int = 0) -> None:
+                 group=None, resident: bool = False, resident_blocks: int = 0, slots: int = 2) -> None:
         import torch.distributed as dist
 
         self.layout = layout
@@ -195,7 +196,12 @@ class FP8BlockRing:
         # the rest stream through two slots
         self.resident_count = n if resident else max(0, min(int(resident_blocks), n))
         self.resident = self.resident_count == n
-        count = self.resident_count + min(2, n - self.resident_count)
+        if slots < 2:
+            raise ValueError("the ring needs at least two slots")
+        # streamed blocks rotate through `slots` buffers: the copy of block i + slots
+        # starts when block i's compute ends, so it has slots - 1 blocks of compute to land
+        self.stream_slots = slots
+        count = self.resident_count + min(slots, n - self.resident_count)
         self.slots = [torch.empty(layout.nbytes, dtype=torch.uint8, device=self.device)
                       for _ in range(count)]
         self.slot_views = [layout.views(s) for s in self.slots]
@@ -227,20 +233,21 @@ class FP8BlockRing:
             if not self.loaded[i]:
                 self._fetch(i, i)
                 self.loaded[i] = True
+        depth = self.stream_slots
         # the first streamed blocks load while the resident ones compute
-        for j in range(min(2, n - r)):
+        for j in range(min(depth, n - r)):
             self._fetch(r + j, r + j)
         for i in range(r):
             if wait_ready:
                 compute.wait_event(self.ready[i])
             hidden = block_fn(self.slot_views[i], hidden)
         for i in range(r, n):
-            slot = r + (i - r) % 2
+            slot = r + (i - r) % depth
             compute.wait_event(self.ready[slot])
             hidden = block_fn(self.slot_views[slot], hidden)
             self.done[slot].record(compute)
-            if i + 2 < n:
-                self._fetch(i + 2, slot)
+            if i + depth < n:
+                self._fetch(i + depth, slot)
         return hidden
 
 
