@@ -519,6 +519,23 @@ def other_configs(device, flush, stream, cpu_seconds: float = 0.0) -> dict:
         "ms": round(fq, 4), "tflops": round(qflop / (fq * 1e-3) / 1e12, 1), "unfused_ms": round(uq, 4),
         "step": "quantiser + QKV GEMM with per-head QK-norm + rotary on Q and K in the epilogue, vs the "
                 "same GEMM then torch rms_norm and vfb_rotary on Q and K"}
+
+    # the same projection stored straight into pack_qkv's destination-major wire
+    # layout (2 destinations x 2 chunks), vs planar Q/K/V then the permuting copy
+    def wire_qkv():
+        ex.qkv_linear(x3, wq, wqs, pack_chunks=2)
+
+    def planar_then_pack():
+        q, k, v = ex.qkv_linear(x3, wq, wqs)
+        torch.stack([t.view(1, m1, 32, 128) for t in (q, k, v)]).reshape(
+            3, 1, m1, 2, 2, 8, 128).permute(4, 3, 0, 1, 2, 5, 6).contiguous()
+
+    fw = statistics.median(_timed(wire_qkv, flush, stream))
+    uw = statistics.median(_timed(planar_then_pack, flush, stream))
+    out["qkv_wire_pack"] = {
+        "ms": round(fw, 4), "tflops": round(qflop / (fw * 1e-3) / 1e12, 1), "unfused_ms": round(uw, 4),
+        "step": "quantiser + QKV GEMM storing (chunk, destination, qkv, rows, heads, dim) directly, vs "
+                "planar Q/K/V then the pack_qkv permutation as a copy"}
     del xq, wq, wqs, rc, rs, ang
 
     # c2: fused FFN, GELU-tanh, per-token requant of the intermediate, residual

@@ -145,6 +145,14 @@ VFB_API int vfb_fp8_norm_modulate_quant(const void *x, int64_t M, int64_t K, int
  * p = n / plane_width (plane_width = 0: one plane of width N) at
  *   out + p * plane_stride + m * ldo + (n % plane_width),
  * which writes the Q, K and V planes of a merged projection directly.
+ * wire_chunks = c > 0 (STORE or QKV_NORM_ROPE with three planes) stores the
+ * planes instead in the destination-major wire layout of pack_qkv
+ * (src/vflash/native/h3_parallel_relayout.py:214-256): each plane's columns
+ * are split into 2c groups of W = plane_width / (2c) columns (W % 32 == 0),
+ * group g = d * c + k (destination d in {0, 1}, chunk k) of plane p going to
+ * slab s = (k * 2 + d) * 3 + p at
+ *   out + s * plane_stride + m * ldo + (n % W),
+ * i.e. out is [c][2][3][M][W] with ldo = W and plane_stride = M * W.
  * A: e4m3 [M rows, K] with row stride lda bytes (multiple of 16); sa: [>=M].
  * W: e4m3 [N,K] row-major with row stride ldw bytes (multiple of 16);
  * sw: [N].  K % 16 == 0.  N % 32 == 0 (SWIGLU: F % 32 == 0).
@@ -157,7 +165,7 @@ VFB_API int vfb_fp8_norm_modulate_quant(const void *x, int64_t M, int64_t K, int
 
 typedef struct vfb_epilogue {
   int32_t kind;              /* VFB_EPI_*                                   */
-  int32_t reserved0;
+  int32_t wire_chunks;       /* 0, or chunks of the pack_qkv wire layout    */
   void *out;                 /* bf16 output                                 */
   int64_t ldo;               /* output row stride (elements)                */
   int64_t plane_width;       /* 0 or a multiple of 32 dividing N            */

@@ -163,3 +163,19 @@ def rotary(value_bits, cos_bits, sin_bits) -> np.ndarray:
     out = value.copy()
     out[..., :rd] = bf16_round(rot * cos) + bf16_round(partner * sin)
     return bf16_bits(out.astype(np.float32))
+
+
+def pack_qkv(q, k, v, chunks: int) -> np.ndarray:
+    """Destination-major QKV wire layout (src/vflash/native/h3_parallel_relayout.py:214-222).
+
+    ``q``, ``k``, ``v`` are ``[B, rows, heads, D]`` arrays (any dtype, here
+    bf16 bit patterns); heads split as (destination 2, chunk, heads per
+    chunk), and the result is ``(chunk, destination, qkv, B, rows,
+    heads / (2 chunks), D)``.  A pure permutation: values are moved, not
+    changed.
+    """
+    b, rows, heads, d = q.shape
+    if heads % (2 * chunks):
+        raise ValueError("QKV heads must divide two destinations and all chunks")
+    stacked = np.stack((q, k, v)).reshape(3, b, rows, 2, chunks, heads // (2 * chunks), d)
+    return np.ascontiguousarray(stacked.transpose(4, 3, 0, 1, 2, 5, 6))

@@ -16,7 +16,9 @@ It imports the reference's own CPU code and freezes its outputs:
 * the eager BF16 compositions that the reference's strict fused kernels are
   written to reproduce (src/vflash/native/h3_fused_ops.py module docstring and
   kernels at 125-224, 901-949): value*silu(gate), residual + gate*projected,
-  base + adapter*scaling, and torch's tanh-GELU on a linear output.
+  base + adapter*scaling, and torch's tanh-GELU on a linear output;
+* ``pack_qkv_reference`` (src/vflash/native/h3_parallel_relayout.py:214-222),
+  the destination-major wire layout of the QKV planes.
 
 Nothing at test time reads the reference: the tests load the ``.npz`` files.
 """
@@ -154,6 +156,15 @@ def main() -> None:
     out["qkv_adapters"] = np.stack([bits(a) for a in adapters])
     out["qkv_scalings"] = np.asarray(scalings, dtype=np.float32)
     out["qkv_out"] = bits(merged)
+
+    # the destination-major QKV wire layout (src/vflash/native/h3_parallel_relayout.py:214-222)
+    from vflash.native.h3_parallel_relayout import pack_qkv_reference
+
+    gen = torch.Generator().manual_seed(12)
+    for chunks in (1, 2):
+        qkv = [torch.randn(2, 3, 8, 4, generator=gen).to(torch.bfloat16) for _ in range(3)]
+        out[f"pack{chunks}_qkv"] = np.stack([bits(t) for t in qkv])
+        out[f"pack{chunks}_out"] = bits(pack_qkv_reference(*qkv, chunks=chunks))
 
     np.savez_compressed(HERE / "fp8_golden.npz", **out)
     print(f"wrote {HERE / 'fp8_golden.npz'} with {len(out)} arrays")

@@ -56,6 +56,7 @@ def test_epilogue_struct_layout_matches_header():
     assert _lib.Epilogue.adapter.offset == 48
     assert _lib.Epilogue.residual.offset == 96
     assert _lib.Epilogue.q_norm.offset == 144
+    assert _lib.Epilogue.wire_chunks.offset == 4
 
 
 @pytest.mark.parametrize(
@@ -116,3 +117,13 @@ def test_new_entry_points_reject_bad_arguments_before_any_launch():
     ep = _lib.Epilogue()
     ep.kind = _lib.EPI_QKV_NORM_ROPE
     assert lib.vfb_fp8_gemm(None, 64, None, None, 64, None, 4, 384, 64, ctypes.byref(ep), None) == _lib.VFB_EINVAL
+    # the pack_qkv wire layout only for STORE / QKV_NORM_ROPE, and a bounded chunk count
+    for kind, chunks in ((_lib.EPI_GELU_TANH, 1), (_lib.EPI_RESIDUAL, 2), (_lib.EPI_STORE, -1),
+                         (_lib.EPI_STORE, 4096)):
+        ep = _lib.Epilogue()
+        ep.kind, ep.wire_chunks = kind, chunks
+        buf = ctypes.create_string_buffer(64)
+        ptr = (ctypes.addressof(buf) + 15) // 16 * 16
+        ep.out, ep.ldo = ptr, 64
+        assert lib.vfb_fp8_gemm(ptr, 64, ptr, ptr, 64, ptr, 4, 384, 64, ctypes.byref(ep), None) == _lib.VFB_EINVAL
+        assert "wire_chunks" in _lib.last_error()

@@ -167,3 +167,11 @@ def test_oracle_rotary_matches_the_reference_eager_expression():
         c, s = cos[None, :, None, :], sin[None, :, None, :]
         eager = torch.cat((rot * c + rotated * s, passthrough), dim=-1)
         np.testing.assert_array_equal(epilogues.rotary(bits_of(x), bits_of(cos), bits_of(sin)), bits_of(eager))
+
+
+@pytest.mark.parametrize("chunks", [1, 2])
+def test_oracle_pack_qkv_matches_the_reference_layout(golden, chunks):
+    q, k, v = golden[f"pack{chunks}_qkv"]
+    np.testing.assert_array_equal(ep.pack_qkv(q, k, v, chunks), golden[f"pack{chunks}_out"])
+    with pytest.raises(ValueError, match="destinations"):
+        ep.pack_qkv(q[:, :, :6], k[:, :, :6], v[:, :, :6], 4)

@@ -37,7 +37,7 @@ class Epilogue(ctypes.Structure):
 
     _fields_ = [
         ("kind", ctypes.c_int32),
-        ("reserved0", ctypes.c_int32),
+        ("wire_chunks", ctypes.c_int32),
         ("out", _vp),
         ("ldo", _c_int64),
         ("plane_width", _c_int64),

@@ -71,6 +71,8 @@ constexpr size_t SMEM_BYTES =
 
 struct EpiParams {
   int32_t plane_width;  // columns per output plane (N when there is one plane)
+  int32_t wire_chunks;  // > 0: planes stored in the (chunk, destination, qkv) slabs of pack_qkv
+  int32_t wire_width;   // columns per slab (plane_width / (2 * wire_chunks))
   const __nv_bfloat16 *bias;
   const __nv_bfloat16 *adapter[3];
   int64_t adapter_ld;
@@ -172,6 +174,29 @@ __device__ __forceinline__ void store_box(uint8_t *warp_smem, int &box, const CU
     bulk_commit_group();
   }
   box = box + 1 == BOXES ? 0 : box + 1;
+}
+
+// Output coordinate (column, plane index of the tensor map) of a 32-column
+// box that starts at column col of plane `plane`.  Without the wire layout the
+// planes are the tensor map's planes.  With it, plane p's columns are split
+// into 2 * wire_chunks groups of wire_width (group g = destination *
+// wire_chunks + chunk, i.e. heads in destination-major, chunk-minor order)
+// and group g goes to slab (chunk * 2 + destination) * 3 + p: the
+// (chunk, destination, qkv, rows, heads, dim) layout of pack_qkv
+// (src/vflash/native/h3_parallel_relayout.py:214-256).  A box never
+// straddles two groups (wire_width % 32 == 0).
+__device__ __forceinline__ void out_coord(const EpiParams &ep, int32_t plane, int32_t col, int32_t &ocol,
+                                          int32_t &oplane) {
+  if (ep.wire_chunks == 0) {
+    ocol = col;
+    oplane = plane;
+    return;
+  }
+  const int32_t g = col / ep.wire_width;
+  const int32_t chunk = g % ep.wire_chunks;
+  const int32_t dest = g / ep.wire_chunks;
+  ocol = col - g * ep.wire_width;
+  oplane = (chunk * 2 + dest) * 3 + plane;
 }
 
 // y = bf16(acc * sa * sw) then bf16(y + bias): the _scaled_mm output followed
@@ -451,8 +476,9 @@ __global__ void __launch_bounds__(num_threads<EPI>(), 1)
 #pragma unroll
                 for (int j = 0; j < 32; ++j) v[j] = 0.0f;
               }
-              store_box<kBoxes>(warp_smem, box, &tmOut, v, lane, col0 + 32 * k, static_cast<int32_t>(row0),
-                                plane, any_row);
+              int32_t oc, op;
+              out_coord(ep, plane, col0 + 32 * k, oc, op);
+              store_box<kBoxes>(warp_smem, box, &tmOut, v, lane, oc, static_cast<int32_t>(row0), op, any_row);
             }
         } else {
           // pass 1: this thread's row of the head (bf16 values, packed), sum of squares in fp32
@@ -492,8 +518,9 @@ __global__ void __launch_bounds__(num_threads<EPI>(), 1)
 #pragma unroll
               for (int j = 0; j < 32; ++j) o[j] = 0.0f;
             }
-            store_box<kBoxes>(warp_smem, box, &tmOut, o, lane, col0 + 32 * k, static_cast<int32_t>(row0), plane,
-                              any_row);
+            int32_t oc, op;
+            out_coord(ep, plane, col0 + 32 * k, oc, op);
+            store_box<kBoxes>(warp_smem, box, &tmOut, o, lane, oc, static_cast<int32_t>(row0), op, any_row);
           }
         }
       } else if (EPI == VFB_EPI_SWIGLU) {
@@ -549,7 +576,9 @@ __global__ void __launch_bounds__(num_threads<EPI>(), 1)
 #pragma unroll
             for (int j = 0; j < 32; ++j) v[j] = 0.0f;
           }
-          store_box<kBoxes>(warp_smem, box, &tmOut, v, lane, col, static_cast<int32_t>(row0), plane, any_row);
+          int32_t oc, op;
+          out_coord(ep, plane, col, oc, op);
+          store_box<kBoxes>(warp_smem, box, &tmOut, v, lane, oc, static_cast<int32_t>(row0), op, any_row);
         }
       }
       tc_fence_before();
@@ -675,6 +704,10 @@ extern "C" int vfb_fp8_gemm(const void *A, int64_t lda, const float *sa, const v
     return set_error(VFB_EINVAL, "vfb_fp8_gemm: sw/out need 16-byte alignment, ldo %% 8 == 0");
   if (ep->bias != nullptr && !aligned16(ep->bias))
     return set_error(VFB_EINVAL, "vfb_fp8_gemm: bias needs 16-byte alignment");
+  if (ep->wire_chunks < 0 || ep->wire_chunks > 1024 ||
+      (ep->wire_chunks > 0 && kind != VFB_EPI_STORE && kind != VFB_EPI_QKV_NORM_ROPE))
+    return set_error(VFB_EINVAL, "vfb_fp8_gemm: wire_chunks must be 0..1024, and 0 unless the epilogue is "
+                                 "STORE or QKV_NORM_ROPE");
 
   int sm_count = 0;
   int rc = check_device(&sm_count);
@@ -712,12 +745,21 @@ extern "C" int vfb_fp8_gemm(const void *A, int64_t lda, const float *sa, const v
       return set_error(VFB_EINVAL, "vfb_fp8_gemm: plane_width must be 0 or a multiple of 32 dividing N");
     const int64_t width = ep->plane_width > 0 ? ep->plane_width : N;
     const int64_t planes = N / width;
-    if (ep->ldo < width) return set_error(VFB_EINVAL, "vfb_fp8_gemm: ldo smaller than the plane width");
-    const int64_t plane_stride = planes > 1 ? ep->plane_stride : M * ep->ldo;
-    if (plane_stride % 8 || (planes > 1 && plane_stride < M * ep->ldo))
+    const int64_t chunks = ep->wire_chunks;
+    if (chunks > 0 && (planes != 3 || width % (2 * chunks) || (width / (2 * chunks)) % 32))
+      return set_error(VFB_EINVAL, "vfb_fp8_gemm: the wire layout needs three planes whose width splits into "
+                                   "2 * wire_chunks groups of a multiple of 32 columns");
+    // the tensor map's planes: the output planes, or the 6 * wire_chunks slabs of the wire layout
+    const int64_t out_width = chunks > 0 ? width / (2 * chunks) : width;
+    const int64_t slabs = chunks > 0 ? 6 * chunks : planes;
+    if (ep->ldo < out_width) return set_error(VFB_EINVAL, "vfb_fp8_gemm: ldo smaller than the plane width");
+    const int64_t plane_stride = slabs > 1 ? ep->plane_stride : M * ep->ldo;
+    if (plane_stride % 8 || (slabs > 1 && plane_stride < M * ep->ldo))
       return set_error(VFB_EINVAL, "vfb_fp8_gemm: plane_stride must be a multiple of 8 and >= M*ldo");
     e.plane_width = static_cast<int32_t>(width);
-    if ((rc = make_map_out(&to, ep->out, width, M, planes, ep->ldo, plane_stride)) != VFB_OK) return rc;
+    e.wire_chunks = static_cast<int32_t>(chunks);
+    e.wire_width = static_cast<int32_t>(out_width);
+    if ((rc = make_map_out(&to, ep->out, out_width, M, slabs, ep->ldo, plane_stride)) != VFB_OK) return rc;
     p.num_n_tiles = static_cast<int>((N + BN - 1) / BN);
     if ((rc = make_map_u8(&tb, W, N, K, ldw, BN_HALF)) != VFB_OK) return rc;
     tb2 = tb;

@@ -147,6 +147,9 @@ class Epilogue:
     rope_cos: torch.Tensor | None = None # bf16 [tokens, 128], unit column stride
     rope_sin: torch.Tensor | None = None # bf16 [tokens, 128], same layout as rope_cos
     qk_eps: float = 1e-5
+    # STORE / QKV_NORM_ROPE with planes = 3: store the planes in pack_qkv's
+    # (chunks, 2, 3, rows, plane width / (2 * chunks)) wire layout instead
+    wire_chunks: int = 0
 
 
 def fp8_gemm(a_codes: torch.Tensor, a_scales: torch.Tensor, rows: int, weight: torch.Tensor,
@@ -157,7 +160,8 @@ def fp8_gemm(a_codes: torch.Tensor, a_scales: torch.Tensor, rows: int, weight: t
     ``a_codes`` e4m3 ``[>=rows, K]``, ``a_scales`` fp32 (>= rows entries),
     ``weight`` e4m3 ``[N, K]`` row-major, ``w_scales`` fp32 ``[N, 1]``.
     Returns bf16 ``[rows, N]`` (``[rows, N/2]`` for SWIGLU, ``[planes, rows,
-    N/planes]`` when the output is split into planes).
+    N/planes]`` when the output is split into planes, ``[chunks, 2, 3, rows,
+    N/(6 chunks)]`` in the wire layout).
     """
     ep = epilogue or Epilogue()
     n, k = weight.shape
@@ -186,6 +190,13 @@ def fp8_gemm(a_codes: torch.Tensor, a_scales: torch.Tensor, rows: int, weight: t
     if ep.kind == _lib.EPI_SWIGLU:
         width = n // 2
         shape = (rows, width)
+    elif ep.wire_chunks:
+        c = ep.wire_chunks
+        if (ep.kind not in (_lib.EPI_STORE, _lib.EPI_QKV_NORM_ROPE) or ep.planes != 3 or c < 0
+                or (n // 3) % (2 * c) or (n // 3 // (2 * c)) % 32):
+            raise KernelInputError("the wire layout splits three planes into 2 * chunks groups of 32k columns")
+        width = n // 3
+        shape = (c, 2, 3, rows, width // (2 * c))
     elif ep.planes > 1:
         width = n // ep.planes
         shape = (ep.planes, rows, width)
@@ -201,6 +212,10 @@ def fp8_gemm(a_codes: torch.Tensor, a_scales: torch.Tensor, rows: int, weight: t
     if ep.planes > 1 and ep.kind != _lib.EPI_SWIGLU:
         e.plane_width = width
         e.plane_stride = rows * width
+    if ep.wire_chunks:
+        e.wire_chunks = ep.wire_chunks
+        e.ldo = shape[-1]
+        e.plane_stride = rows * shape[-1]
     if ep.adapters is not None:
         for i, adapter in enumerate(ep.adapters):
             if adapter is None:

@@ -196,12 +196,20 @@ class RowFP8Execution:
         return value.shape, matrix, matrix.shape[0]
 
     def qkv_linear(self, value, weight, scale, bias=None, *, adapters=None, scalings=None,
-                   prologue: NormModulate | None = None, qk_norm_rope: QKNormRope | None = None):
+                   prologue: NormModulate | None = None, qk_norm_rope: QKNormRope | None = None,
+                   pack_chunks: int | None = None, head_dim: int = 128):
         """Merged QKV projection writing Q, K and V planes directly.
 
         With ``qk_norm_rope`` the Q and K planes also get the block's per-head
         RMSNorm and rotary embedding in the epilogue (one pass instead of
         ``_qk_norm_rotary``'s four launches).
+
+        With ``pack_chunks`` the epilogue stores straight into the
+        destination-major wire layout of ``pack_qkv(q, k, v, chunks=...)``
+        (src/vflash/native/h3_parallel_relayout.py:214-256) and returns that
+        one tensor, ``(chunks, 2, 3, *value.shape[:-1], heads / (2 chunks),
+        head_dim)``, instead of the three planes: the pack pass before the
+        sequence-head all-to-all disappears.
 
         Equivalent to ``linear(value, weight, scale, bias).chunk(3, -1)``
         (src/vflash/native/h3_native_denoiser.py:541) followed, when
@@ -224,6 +232,11 @@ class RowFP8Execution:
             flat_adapters = tuple(a.reshape(rows, width) for a in adapters)
             scales = tuple(float(s) for s in scalings)
         epilogue = Epilogue(bias=bias, planes=3, adapters=flat_adapters, scalings=scales)
+        if pack_chunks is not None:
+            if (not isinstance(pack_chunks, int) or pack_chunks < 1 or head_dim < 1
+                    or width % (2 * pack_chunks * head_dim) or (width // (2 * pack_chunks)) % 32):
+                raise ValueError("QKV heads must divide two destinations and all chunks")
+            epilogue.wire_chunks = pack_chunks
         if qk_norm_rope is not None:
             tokens = qk_norm_rope.cos.shape[0] if qk_norm_rope.cos.ndim == 2 else 0
             if width % 128 or tokens < 1 or rows % tokens or (len(shape) >= 3 and tokens not in (1, shape[-2])):
@@ -235,6 +248,9 @@ class RowFP8Execution:
         codes, act_scale = self._quantize(matrix, prologue, shape)
         with self.measure("linear.fp8_gemm"):
             planes = fp8_gemm(codes, act_scale, rows, weight, scale, epilogue)
+        if pack_chunks is not None:
+            per_chunk = width // (2 * pack_chunks)
+            return planes.view(pack_chunks, 2, 3, *shape[:-1], per_chunk // head_dim, head_dim)
         return tuple(planes[i].reshape(*shape[:-1], width) for i in range(3))
 
     def gelu_linear(self, value, weight, scale, bias=None, *, prologue: NormModulate | None = None):
