@@ -536,7 +536,51 @@ def other_configs(device, flush, stream, cpu_seconds: float = 0.0) -> dict:
         "ms": round(fw, 4), "tflops": round(qflop / (fw * 1e-3) / 1e12, 1), "unfused_ms": round(uw, 4),
         "step": "quantiser + QKV GEMM storing (chunk, destination, qkv, rows, heads, dim) directly, vs "
                 "planar Q/K/V then the pack_qkv permutation as a copy"}
-    del xq, wq, wqs, rc, rs, ang
+
+    # the QKV projection with three rank-32 low-rank branches: native (one
+    # concatenated down GEMM, three up GEMMs on tcgen05, merge in the QKV
+    # epilogue) vs the reference's composition (cuBLAS bf16 linears, eager
+    # scale and add after the projection)
+    from dataclasses import dataclass as _dc
+
+    @_dc(frozen=True)
+    class _Residual:
+        down: torch.Tensor
+        up: torch.Tensor
+        scaling: float
+
+    lr_rank = 32
+    residuals = tuple(_Residual(seeded(lr_rank, 4096, 1020 + i, std=0.02), seeded(4096, lr_rank, 1030 + i, std=0.02),
+                                s) for i, s in enumerate((0.5, 1.0, 0.25)))
+
+    def native_lora_qkv():
+        ex.qkv_linear(x3, wq, wqs, residuals=residuals)
+
+    def reference_lora_qkv():
+        planes = ex.qkv_linear(x3, wq, wqs)
+        torch.cat([p + torch.nn.functional.linear(torch.nn.functional.linear(x3, r.down), r.up) * r.scaling
+                   for p, r in zip(planes, residuals)], dim=-1)
+
+    def native_products():
+        ex.qkv_low_rank(x3, residuals)
+
+    def cublas_products():
+        for r in residuals:
+            torch.nn.functional.linear(torch.nn.functional.linear(x3, r.down), r.up)
+
+    fl = statistics.median(_timed(native_lora_qkv, flush, stream))
+    rl = statistics.median(_timed(reference_lora_qkv, flush, stream))
+    fp_ = statistics.median(_timed(native_products, flush, stream))
+    cp_ = statistics.median(_timed(cublas_products, flush, stream))
+    lr_bytes = m1 * 4096 * 2 + 3 * m1 * 4096 * 2  # read the input once, write three [M, 4096] outputs
+    out["qkv_low_rank_r32"] = {
+        "ms": round(fl, 4), "reference_composition_ms": round(rl, 4),
+        "products_ms": round(fp_, 4), "products_cublas_ms": round(cp_, 4),
+        "products_gb_per_s": round(lr_bytes / (fp_ * 1e-3) / 1e9, 1),
+        "step": "QKV projection + three rank-32 LoRA branches (down [32,4096], up [4096,32] each): one "
+                "concatenated bf16 down GEMM, three bf16 up GEMMs (tcgen05 kind::f16), merge fused in the "
+                "QKV epilogue; vs planar QKV then per branch cuBLAS linear(linear(x, down), up) * s + add"}
+    del xq, wq, wqs, rc, rs, ang, residuals
 
     # c2: fused FFN, GELU-tanh, per-token requant of the intermediate, residual
     m, h, f = 32760, 4096, 16384

@@ -198,6 +198,21 @@ VFB_API int vfb_fp8_gemm(const void *A, int64_t lda, const float *sa,
                  int64_t M, int64_t N, int64_t K,
                  const vfb_epilogue *ep, void *stream);
 
+/* Low-rank adapter products: out = bf16(A @ W^T), bf16
+ * operands, fp32 accumulation on the same CTA-pair tensor-core pipeline
+ * (tcgen05.mma kind::f16).  Replaces the two functional.linear calls of
+ * _residual_linear_unscaled (src/vflash/native/h3_native_denoiser.py:288-299):
+ * the down product states @ down^T ([M, r]; the three QKV branches' downs
+ * concatenated into one [3r, H] weight) and the up product low @ up^T
+ * ([M, inner]), whose result the STORE adapters of vfb_fp8_gemm then scale and
+ * merge.  A: bf16 [M, K] with row stride lda ELEMENTS; W: bf16 [N, K], row
+ * stride ldw elements; K % 8 == 0, strides multiples of 8, 16-byte aligned
+ * bases; N % 8 == 0.  ep: kind VFB_EPI_STORE with out, ldo (elements,
+ * multiple of 8, >= N) and nothing else: one plane, no bias, no adapters, no
+ * wire layout (the reference's low-rank linears have no bias). */
+VFB_API int vfb_bf16_gemm(const void *A, int64_t lda, const void *W, int64_t ldw,
+                  int64_t M, int64_t N, int64_t K, const vfb_epilogue *ep, void *stream);
+
 /* ---- NVFP4 ----------------------------------------------------------------
  * Activation quantiser: replaces FlashInfer nvfp4_quantize(x, global_scale,
  * sfLayout=128x4, do_shuffle=False) as NVFP4Execution.linear calls it

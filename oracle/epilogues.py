@@ -179,3 +179,39 @@ def pack_qkv(q, k, v, chunks: int) -> np.ndarray:
         raise ValueError("QKV heads must divide two destinations and all chunks")
     stacked = np.stack((q, k, v)).reshape(3, b, rows, 2, chunks, heads // (2 * chunks), d)
     return np.ascontiguousarray(stacked.transpose(4, 3, 0, 1, 2, 5, 6))
+
+
+def bf16_linear(a_bits, w_bits) -> np.ndarray:
+    """``functional.linear(a, w)`` in bf16 without bias: bf16(exact a @ w^T), as bf16 bits.
+
+    The products and their sum are formed in float64 (exact for these sizes
+    up to the final rounding), so a fp32-accumulating kernel may differ from
+    this by one bf16 step where its sum lands next to a rounding boundary.
+    Follows the low-rank products of _residual_linear_unscaled
+    (src/vflash/native/h3_native_denoiser.py:288-299).
+    """
+    a = bf16_value(a_bits).astype(np.float64)
+    w = bf16_value(w_bits).astype(np.float64)
+    return f64_to_bf16_bits(a @ w.T)
+
+
+def f64_to_bf16_bits(x: np.ndarray) -> np.ndarray:
+    """float64 -> bf16 bits with ONE round-to-nearest-even.
+
+    Goes through float32 rounded to odd (an inexact result takes the odd one
+    of its two float32 neighbours), which keeps the sticky information, so
+    the final bf16 rounding equals a direct rounding of the float64 value.
+    """
+    x = np.asarray(x, dtype=np.float64)
+    t = x.astype(np.float32)
+    inexact = t.astype(np.float64) != x
+    even = (t.view(np.uint32) & 1) == 0
+    fix = inexact & even & np.isfinite(t)
+    toward = np.where(x > t.astype(np.float64), np.float32(np.inf), np.float32(-np.inf))
+    t = np.where(fix, np.nextafter(t, toward), t).astype(np.float32)
+    return bf16_bits(t)
+
+
+def low_rank(x_bits, down_bits, up_bits) -> np.ndarray:
+    """Unscaled low-rank residual: bf16 rounding after each product (h3_native_denoiser.py:297-299)."""
+    return bf16_linear(bf16_linear(x_bits, down_bits), up_bits)

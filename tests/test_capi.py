@@ -127,3 +127,24 @@ def test_new_entry_points_reject_bad_arguments_before_any_launch():
         ep.out, ep.ldo = ptr, 64
         assert lib.vfb_fp8_gemm(ptr, 64, ptr, ptr, 64, ptr, 4, 384, 64, ctypes.byref(ep), None) == _lib.VFB_EINVAL
         assert "wire_chunks" in _lib.last_error()
+
+
+def test_bf16_gemm_rejects_bad_arguments_before_any_launch():
+    lib = _lib.load()
+    buf = ctypes.create_string_buffer(64)
+    ptr = (ctypes.addressof(buf) + 15) // 16 * 16
+    ep = _lib.Epilogue()
+    ep.kind, ep.out, ep.ldo = _lib.EPI_STORE, ptr, 64
+    # K % 8, strides
+    assert lib.vfb_bf16_gemm(ptr, 64, ptr, 64, 4, 64, 12, ctypes.byref(ep), None) == _lib.VFB_EINVAL
+    assert lib.vfb_bf16_gemm(ptr, 12, ptr, 64, 4, 64, 8, ctypes.byref(ep), None) == _lib.VFB_EINVAL
+    assert "vfb_bf16_gemm" in _lib.last_error()
+    # N % 8
+    assert lib.vfb_bf16_gemm(ptr, 64, ptr, 64, 4, 60, 64, ctypes.byref(ep), None) == _lib.VFB_EINVAL
+    # plain STORE only: no bias, adapters, planes or other kinds
+    for field, value in (("bias", ptr), ("plane_width", 32), ("wire_chunks", 1), ("kind", _lib.EPI_GELU_TANH)):
+        bad = _lib.Epilogue()
+        bad.kind, bad.out, bad.ldo = _lib.EPI_STORE, ptr, 64
+        setattr(bad, field, value)
+        assert lib.vfb_bf16_gemm(ptr, 64, ptr, 64, 4, 64, 64, ctypes.byref(bad), None) == _lib.VFB_EINVAL
+        assert "vfb_bf16_gemm" in _lib.last_error()

@@ -175,3 +175,17 @@ def test_oracle_pack_qkv_matches_the_reference_layout(golden, chunks):
     np.testing.assert_array_equal(ep.pack_qkv(q, k, v, chunks), golden[f"pack{chunks}_out"])
     with pytest.raises(ValueError, match="destinations"):
         ep.pack_qkv(q[:, :, :6], k[:, :, :6], v[:, :, :6], 4)
+
+
+def test_oracle_f64_to_bf16_rounds_once():
+    # values at, just above and just below bf16 midpoints: a float32 detour that
+    # rounds to nearest would land on the midpoint and round the tie wrongly
+    from oracle.epilogues import f64_to_bf16_bits
+
+    b = np.random.default_rng(0).integers(0, 0x7F00, 4096).astype(np.uint16)
+    lo, hi = fp8.bf16_value(b).astype(np.float64), fp8.bf16_value(b + 1).astype(np.float64)
+    mid, step = (lo + hi) / 2, hi - lo
+    np.testing.assert_array_equal(f64_to_bf16_bits(mid), np.where(b & 1, b + 1, b).astype(np.uint16))
+    np.testing.assert_array_equal(f64_to_bf16_bits(mid + step * 1e-9), (b + 1).astype(np.uint16))
+    np.testing.assert_array_equal(f64_to_bf16_bits(mid - step * 1e-9), b)
+    np.testing.assert_array_equal(f64_to_bf16_bits(-mid - step * 1e-9), (b + 1).astype(np.uint16) | 0x8000)

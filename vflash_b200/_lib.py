@@ -87,6 +87,10 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         [_vp, _c_int64, _vp, _vp, _c_int64, _vp, _c_int64, _c_int64, _c_int64,
          ctypes.POINTER(Epilogue), _vp],
     ),
+    "vfb_bf16_gemm": (
+        ctypes.c_int,
+        [_vp, _c_int64, _vp, _c_int64, _c_int64, _c_int64, _c_int64, ctypes.POINTER(Epilogue), _vp],
+    ),
     "vfb_nvfp4_quant_rows": (
         ctypes.c_int, [_vp, ctypes.c_int32, _c_int64, _c_int64, _c_int64, _vp, _vp, _vp, _vp]),
     "vfb_nvfp4_gemm": (

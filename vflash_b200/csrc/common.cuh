@@ -239,6 +239,14 @@ __host__ __device__ constexpr uint32_t idesc_e4m3_f32(int m, int n) {
          | (static_cast<uint32_t>(m >> 4) << 24);   // M / 16
 }
 
+// Instruction descriptor (kind::f16): bf16 x bf16 -> f32, both operands K-major.
+__host__ __device__ constexpr uint32_t idesc_bf16_f32(int m, int n) {
+  return (1u << 4)                                  // D format f32
+         | (1u << 7) | (1u << 10)                   // A, B format bf16
+         | (static_cast<uint32_t>(n >> 3) << 17)    // N / 8
+         | (static_cast<uint32_t>(m >> 4) << 24);   // M / 16
+}
+
 // 32 lanes x 32 consecutive 32-bit TMEM columns; thread i gets lane base+i.
 __device__ __forceinline__ void tmem_ld_32x32b_x32(uint32_t taddr, float (&v)[32]) {
   uint32_t r[32];
@@ -437,6 +445,19 @@ __device__ __forceinline__ void mma_f8f6f4_pair(uint32_t d_tmem, uint64_t a_desc
       "{\n\t.reg .pred p;\n\t"
       "setp.ne.b32 p, %4, 0;\n\t"
       "tcgen05.mma.cta_group::2.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// Pair-wide D (+)= A * B^T with 16-bit operands (kind::f16; both operands
+// bf16, as the instruction descriptor says): K = 16 elements = 32 bytes per
+// instruction, the same byte step as the 8-bit form.
+__device__ __forceinline__ void mma_f16_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                             uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
       "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
       : "memory");
 }

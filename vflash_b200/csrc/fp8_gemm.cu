@@ -44,8 +44,12 @@ namespace {
 constexpr int BM = 128;       // A rows per CTA (a CTA pair covers 256 rows)
 constexpr int BN = 256;       // output columns per pair tile
 constexpr int BN_HALF = BN / 2;  // weight rows each CTA of the pair loads
-constexpr int BK = 128;       // bytes = e4m3 elements per stage
-constexpr int UMMA_K = 32;
+constexpr int BK = 128;       // bytes per stage: 128 e4m3 or 64 bf16 elements of K
+constexpr int UMMA_K = 32;    // bytes of K per MMA: 32 e4m3 (kind::f8f6f4) or 16 bf16 (kind::f16)
+// operand types of the kernel: row-scaled e4m3 (the FP8 linear) or plain bf16
+// (the low-rank adapter products, F.linear in bf16)
+constexpr int OPS_E4M3 = 0;
+constexpr int OPS_BF16 = 1;
 constexpr int STAGES = 5;
 constexpr int A_STAGE_BYTES = BM * BK;       // 16 KB
 constexpr int B_STAGE_BYTES = BN_HALF * BK;  // 16 KB
@@ -200,13 +204,17 @@ __device__ __forceinline__ void out_coord(const EpiParams &ep, int32_t plane, in
 }
 
 // y = bf16(acc * sa * sw) then bf16(y + bias): the _scaled_mm output followed
-// by the separate bias add of the reference.
+// by the separate bias add of the reference.  Unscaled (bf16 operands):
+// y = bf16(acc), the F.linear output, then the bias the same way.
+template <bool SCALED = true>
 __device__ __forceinline__ void scale_bias(float (&v)[32], float sa, const float *sw,
                                            const __nv_bfloat16 *bias) {
-  float w[32];
-  load_f32x32(sw, w);
+  if constexpr (SCALED) {
+    float w[32];
+    load_f32x32(sw, w);
 #pragma unroll
-  for (int j = 0; j < 32; ++j) v[j] = v[j] * sa * w[j];
+    for (int j = 0; j < 32; ++j) v[j] = v[j] * sa * w[j];
+  }
   bf16r_x32(v);
   if (bias != nullptr) {
     float b[32];
@@ -218,9 +226,10 @@ __device__ __forceinline__ void scale_bias(float (&v)[32], float sa, const float
 }
 
 // STORE value of 32 columns: scale_bias, then the plane's LoRA branch if any.
+template <bool SCALED = true>
 __device__ __forceinline__ void store_value(float (&v)[32], float sa, const float *sw, const EpiParams &ep,
                                             int32_t n, int32_t plane, int32_t col, int64_t m) {
-  scale_bias(v, sa, sw + n, ep.bias ? ep.bias + n : nullptr);
+  scale_bias<SCALED>(v, sa, SCALED ? sw + n : nullptr, ep.bias ? ep.bias + n : nullptr);
   const __nv_bfloat16 *ad = plane < 3 ? ep.adapter[plane] : nullptr;
   if (ad != nullptr) {
     float a[32];
@@ -282,7 +291,7 @@ __device__ __forceinline__ void qk_norm_rope_chunk(const uint32_t (&hp)[64], flo
   }
 }
 
-template <int EPI>
+template <int EPI, int OPS>
 __global__ void __launch_bounds__(num_threads<EPI>(), 1)
     fp8_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                     const __grid_constant__ CUtensorMap tmB2, const __grid_constant__ CUtensorMap tmOut,
@@ -385,7 +394,7 @@ __global__ void __launch_bounds__(num_threads<EPI>(), 1)
   } else if (warp == 1) {
     if (rank == 0) {
       // ---------------- MMA issuer (leader CTA only): whole warp, one elected lane ----------------
-      constexpr uint32_t idesc = idesc_e4m3_f32(2 * BM, BN);
+      constexpr uint32_t idesc = OPS == OPS_BF16 ? idesc_bf16_f32(2 * BM, BN) : idesc_e4m3_f32(2 * BM, BN);
       const bool leader = elect_one();  // the same lane issues and commits every tcgen05 op
       int s = 0;
       uint32_t ph = 0;
@@ -409,7 +418,10 @@ __global__ void __launch_bounds__(num_threads<EPI>(), 1)
 #pragma unroll
             for (int k = 0; k < BK / UMMA_K; ++k) {
               // +32 bytes along K inside the swizzled 128-byte row = +2 in 16-byte units.
-              mma_f8f6f4_pair(d_tmem, a_desc + 2 * k, b_desc + 2 * k, idesc, (kb | k) != 0);
+              if constexpr (OPS == OPS_BF16)
+                mma_f16_pair(d_tmem, a_desc + 2 * k, b_desc + 2 * k, idesc, (kb | k) != 0);
+              else
+                mma_f8f6f4_pair(d_tmem, a_desc + 2 * k, b_desc + 2 * k, idesc, (kb | k) != 0);
             }
             tc_commit_pair(smem_u32(&empty_bar[s]));
             tc_commit_pair(map_to_rank(smem_u32(&empty_bar[s]), 1));
@@ -454,7 +466,8 @@ __global__ void __launch_bounds__(num_threads<EPI>(), 1)
       const int64_t m = row0 + lane;
       const bool live = m < p.M;
       const bool any_row = row0 < p.M;  // warp-uniform
-      const float sa = live ? __ldg(p.sa + m) : 0.0f;
+      constexpr bool kScaled = OPS == OPS_E4M3;
+      const float sa = kScaled && live ? __ldg(p.sa + m) : 1.0f;
       const uint32_t t_row = tmem_base + acc * BN + (static_cast<uint32_t>(q * 32) << 16);
 
       if (EPI == VFB_EPI_QKV_NORM_ROPE) {
@@ -554,7 +567,7 @@ __global__ void __launch_bounds__(num_threads<EPI>(), 1)
           const int32_t col = n - plane * ep.plane_width;
           if (live) {
             if (EPI == VFB_EPI_STORE) {
-              store_value(v, sa, p.sw, ep, n, plane, col, m);
+              store_value<kScaled>(v, sa, p.sw, ep, n, plane, col, m);
             } else if (EPI == VFB_EPI_GELU_TANH) {
               scale_bias(v, sa, p.sw + n, ep.bias ? ep.bias + n : nullptr);
 #pragma unroll
@@ -641,10 +654,10 @@ int make_map_out(CUtensorMap *map, void *base, int64_t width, int64_t rows, int6
 
 bool aligned16(const void *ptr) { return reinterpret_cast<uintptr_t>(ptr) % 16 == 0; }
 
-template <int EPI>
+template <int EPI, int OPS = OPS_E4M3>
 int launch(const CUtensorMap &a, const CUtensorMap &b, const CUtensorMap &b2, const CUtensorMap &o,
            const GemmParams &p, int sm_count, cudaStream_t stream) {
-  auto kernel = fp8_gemm_kernel<EPI>;
+  auto kernel = fp8_gemm_kernel<EPI, OPS>;
   // the shared-memory opt-in is a per-device function attribute: set it once
   static std::atomic<bool> smem_set[kMaxAttrDevices];
   int dev = 0;
@@ -678,36 +691,41 @@ int launch(const CUtensorMap &a, const CUtensorMap &b, const CUtensorMap &b2, co
   return VFB_OK;
 }
 
-}  // namespace
-}  // namespace vfb
-
-extern "C" int vfb_fp8_gemm(const void *A, int64_t lda, const float *sa, const void *W, int64_t ldw,
-                            const float *sw, int64_t M, int64_t N, int64_t K,
-                            const vfb_epilogue *ep, void *stream) {
-  using namespace vfb;
-  if (ep == nullptr) return set_error(VFB_EINVAL, "vfb_fp8_gemm: epilogue is NULL");
+// Shared body of vfb_fp8_gemm and vfb_bf16_gemm.  K, lda and ldw are in BYTES
+// of the operand rows (= elements for e4m3); fn names the entry point in errors.
+int gemm_impl(const char *fn, int ops, const void *A, int64_t lda, const float *sa, const void *W,
+              int64_t ldw, const float *sw, int64_t M, int64_t N, int64_t K, const vfb_epilogue *ep,
+              void *stream) {
+  if (ep == nullptr) return set_error(VFB_EINVAL, "%s: epilogue is NULL", fn);
   const int kind = ep->kind;
   if (kind < VFB_EPI_STORE || kind > VFB_EPI_QKV_NORM_ROPE)
-    return set_error(VFB_EINVAL, "vfb_fp8_gemm: unknown epilogue kind %d", kind);
-  if (M < 0 || N <= 0 || K <= 0 || K % 16 || N % 32)
-    return set_error(VFB_EINVAL, "vfb_fp8_gemm: need M >= 0, N > 0 with N %% 32 == 0, K > 0 with "
-                                 "K %% 16 == 0 (M=%lld N=%lld K=%lld)",
-                     (long long)M, (long long)N, (long long)K);
+    return set_error(VFB_EINVAL, "%s: unknown epilogue kind %d", fn, kind);
+  // bf16 operands: N % 8 (the output boxes clip at N), plain STORE, no scales
+  const bool bf16 = ops == OPS_BF16;
+  if (M < 0 || N <= 0 || K <= 0 || K % 16 || N % (bf16 ? 8 : 32))
+    return set_error(VFB_EINVAL, "%s: need M >= 0, N > 0 with N %% %d == 0, K > 0 with "
+                                 "%d-byte rows (M=%lld N=%lld K=%lld)", fn, bf16 ? 8 : 32, 16,
+                     (long long)M, (long long)N, (long long)(bf16 ? K / 2 : K));
+  if (bf16 && (kind != VFB_EPI_STORE || ep->wire_chunks != 0 || ep->plane_width != 0 ||
+               ep->adapter[0] != nullptr || ep->adapter[1] != nullptr || ep->adapter[2] != nullptr ||
+               ep->bias != nullptr))
+    return set_error(VFB_EINVAL, "%s: bf16 operands take a plain STORE epilogue (one plane, no bias, "
+                                 "no adapters)", fn);
   if (M == 0) return VFB_OK;
   if (M > (int64_t)2 * BM * 0x3FFFFF || N > (int64_t)1 << 24 || K > (int64_t)1 << 20)
-    return set_error(VFB_EINVAL, "vfb_fp8_gemm: problem too large");
-  if (A == nullptr || W == nullptr || sa == nullptr || sw == nullptr || ep->out == nullptr)
-    return set_error(VFB_EINVAL, "vfb_fp8_gemm: NULL operand");
+    return set_error(VFB_EINVAL, "%s: problem too large", fn);
+  if (A == nullptr || W == nullptr || (!bf16 && (sa == nullptr || sw == nullptr)) || ep->out == nullptr)
+    return set_error(VFB_EINVAL, "%s: NULL operand", fn);
   if (lda < K || ldw < K || lda % 16 || ldw % 16 || !aligned16(A) || !aligned16(W))
-    return set_error(VFB_EINVAL, "vfb_fp8_gemm: A/W need 16-byte aligned bases and row strides");
-  if (!aligned16(sw) || !aligned16(ep->out) || ep->ldo % 8)
-    return set_error(VFB_EINVAL, "vfb_fp8_gemm: sw/out need 16-byte alignment, ldo %% 8 == 0");
+    return set_error(VFB_EINVAL, "%s: A/W need 16-byte aligned bases and row strides", fn);
+  if ((!bf16 && !aligned16(sw)) || !aligned16(ep->out) || ep->ldo % 8)
+    return set_error(VFB_EINVAL, "%s: sw/out need 16-byte alignment, ldo %% 8 == 0", fn);
   if (ep->bias != nullptr && !aligned16(ep->bias))
-    return set_error(VFB_EINVAL, "vfb_fp8_gemm: bias needs 16-byte alignment");
+    return set_error(VFB_EINVAL, "%s: bias needs 16-byte alignment", fn);
   if (ep->wire_chunks < 0 || ep->wire_chunks > 1024 ||
       (ep->wire_chunks > 0 && kind != VFB_EPI_STORE && kind != VFB_EPI_QKV_NORM_ROPE))
-    return set_error(VFB_EINVAL, "vfb_fp8_gemm: wire_chunks must be 0..1024, and 0 unless the epilogue is "
-                                 "STORE or QKV_NORM_ROPE");
+    return set_error(VFB_EINVAL, "%s: wire_chunks must be 0..1024, and 0 unless the epilogue is "
+                                 "STORE or QKV_NORM_ROPE", fn);
 
   int sm_count = 0;
   int rc = check_device(&sm_count);
@@ -731,9 +749,9 @@ extern "C" int vfb_fp8_gemm(const void *A, int64_t lda, const float *sa, const v
 
   if (kind == VFB_EPI_SWIGLU) {
     if (N % 64)
-      return set_error(VFB_EINVAL, "vfb_fp8_gemm: SWIGLU needs the packed width N = 2F, F %% 32 == 0");
+      return set_error(VFB_EINVAL, "%s: SWIGLU needs the packed width N = 2F, F %% 32 == 0", fn);
     const int64_t F = N / 2;
-    if (ep->ldo < F) return set_error(VFB_EINVAL, "vfb_fp8_gemm: SWIGLU output ldo < F");
+    if (ep->ldo < F) return set_error(VFB_EINVAL, "%s: SWIGLU output ldo < F", fn);
     e.plane_width = static_cast<int32_t>(F);
     p.num_n_tiles = static_cast<int>((F + BN_HALF - 1) / BN_HALF);
     if ((rc = make_map_out(&to, ep->out, F, M, 1, ep->ldo, M * ep->ldo)) != VFB_OK) return rc;
@@ -742,20 +760,20 @@ extern "C" int vfb_fp8_gemm(const void *A, int64_t lda, const float *sa, const v
     if ((rc = make_map_u8(&tb2, gate_rows, F, K, ldw, BN_HALF)) != VFB_OK) return rc;
   } else {
     if (ep->plane_width < 0 || (ep->plane_width > 0 && (ep->plane_width % 32 || N % ep->plane_width)))
-      return set_error(VFB_EINVAL, "vfb_fp8_gemm: plane_width must be 0 or a multiple of 32 dividing N");
+      return set_error(VFB_EINVAL, "%s: plane_width must be 0 or a multiple of 32 dividing N", fn);
     const int64_t width = ep->plane_width > 0 ? ep->plane_width : N;
     const int64_t planes = N / width;
     const int64_t chunks = ep->wire_chunks;
     if (chunks > 0 && (planes != 3 || width % (2 * chunks) || (width / (2 * chunks)) % 32))
-      return set_error(VFB_EINVAL, "vfb_fp8_gemm: the wire layout needs three planes whose width splits into "
-                                   "2 * wire_chunks groups of a multiple of 32 columns");
+      return set_error(VFB_EINVAL, "%s: the wire layout needs three planes whose width splits into "
+                                   "2 * wire_chunks groups of a multiple of 32 columns", fn);
     // the tensor map's planes: the output planes, or the 6 * wire_chunks slabs of the wire layout
     const int64_t out_width = chunks > 0 ? width / (2 * chunks) : width;
     const int64_t slabs = chunks > 0 ? 6 * chunks : planes;
-    if (ep->ldo < out_width) return set_error(VFB_EINVAL, "vfb_fp8_gemm: ldo smaller than the plane width");
+    if (ep->ldo < out_width) return set_error(VFB_EINVAL, "%s: ldo smaller than the plane width", fn);
     const int64_t plane_stride = slabs > 1 ? ep->plane_stride : M * ep->ldo;
     if (plane_stride % 8 || (slabs > 1 && plane_stride < M * ep->ldo))
-      return set_error(VFB_EINVAL, "vfb_fp8_gemm: plane_stride must be a multiple of 8 and >= M*ldo");
+      return set_error(VFB_EINVAL, "%s: plane_stride must be a multiple of 8 and >= M*ldo", fn);
     e.plane_width = static_cast<int32_t>(width);
     e.wire_chunks = static_cast<int32_t>(chunks);
     e.wire_width = static_cast<int32_t>(out_width);
@@ -766,14 +784,13 @@ extern "C" int vfb_fp8_gemm(const void *A, int64_t lda, const float *sa, const v
     if (kind == VFB_EPI_QKV_NORM_ROPE) {
       const auto a16p = [](const void *q) { return q == nullptr || aligned16(q); };
       if (planes != 3 || width % 128)
-        return set_error(VFB_EINVAL, "vfb_fp8_gemm: QKV_NORM_ROPE needs three planes of 128-column heads");
+        return set_error(VFB_EINVAL, "%s: QKV_NORM_ROPE needs three planes of 128-column heads", fn);
       if (ep->rope_cos == nullptr || ep->rope_sin == nullptr || !aligned16(ep->rope_cos) ||
           !aligned16(ep->rope_sin) || ep->rope_token_stride < 0 || ep->rope_token_stride % 8 ||
           (ep->tokens > 1 && ep->rope_token_stride < 128) || ep->tokens <= 0)
-        return set_error(VFB_EINVAL,
-                         "vfb_fp8_gemm: rotary cos/sin need 16-byte aligned [tokens, 128] rows, tokens > 0");
+        return set_error(VFB_EINVAL, "%s: rotary cos/sin need 16-byte aligned [tokens, 128] rows, tokens > 0", fn);
       if (!a16p(ep->q_norm) || !a16p(ep->k_norm) || !(ep->qk_eps > 0.0f))
-        return set_error(VFB_EINVAL, "vfb_fp8_gemm: QK-norm weights need 16-byte alignment, qk_eps > 0");
+        return set_error(VFB_EINVAL, "%s: QK-norm weights need 16-byte alignment, qk_eps > 0", fn);
       e.q_norm = static_cast<const __nv_bfloat16 *>(ep->q_norm);
       e.k_norm = static_cast<const __nv_bfloat16 *>(ep->k_norm);
       e.rope_cos = static_cast<const __nv_bfloat16 *>(ep->rope_cos);
@@ -788,22 +805,22 @@ extern "C" int vfb_fp8_gemm(const void *A, int64_t lda, const float *sa, const v
         e.scaling[i] = ep->scaling[i];
         if (e.adapter[i] != nullptr) {
           if (i >= planes || !aligned16(e.adapter[i]) || ep->adapter_ld % 8 || ep->adapter_ld < width)
-            return set_error(VFB_EINVAL, "vfb_fp8_gemm: adapter %d misaligned or beyond the planes", i);
+            return set_error(VFB_EINVAL, "%s: adapter %d misaligned or beyond the planes", fn, i);
         }
       }
       e.adapter_ld = ep->adapter_ld;
     }
     if (kind == VFB_EPI_RESIDUAL) {
       if (ep->residual == nullptr || !aligned16(ep->residual) || ep->ldr % 8 || ep->ldr < N)
-        return set_error(VFB_EINVAL, "vfb_fp8_gemm: residual needs a 16-byte aligned [M,N] view");
+        return set_error(VFB_EINVAL, "%s: residual needs a 16-byte aligned [M,N] view", fn);
       if (planes != 1)
-        return set_error(VFB_EINVAL, "vfb_fp8_gemm: RESIDUAL writes one plane");
+        return set_error(VFB_EINVAL, "%s: RESIDUAL writes one plane", fn);
       e.residual = static_cast<const __nv_bfloat16 *>(ep->residual);
       e.ldr = ep->ldr;
       e.gate = static_cast<const __nv_bfloat16 *>(ep->gate);
       if (e.gate != nullptr) {
         if (ep->tokens <= 0)
-          return set_error(VFB_EINVAL, "vfb_fp8_gemm: gate needs tokens > 0");
+          return set_error(VFB_EINVAL, "%s: gate needs tokens > 0", fn);
         e.gate_ts = ep->gate_token_stride;
         e.gate_hs = ep->gate_hidden_stride;
         e.tokens = ep->tokens;
@@ -812,6 +829,7 @@ extern "C" int vfb_fp8_gemm(const void *A, int64_t lda, const float *sa, const v
   }
 
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (bf16) return launch<VFB_EPI_STORE, OPS_BF16>(ta, tb, tb2, to, p, sm_count, s);
   switch (kind) {
     case VFB_EPI_STORE:
       return launch<VFB_EPI_STORE>(ta, tb, tb2, to, p, sm_count, s);
@@ -824,4 +842,25 @@ extern "C" int vfb_fp8_gemm(const void *A, int64_t lda, const float *sa, const v
     default:
       return launch<VFB_EPI_RESIDUAL>(ta, tb, tb2, to, p, sm_count, s);
   }
+}
+
+}  // namespace
+}  // namespace vfb
+
+extern "C" int vfb_fp8_gemm(const void *A, int64_t lda, const float *sa, const void *W, int64_t ldw,
+                            const float *sw, int64_t M, int64_t N, int64_t K,
+                            const vfb_epilogue *ep, void *stream) {
+  return vfb::gemm_impl("vfb_fp8_gemm", vfb::OPS_E4M3, A, lda, sa, W, ldw, sw, M, N, K, ep, stream);
+}
+
+extern "C" int vfb_bf16_gemm(const void *A, int64_t lda, const void *W, int64_t ldw, int64_t M, int64_t N,
+                             int64_t K, const vfb_epilogue *ep, void *stream) {
+  using namespace vfb;
+  if (K <= 0 || K % 8 || lda < K || ldw < K || lda % 8 || ldw % 8 || K > (int64_t)1 << 19)
+    return set_error(VFB_EINVAL, "vfb_bf16_gemm: need 0 < K <= 2^19 with K %% 8 == 0 and row strides "
+                                 ">= K, multiples of 8 (K=%lld lda=%lld ldw=%lld)",
+                     (long long)K, (long long)lda, (long long)ldw);
+  // the operands travel as bytes: 2 per element
+  return gemm_impl("vfb_bf16_gemm", OPS_BF16, A, 2 * lda, nullptr, W, 2 * ldw, nullptr, M, N, 2 * K, ep,
+                   stream);
 }

@@ -281,6 +281,40 @@ def nvfp4_sf_shape(rows: int, cols: int) -> tuple[int, int]:
     return (-(-rows // 128) * 128, -(-(cols // 16) // 4) * 4)
 
 
+def bf16_gemm(a: torch.Tensor, w: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    """``bf16(a @ w^T)``: bias-free ``functional.linear`` in bf16 on the tcgen05 pipeline.
+
+    ``a`` bf16 ``[M, K]`` and ``w`` bf16 ``[N, K]``, unit column stride, row
+    strides multiples of 8, 16-byte aligned; K % 8 == 0, N % 8 == 0.  ``out``
+    (bf16 ``[M, N]``, unit column stride) may be a strided view, e.g. a
+    column slice of a wider buffer.
+    """
+    if (a.dtype != BF16 or w.dtype != BF16 or a.ndim != 2 or w.ndim != 2 or a.shape[1] != w.shape[1]
+            or a.stride(1) != 1 or w.stride(1) != 1 or a.device != w.device):
+        raise KernelInputError("bf16 GEMM operands must be bf16 [M,K] and [N,K] with unit column stride")
+    rows, k = a.shape
+    n = w.shape[0]
+    if k % 8 or n % 8 or a.stride(0) % 8 or w.stride(0) % 8 or not (_aligned(a) and _aligned(w)):
+        raise KernelInputError("bf16 GEMM needs K % 8 == 0, N % 8 == 0 and 16-byte aligned rows")
+    e = _lib.Epilogue()
+    e.kind = _lib.EPI_STORE
+    if out is None:
+        out = torch.empty((rows, n), device=a.device, dtype=BF16)
+    elif (out.dtype != BF16 or out.shape != (rows, n) or out.stride(1) != 1 or out.stride(0) % 8
+          or not _aligned(out) or out.device != a.device):
+        raise KernelInputError("bf16 GEMM output must be bf16 [M, N], unit column stride, aligned rows")
+    e.out = out.data_ptr()
+    e.ldo = out.stride(0)
+    if rows == 0:
+        return out
+    lib = _lib.load()
+    with torch.cuda.device(a.device):
+        rc = lib.vfb_bf16_gemm(a.data_ptr(), a.stride(0), w.data_ptr(), w.stride(0), rows, n, k,
+                               ctypes.byref(e), _lib.stream_handle(a.device))
+    _lib.check(rc, "vfb_bf16_gemm")
+    return out
+
+
 def nvfp4_quantize(matrix: torch.Tensor, global_scale: torch.Tensor):
     """e2m1 codes ``[M, K/2]`` (uint8) and 128x4 ue4m3 scales ``[ceil128(M), ceil4(K/16)]`` (uint8).
 

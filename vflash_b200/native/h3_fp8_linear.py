@@ -38,7 +38,7 @@ from typing import Any
 import torch
 
 from .. import _lib
-from ..kernels import Epilogue, fp8_gemm, quantize_fp8_norm_modulate, quantize_fp8_rows
+from ..kernels import Epilogue, bf16_gemm, fp8_gemm, quantize_fp8_norm_modulate, quantize_fp8_rows
 
 
 @dataclass(frozen=True)
@@ -195,9 +195,50 @@ class RowFP8Execution:
         matrix = value.reshape(-1, value.shape[-1])
         return value.shape, matrix, matrix.shape[0]
 
+    def low_rank(self, value, down, up):
+        """Unscaled low-rank residual ``linear(linear(value, down), up)`` in bf16.
+
+        ``_residual_linear_unscaled`` (src/vflash/native/h3_native_denoiser.py:
+        288-299) with both products on the tcgen05 pipeline (``vfb_bf16_gemm``):
+        ``value`` bf16 ``[..., K]``, ``down`` ``[r, K]``, ``up`` ``[N, r]``;
+        each product is rounded to bf16 as ``functional.linear`` rounds it.
+        """
+        shape, matrix = self._low_rank_input(value, down)
+        low = bf16_gemm(matrix, down.to(device=value.device, dtype=torch.bfloat16).contiguous())
+        out = bf16_gemm(low, up.to(device=value.device, dtype=torch.bfloat16).contiguous())
+        return out.reshape(*shape[:-1], out.shape[-1])
+
+    def qkv_low_rank(self, value, residuals) -> tuple:
+        """The three QKV branches' unscaled low-rank outputs ``[rows, inner]``.
+
+        The branches share their input, so their ``down`` matrices run as ONE
+        GEMM over ``[3r, K]`` (the input is read once), then each branch's
+        ``up`` reads its ``r`` columns of that product in place.
+        """
+        if len(residuals) != 3:
+            raise ValueError("H3 QKV residual pack must contain three branches")
+        downs = [r.down.to(device=value.device, dtype=torch.bfloat16) for r in residuals]
+        rank = downs[0].shape[0]
+        if any(d.shape != downs[0].shape for d in downs) or rank % 8:
+            raise ValueError("QKV low-rank branches need one shared rank, a multiple of 8")
+        _shape, matrix = self._low_rank_input(value, downs[0])
+        low = bf16_gemm(matrix, torch.cat(downs, dim=0))
+        return tuple(bf16_gemm(low[:, i * rank:(i + 1) * rank],
+                               r.up.to(device=value.device, dtype=torch.bfloat16).contiguous())
+                     for i, r in enumerate(residuals))
+
+    @staticmethod
+    def _low_rank_input(value, down):
+        if value.dtype != torch.bfloat16 or value.shape[-1] != down.shape[-1] or value.device.type != "cuda":
+            raise ValueError("low-rank branches take bf16 CUDA states matching their down matrix")
+        matrix = value.reshape(-1, value.shape[-1])
+        if matrix.stride(-1) != 1:
+            matrix = matrix.contiguous()
+        return value.shape, matrix
+
     def qkv_linear(self, value, weight, scale, bias=None, *, adapters=None, scalings=None,
                    prologue: NormModulate | None = None, qk_norm_rope: QKNormRope | None = None,
-                   pack_chunks: int | None = None, head_dim: int = 128):
+                   pack_chunks: int | None = None, head_dim: int = 128, residuals=None):
         """Merged QKV projection writing Q, K and V planes directly.
 
         With ``qk_norm_rope`` the Q and K planes also get the block's per-head
@@ -211,6 +252,12 @@ class RowFP8Execution:
         head_dim)``, instead of the three planes: the pack pass before the
         sequence-head all-to-all disappears.
 
+        ``residuals`` (three objects with ``down``, ``up`` and ``scaling``, as
+        ``H3LowRankResidualWeights``) computes the branches' adapters with
+        ``qkv_low_rank`` and merges them in the epilogue: the reference's
+        ``_qkv_linear`` with residuals (h3_native_denoiser.py:301-316) end to
+        end on the GPU, ``value`` being the projection's bf16 input.
+
         Equivalent to ``linear(value, weight, scale, bias).chunk(3, -1)``
         (src/vflash/native/h3_native_denoiser.py:541) followed, when
         ``adapters`` is given, by ``triton_strict_bf16_qkv_direct_merge``
@@ -218,6 +265,11 @@ class RowFP8Execution:
         ``bf16(base + bf16(adapter * scaling))``.  Returns three contiguous
         ``[..., N/3]`` tensors that are views of one ``[3, rows, N/3]`` buffer.
         """
+        if residuals is not None:
+            if adapters is not None or prologue is not None:
+                raise ValueError("residuals replace adapters and need the materialised bf16 input")
+            adapters = self.qkv_low_rank(value, residuals)
+            scalings = tuple(float(r.scaling) for r in residuals)
         shape, matrix, rows = self._fused_prologue(value, weight, scale, bias)
         n = weight.shape[0]
         if n % 3:
