@@ -56,17 +56,19 @@ constexpr int B_STAGE_BYTES = BN_HALF * BK;  // 16 KB
 // Warps 0 (TMA) and 1 (MMA) plus the epilogue warps: four (one per TMEM lane
 // quarter) for the light epilogues, eight for QK-norm + rotary, where each
 // 256-column tile is two 128-column heads and each head gets its own four
-// warps.
-template <int EPI>
-__host__ __device__ constexpr int epi_warps() { return EPI == VFB_EPI_QKV_NORM_ROPE ? 8 : 4; }
-template <int EPI>
-__host__ __device__ constexpr int num_threads() { return 64 + 32 * epi_warps<EPI>(); }
+// warps, and eight for bf16 operands, whose products are mostly output writes
+// (each group of four stores one 128-column half of the tile, so two warps
+// per lane quarter hide each other's TMEM-load latency).
+template <int EPI, int OPS = OPS_E4M3>
+__host__ __device__ constexpr int epi_warps() { return EPI == VFB_EPI_QKV_NORM_ROPE || OPS == OPS_BF16 ? 8 : 4; }
+template <int EPI, int OPS = OPS_E4M3>
+__host__ __device__ constexpr int num_threads() { return 64 + 32 * epi_warps<EPI, OPS>(); }
 constexpr int TMEM_COLS = 512;
 // Epilogue staging: per epilogue warp a ring of EPI_BOXES 32 x 32 bf16 boxes
 // (2 KB each), so TMA stores drain while the warp fills the next boxes.
 constexpr int EPI_BOXES = 4;  // with four epilogue warps; two with eight (same shared memory)
-template <int EPI>
-__host__ __device__ constexpr int epi_boxes() { return 16 / epi_warps<EPI>(); }
+template <int EPI, int OPS = OPS_E4M3>
+__host__ __device__ constexpr int epi_boxes() { return 16 / epi_warps<EPI, OPS>(); }
 constexpr int EPI_BOX_BYTES = 32 * 32 * 2;
 constexpr int EPI_SMEM_BYTES = 4 * EPI_BOXES * EPI_BOX_BYTES;
 static_assert(8 * 2 * EPI_BOX_BYTES == EPI_SMEM_BYTES, "eight-warp epilogue staging must fit");
@@ -292,7 +294,7 @@ __device__ __forceinline__ void qk_norm_rope_chunk(const uint32_t (&hp)[64], flo
 }
 
 template <int EPI, int OPS>
-__global__ void __launch_bounds__(num_threads<EPI>(), 1)
+__global__ void __launch_bounds__(num_threads<EPI, OPS>(), 1)
     fp8_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                     const __grid_constant__ CUtensorMap tmB2, const __grid_constant__ CUtensorMap tmOut,
                     const GemmParams p) {
@@ -323,7 +325,7 @@ __global__ void __launch_bounds__(num_threads<EPI>(), 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tfull_bar[a], 1);
-      mbar_init(&tempty_bar[a], 2 * 32 * epi_warps<EPI>());  // leader: every epilogue thread of both CTAs
+      mbar_init(&tempty_bar[a], 2 * 32 * epi_warps<EPI, OPS>());  // leader: every epilogue thread of both CTAs
     }
     mbar_init(drain_bar, 1);
     *abort_flag = 0;
@@ -450,8 +452,11 @@ __global__ void __launch_bounds__(num_threads<EPI>(), 1)
     // ---------------- epilogue (warps 2..5 of both CTAs) ----------------
     const int q = warp & 3;  // TMEM lane quarter this warp may access
     const EpiParams &ep = p.ep;
-    constexpr int kBoxes = epi_boxes<EPI>();
-    const int group = (warp - 2) >> 2;  // QKV_NORM_ROPE: the head of the tile this warp handles
+    constexpr int kBoxes = epi_boxes<EPI, OPS>();
+    // eight warps: the 128-column half of the tile (QKV_NORM_ROPE: the head) this warp handles
+    const int group = (warp - 2) >> 2;
+    constexpr bool kHalves = EPI != VFB_EPI_QKV_NORM_ROPE && epi_warps<EPI, OPS>() == 8;
+    constexpr int kChunks = kHalves ? BN / 64 : BN / 32;  // 32-column chunks per warp and tile
     uint8_t *warp_smem = sEpi + (q + 4 * group) * kBoxes * EPI_BOX_BYTES;
     int box = 0;
     int t = 0;
@@ -558,7 +563,8 @@ __global__ void __launch_bounds__(num_threads<EPI>(), 1)
         }
       } else {
 #pragma unroll 1
-        for (int c = 0; c < BN / 32; ++c) {
+        for (int cc = 0; cc < kChunks; ++cc) {
+          const int c = kHalves ? group * kChunks + cc : cc;
           const int32_t n = n_tile * BN + c * 32;
           if (n >= p.N) break;  // warp-uniform
           float v[32];
@@ -675,7 +681,7 @@ int launch(const CUtensorMap &a, const CUtensorMap &b, const CUtensorMap &b2, co
   const int pairs = tiles < max_pairs ? tiles : max_pairs;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(2 * pairs, 1, 1);
-  cfg.blockDim = dim3(num_threads<EPI>(), 1, 1);
+  cfg.blockDim = dim3(num_threads<EPI, OPS>(), 1, 1);
   cfg.dynamicSmemBytes = SMEM_BYTES;
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
