@@ -213,6 +213,30 @@ VFB_API int vfb_fp8_gemm(const void *A, int64_t lda, const float *sa,
 VFB_API int vfb_bf16_gemm(const void *A, int64_t lda, const void *W, int64_t ldw,
                   int64_t M, int64_t N, int64_t K, const vfb_epilogue *ep, void *stream);
 
+/* Fused FP8 FFN in one call: replaces RowFP8Execution.ffn's sequence (the
+ * FFN input and output linears of the H3 block, src/vflash/native/
+ * h3_native_denoiser.py:561-576, with the reference's per-token activation
+ * quantiser before each, h3_fp8_linear.py:92-121): vfb_fp8_quant_rows(x) ->
+ * vfb_fp8_gemm(activation = VFB_EPI_GELU_TANH with w_up [F, H], or
+ * VFB_EPI_SWIGLU with the packed w_up [2F, H]; bias_up) -> vfb_fp8_quant_rows
+ * of the bf16 intermediate [M, F] -> vfb_fp8_gemm(w_down [H, F]; bias_down;
+ * RESIDUAL with residual [M, H] (row stride ldr) and optional gate [tokens, H]
+ * (row stride gate_token_stride), else STORE) into out [M, H] (row stride
+ * ldo).  Same kernels and bits as the separate calls.  x: bf16 [M, H], row
+ * stride ldx; s_up [n_up], s_down [H] fp32.  H and F multiples of 32, at most
+ * 32768.  The intermediates live in `workspace` (256-byte aligned, at least
+ * vfb_fp8_ffn_workspace_bytes(M, H, F) bytes, F = intermediate width); the
+ * call allocates nothing.  vfb_fp8_ffn_workspace_bytes returns -1 for an
+ * invalid shape. */
+VFB_API int64_t vfb_fp8_ffn_workspace_bytes(int64_t M, int64_t H, int64_t F);
+VFB_API int vfb_fp8_ffn(const void *x, int64_t M, int64_t H, int64_t ldx,
+                const void *w_up, const float *s_up, int64_t n_up,
+                const void *w_down, const float *s_down, int32_t activation,
+                const void *bias_up, const void *bias_down,
+                const void *residual, int64_t ldr,
+                const void *gate, int64_t gate_token_stride, int64_t tokens,
+                void *out, int64_t ldo, void *workspace, int64_t workspace_bytes, void *stream);
+
 /* ---- NVFP4 ----------------------------------------------------------------
  * Activation quantiser: replaces FlashInfer nvfp4_quantize(x, global_scale,
  * sfLayout=128x4, do_shuffle=False) as NVFP4Execution.linear calls it

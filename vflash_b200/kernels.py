@@ -281,6 +281,54 @@ def nvfp4_sf_shape(rows: int, cols: int) -> tuple[int, int]:
     return (-(-rows // 128) * 128, -(-(cols // 16) // 4) * 4)
 
 
+def fp8_ffn(x: torch.Tensor, up: torch.Tensor, up_scales: torch.Tensor, down: torch.Tensor,
+            down_scales: torch.Tensor, *, activation: int = _lib.EPI_GELU_TANH, up_bias=None, down_bias=None,
+            residual=None, gate=None) -> torch.Tensor:
+    """The whole FP8 FFN through ``vfb_fp8_ffn`` (one C call, workspace from torch's allocator).
+
+    ``x`` bf16 ``[M, H]`` (unit column stride), ``up`` e4m3 ``[F or 2F, H]``,
+    ``down`` e4m3 ``[H, F]``, scales fp32 ``[N, 1]``; ``residual`` bf16
+    ``[M, H]`` and ``gate`` bf16 ``[tokens, H]`` as the down GEMM's RESIDUAL
+    epilogue.  Returns bf16 ``[M, H]``.
+    """
+    rows, hidden = x.shape
+    n_up = up.shape[0]
+    width = n_up // 2 if activation == _lib.EPI_SWIGLU else n_up
+    device = x.device
+    if (x.dtype != BF16 or x.stride(1) != 1 or up.dtype != FP8 or down.dtype != FP8
+            or up.shape[1] != hidden or down.shape != (hidden, width) or not up.is_contiguous()
+            or not down.is_contiguous() or up_scales.numel() != n_up or down_scales.numel() != hidden
+            or up_scales.dtype != torch.float32 or down_scales.dtype != torch.float32):
+        raise KernelInputError("FP8 FFN operands differ from the declared layouts")
+    for t in (up, down, up_scales, down_scales, up_bias, down_bias, residual, gate):
+        if t is not None and t.device != device:
+            raise KernelInputError("FP8 FFN operands must share one device")
+    if residual is not None and (residual.dtype != BF16 or residual.shape != (rows, hidden)
+                                 or residual.stride(1) != 1):
+        raise KernelInputError("FP8 FFN residual must be bf16 [M, H] with unit column stride")
+    if gate is not None and (gate.dtype != BF16 or gate.ndim != 2 or gate.shape[1] != hidden
+                             or gate.stride(1) != 1):
+        raise KernelInputError("FP8 FFN gate must be bf16 [tokens, H] with unit column stride")
+    lib = _lib.load()
+    need = lib.vfb_fp8_ffn_workspace_bytes(rows, hidden, width)
+    if need < 0:
+        raise KernelInputError("FP8 FFN shape is outside the supported range")
+    out = torch.empty((rows, hidden), device=device, dtype=BF16)
+    workspace = torch.empty(need + 256, device=device, dtype=torch.uint8)
+    base = workspace.data_ptr() + (-workspace.data_ptr()) % 256
+    with torch.cuda.device(device):
+        rc = lib.vfb_fp8_ffn(
+            x.data_ptr(), rows, hidden, x.stride(0), up.data_ptr(), up_scales.data_ptr(), n_up,
+            down.data_ptr(), down_scales.data_ptr(), activation,
+            None if up_bias is None else up_bias.data_ptr(), None if down_bias is None else down_bias.data_ptr(),
+            None if residual is None else residual.data_ptr(), 0 if residual is None else residual.stride(0),
+            None if gate is None else gate.data_ptr(), 0 if gate is None else gate.stride(0),
+            0 if gate is None else gate.shape[0], out.data_ptr(), hidden, base, need,
+            _lib.stream_handle(device))
+    _lib.check(rc, "vfb_fp8_ffn")
+    return out
+
+
 def bf16_gemm(a: torch.Tensor, w: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
     """``bf16(a @ w^T)``: bias-free ``functional.linear`` in bf16 on the tcgen05 pipeline.
 
