@@ -237,6 +237,27 @@ VFB_API int vfb_fp8_ffn(const void *x, int64_t M, int64_t H, int64_t ldx,
                 const void *gate, int64_t gate_token_stride, int64_t tokens,
                 void *out, int64_t ldo, void *workspace, int64_t workspace_bytes, void *stream);
 
+/* vfb_fp8_ffn for callers that cannot allocate device memory: a process that
+ * embeds this library in a runtime which has already reserved the GPU's
+ * memory for its own pool, or code that runs where cudaMalloc's implicit
+ * synchronisation is not allowed.  This entry point has no counterpart in
+ * the reference.  Same arguments and result as vfb_fp8_ffn without the
+ * workspace: the intermediates live in a fixed 64 MiB array of device memory
+ * owned by the library, which every GPU that loads the library holds until
+ * the process exits.  Shapes whose intermediates need more
+ * (vfb_fp8_ffn_workspace_bytes(M, H, F) > 64 MiB) are rejected with
+ * VFB_EINVAL.  The first call on a device looks the array's address up
+ * (cudaGetSymbolAddress); make that first call before any stream capture.
+ * All calls on a device share the array: calls whose kernels may overlap on
+ * the GPU (other streams, unordered host threads) race, so order them. */
+VFB_API int vfb_fp8_ffn_noalloc(const void *x, int64_t M, int64_t H, int64_t ldx,
+                const void *w_up, const float *s_up, int64_t n_up,
+                const void *w_down, const float *s_down, int32_t activation,
+                const void *bias_up, const void *bias_down,
+                const void *residual, int64_t ldr,
+                const void *gate, int64_t gate_token_stride, int64_t tokens,
+                void *out, int64_t ldo, void *stream);
+
 /* ---- NVFP4 ----------------------------------------------------------------
  * Activation quantiser: replaces FlashInfer nvfp4_quantize(x, global_scale,
  * sfLayout=128x4, do_shuffle=False) as NVFP4Execution.linear calls it

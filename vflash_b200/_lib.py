@@ -93,6 +93,11 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         [_vp, _c_int64, _c_int64, _c_int64, _vp, _vp, _c_int64, _vp, _vp, ctypes.c_int32, _vp, _vp, _vp,
          _c_int64, _vp, _c_int64, _c_int64, _vp, _c_int64, _vp, _c_int64, _vp],
     ),
+    "vfb_fp8_ffn_noalloc": (
+        ctypes.c_int,
+        [_vp, _c_int64, _c_int64, _c_int64, _vp, _vp, _c_int64, _vp, _vp, ctypes.c_int32, _vp, _vp, _vp,
+         _c_int64, _vp, _c_int64, _c_int64, _vp, _c_int64, _vp],
+    ),
     "vfb_bf16_gemm": (
         ctypes.c_int,
         [_vp, _c_int64, _vp, _c_int64, _c_int64, _c_int64, _c_int64, ctypes.POINTER(Epilogue), _vp],
