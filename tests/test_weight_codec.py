@@ -126,3 +126,97 @@ def test_sidecar_blocks_equal_file_blocks(tmp_path, world):
         got = pin_fp8_block_sidecars(pairs, layout, arena, rank=rank, world=world)
         for g, w in zip(got, want):
             assert torch.equal(g, w) and g.data_ptr() % ALIGN == 0
+
+
+# the failure cases of the reference's own sidecar tests (tests/test_weight_codec.py
+# of vflash), which need the zstandard module to run there
+
+
+def sidecar_case(tmp_path):
+    src = source_file(tmp_path)
+    manifest = prepare(src, tmp_path / "side", chunk_bytes=4096)
+    payload, offset = payload_of(src)
+    return src, tmp_path / "side", payload, dict(source_name=src.name, source_size=src.stat().st_size,
+                                                 header_bytes=offset), manifest
+
+
+@pytest.mark.parametrize("change", ["overlap", "oversize", "source", "name", "truncated", "symlink"])
+def test_inconsistent_or_unsafe_sidecars_are_refused(tmp_path, change):
+    src, side, payload, layout, manifest = sidecar_case(tmp_path)
+    if change == "overlap":
+        manifest["frames"][1][0] -= 1
+    elif change == "oversize":
+        manifest["frames"][0][2] = 12 * 1024**3
+    elif change == "source":
+        manifest["source_size"] += 1
+    elif change == "name":
+        manifest["source_name"] = "another.safetensors"
+    elif change == "truncated":
+        with (side / "payload.zst").open("r+b") as handle:
+            handle.truncate(5)
+    else:
+        (side / "payload.zst").rename(side / "real.zst")
+        (side / "payload.zst").symlink_to(side / "real.zst")
+    (side / "index.json").write_text(json.dumps(manifest))
+    with pytest.raises((ValueError, OSError)):
+        read_into(side, memoryview(bytearray(len(payload))), **layout)
+
+
+def test_short_positioned_reads_and_early_end(tmp_path, monkeypatch):
+    from vflash_b200.native import h3_weight_codec as codec
+
+    src, side, payload, layout, _manifest = sidecar_case(tmp_path)
+    real = codec.os.pread
+    monkeypatch.setattr(codec.os, "pread", lambda fd, n, at: real(fd, min(n, 7), at))
+    target = bytearray(len(payload))
+    read_into(side, memoryview(target), **layout)
+    assert bytes(target) == payload
+    monkeypatch.setattr(codec.os, "pread", lambda *args: b"")
+    with pytest.raises(ValueError, match="ended early"):
+        read_into(side, memoryview(target), **layout)
+
+
+def test_a_second_frame_inside_one_record_is_refused(tmp_path):
+    src, side, payload, layout, manifest = sidecar_case(tmp_path)
+    blob = side / "payload.zst"
+    raw = blob.read_bytes()
+    first = manifest["frames"][0][1]
+    extra = pa.Codec("zstd", compression_level=3).compress(b"not a declared frame", asbytes=True)
+    blob.write_bytes(raw[:first] + extra + raw[first:])
+    manifest["frames"][0][1] += len(extra)
+    for record in manifest["frames"][1:]:
+        record[0] += len(extra)
+    manifest["compressed_bytes"] += len(extra)
+    (side / "index.json").write_text(json.dumps(manifest))
+    with pytest.raises(ValueError, match="beyond its one frame"):
+        read_into(side, memoryview(bytearray(len(payload))), **layout)
+
+
+@pytest.mark.parametrize("kind", ["symlink", "fifo", "list"])
+def test_index_must_be_a_bounded_regular_object(tmp_path, kind):
+    import os
+
+    src, side, payload, layout, _manifest = sidecar_case(tmp_path)
+    index = side / "index.json"
+    if kind == "symlink":
+        index.rename(side / "real.json")
+        index.symlink_to(side / "real.json")
+    elif kind == "fifo":
+        index.unlink()
+        os.mkfifo(index)
+    else:
+        index.write_text("[]")
+    with pytest.raises((ValueError, OSError)):
+        read_into(side, memoryview(bytearray(len(payload))), **layout)
+
+
+def test_frame_length_walks_the_blocks():
+    from vflash_b200.native.h3_weight_codec import frame_length
+
+    codec = pa.Codec("zstd", compression_level=3)
+    for data in (b"a", bytes(5000), bytes(range(256)) * 300):
+        frame = codec.compress(data, asbytes=True)
+        assert frame_length(frame) == len(frame)
+        assert frame_length(frame + codec.compress(b"tail", asbytes=True)) == len(frame)
+        with pytest.raises(ValueError, match="truncated"):
+            frame_length(frame[:-1])

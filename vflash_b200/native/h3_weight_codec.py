@@ -14,7 +14,10 @@ The zstd codec is pyarrow's (the reference uses the ``zstandard`` module,
 which this image does not have; both produce and read standard RFC 8878
 frames).  The frame header is parsed here (``frame_parameters``) so that a
 frame's declared content size and window are checked before it is decoded,
-as the reference checks ``zstandard.get_frame_parameters``.
+as the reference checks ``zstandard.get_frame_parameters``, and its block
+headers are walked (``frame_length``) so that a record holding anything
+after its one frame is refused, as the reference's ``allow_extra_data=False``
+refuses it.
 
 ``pin_fp8_block_sidecars`` feeds the FP8 block ring from sidecars: only the
 frames that overlap this rank's share of each packed block are decoded, and
@@ -76,6 +79,36 @@ def frame_parameters(frame: bytes) -> tuple[int | None, int]:
     return content, window
 
 
+def frame_length(frame: bytes) -> int:
+    """Bytes of the zstd frame that starts ``frame``: header, blocks, optional checksum (RFC 8878 3.1.1).
+
+    Each block header is 3 bytes (little endian: bit 0 last block, bits 1-2
+    type, bits 3-23 size); a raw or compressed block carries ``size`` bytes,
+    an RLE block one byte, type 3 is reserved.
+    """
+    if len(frame) < 6 or int.from_bytes(frame[:4], "little") != ZSTD_MAGIC:
+        raise ValueError("compressed frame is not a zstd frame")
+    descriptor = frame[4]
+    fcs_flag, single_segment, checksum, dict_flag = (descriptor >> 6, (descriptor >> 5) & 1,
+                                                     (descriptor >> 2) & 1, descriptor & 3)
+    at = (5 + (0 if single_segment else 1) + (0, 1, 2, 4)[dict_flag]
+          + (1 if single_segment else 0, 2, 4, 8)[fcs_flag])
+    while True:
+        if len(frame) < at + 3:
+            raise ValueError("compressed frame is truncated")
+        header = int.from_bytes(frame[at:at + 3], "little")
+        last, kind, size = header & 1, (header >> 1) & 3, header >> 3
+        if kind == 3:
+            raise ValueError("compressed frame has a reserved block type")
+        at += 3 + (1 if kind == 1 else size)
+        if last:
+            break
+    at += 4 if checksum else 0
+    if len(frame) < at:
+        raise ValueError("compressed frame is truncated")
+    return at
+
+
 def prepare(source: Path, destination: Path, *, chunk_bytes=CHUNK):
     """Create one new sidecar; compare each decoded frame with its input."""
     from .h3_weight_files import read_header
@@ -102,7 +135,8 @@ def prepare(source: Path, destination: Path, *, chunk_bytes=CHUNK):
                 raise ValueError("source ended during compression")
             compressed = codec.compress(data, asbytes=True)
             content, _window = frame_parameters(compressed)
-            if content != len(data) or codec.decompress(compressed, len(data), asbytes=True) != data:
+            if (content != len(data) or frame_length(compressed) != len(compressed)
+                    or codec.decompress(compressed, len(data), asbytes=True) != data):
                 raise ValueError("compressed frame differs from its source")
             records.append([output.tell(), len(compressed), len(data)])
             output.write(compressed)
@@ -196,6 +230,8 @@ def _decode_frames(directory: Path, plan: list[tuple], compressed_bytes: int, si
             content, window = frame_parameters(frame)
             if content != decoded or window is None or window > CHUNK:
                 raise ValueError("compressed frame content/window exceeds declaration")
+            if frame_length(frame) != packed:
+                raise ValueError("compressed record holds data beyond its one frame")
             value = codec.decompress(frame, decoded, asbytes=True)
             if len(value) != decoded:
                 raise ValueError("decoded frame size differs")
