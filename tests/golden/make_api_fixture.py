@@ -19,7 +19,8 @@ import inspect
 import json
 from pathlib import Path
 
-MODULES = ("h3_fp8_linear", "h3_fp8_activation", "h3_nvfp4_linear", "h3_fused_ops", "h3_weight_codec")
+MODULES = ("h3_fp8_linear", "h3_fp8_activation", "h3_nvfp4_linear", "h3_fused_ops", "h3_weight_codec",
+           "h3_buffered_weights")
 HOOKS = {"_require_device", "_operators", "_quantize_activation_torch"}
 
 
