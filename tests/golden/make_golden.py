@@ -61,7 +61,7 @@ def outlier_matrix(rows, cols, seed):
 
 def main() -> None:
     parser = argparse.ArgumentParser()
-    parser.add_argument("--reference-src", default="/root/reference/src")
+    parser.add_argument("--reference-src", required=True, help="the src/ directory of a vflash checkout")
     args = parser.parse_args()
     sys.path.insert(0, args.reference_src)
     import torch
