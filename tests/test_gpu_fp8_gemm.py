@@ -20,8 +20,7 @@ import torch
 
 from oracle import epilogues as ep
 from oracle import fp8
-from tests.helpers import (bf16_close, bits_of, codes_of, fp8_weight, outlier_activations,
-                           to_bf16_tensor)
+from tests.helpers import bf16_close, bits_of, codes_of, fp8_weight, outlier_activations
 from vflash_b200 import _lib
 from vflash_b200.kernels import Epilogue, fp8_gemm, quantize_fp8_rows
 

@@ -14,8 +14,6 @@ failure has run every other test before it.
 
 from __future__ import annotations
 
-import ctypes
-
 import pytest
 import torch
 
