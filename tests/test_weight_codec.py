@@ -11,7 +11,8 @@ from tests.test_weight_files import SHAPES, random_block, write_block
 from vflash_b200.native.h3_pinned_arena import ALIGN, BlockLayout, PinnedHostArena
 from vflash_b200.native.h3_weight_codec import (ZSTD_MAGIC, frame_parameters, pin_fp8_block_sidecars, prepare,
                                                 read_into)
-from vflash_b200.native.h3_weight_files import pin_fp8_block_files, read_header
+from vflash_b200.native.h3_buffered_weights import payload_header
+from vflash_b200.native.h3_weight_files import pin_fp8_block_files
 
 pytest.importorskip("safetensors.torch")
 pa = pytest.importorskip("pyarrow")
@@ -26,7 +27,7 @@ def source_file(tmp_path, seed=0, name="block.safetensors"):
 
 
 def payload_of(path):
-    offset, _ = read_header(path)
+    offset, _ = payload_header(path)
     return path.read_bytes()[offset:], offset
 
 
@@ -220,3 +221,16 @@ def test_frame_length_walks_the_blocks():
         assert frame_length(frame + codec.compress(b"tail", asbytes=True)) == len(frame)
         with pytest.raises(ValueError, match="truncated"):
             frame_length(frame[:-1])
+
+
+def test_prepare_accepts_any_dense_dtype_the_reference_accepts(tmp_path):
+    path = tmp_path / "mixed.safetensors"
+    from safetensors.torch import save_file
+
+    save_file({"a": torch.arange(6, dtype=torch.float64), "b": torch.ones(3, dtype=torch.int16)}, str(path))
+    manifest = prepare(path, tmp_path / "side", chunk_bytes=4096)
+    payload, offset = payload_of(path)
+    target = bytearray(len(payload))
+    read_into(tmp_path / "side", memoryview(target), source_name=path.name, source_size=path.stat().st_size,
+              header_bytes=offset)
+    assert bytes(target) == payload and manifest["payload_bytes"] == len(payload)

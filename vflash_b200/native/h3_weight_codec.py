@@ -111,13 +111,13 @@ def frame_length(frame: bytes) -> int:
 
 def prepare(source: Path, destination: Path, *, chunk_bytes=CHUNK):
     """Create one new sidecar; compare each decoded frame with its input."""
-    from .h3_weight_files import read_header
+    from .h3_buffered_weights import payload_header
 
     source, destination = Path(source), Path(destination)
     if type(chunk_bytes) is not int or not 4096 <= chunk_bytes <= CHUNK:
         raise ValueError("bounded compression chunks required")
     before = source.stat()
-    offset, _ = read_header(source)
+    offset, _ = payload_header(source)
     payload = before.st_size - offset
     if not 0 < payload <= MAX_FILE or destination.exists() or destination.is_symlink():
         raise ValueError("one bounded source and a new destination required")
