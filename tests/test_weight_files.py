@@ -109,3 +109,15 @@ def test_wrong_dtype_or_missing_tensor_is_rejected(tmp_path):
     safetensors_torch.save_file(tensors, str(path))
     with pytest.raises(ValueError, match="no tensor attn.out.weight.row_scale"):
         pin_fp8_block_files([path], layout, arena)
+
+
+def test_block_files_may_carry_tensors_of_other_dtypes(tmp_path):
+    layout = BlockLayout.for_shapes(SHAPES)
+    block = random_block(7)
+    path = tmp_path / "b.safetensors"
+    write_block(path, block, extra={"x.f64": torch.ones(3, dtype=torch.float64),
+                                    "x.flag": torch.tensor([True, False]), "x.i16": torch.arange(4, dtype=torch.int16)})
+    arena = PinnedHostArena(1 << 20, pin_memory=False)
+    got = pin_fp8_block_files([path], layout, arena)[0]
+    want = pin_blocks(layout, [block], arena)[0]
+    assert torch.equal(got, want)

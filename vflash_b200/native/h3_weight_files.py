@@ -33,7 +33,9 @@ import torch
 from .h3_pinned_arena import BlockLayout, PinnedHostArena
 
 HEADER_LIMIT = 100 * 1024 * 1024
-DTYPE_BYTES = {"F8_E4M3": 1, "F32": 4, "BF16": 2, "F16": 2, "U8": 1, "I8": 1, "I32": 4, "I64": 8}
+# element sizes of the safetensors dtypes (a block file may carry tensors of any of them)
+DTYPE_BYTES = {"F64": 8, "F32": 4, "F16": 2, "BF16": 2, "F8_E4M3": 1, "F8_E5M2": 1, "I64": 8, "I32": 4,
+               "I16": 2, "I8": 1, "U64": 8, "U32": 4, "U16": 2, "U8": 1, "BOOL": 1}
 
 # block linear -> safetensors key of its FP8 codes (the scales are key + ".row_scale")
 FP8_BLOCK_KEYS = {"qkv": "attn.qkv.weight", "attention_out": "attn.out.weight",
