@@ -248,6 +248,10 @@ VFB_API int vfb_fp8_ffn(const void *x, int64_t M, int64_t H, int64_t ldx,
  * (vfb_fp8_ffn_workspace_bytes(M, H, F) > 64 MiB) are rejected with
  * VFB_EINVAL.  The first call on a device looks the array's address up
  * (cudaGetSymbolAddress); make that first call before any stream capture.
+ * A cudaDeviceReset gives the device a new context in which the array has a
+ * new address: the first call after it looks the address up again (the
+ * library keeps each cached address with the id of its context), so that
+ * call, too, belongs before any capture.
  * All calls on a device share the array: calls whose kernels may overlap on
  * the GPU (other streams, unordered host threads) race, so order them. */
 VFB_API int vfb_fp8_ffn_noalloc(const void *x, int64_t M, int64_t H, int64_t ldx,

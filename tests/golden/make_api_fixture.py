@@ -6,10 +6,6 @@ defaults, and for classes the public methods.  tests/test_api_surface.py checks
 the drop-in modules against it.
 
     PYTHONPATH=<vflash>/src python tests/golden/make_api_fixture.py
-
-The reference's h3_weight_codec imports ``zstandard`` at module level; where
-that package is absent a placeholder module is installed before the import,
-which is enough to read signatures.
 """
 
 from __future__ import annotations
@@ -19,8 +15,7 @@ import inspect
 import json
 from pathlib import Path
 
-MODULES = ("h3_fp8_linear", "h3_fp8_activation", "h3_nvfp4_linear", "h3_fused_ops", "h3_weight_codec",
-           "h3_buffered_weights")
+MODULES = ("h3_fp8_linear", "h3_fp8_activation", "h3_nvfp4_linear", "h3_fused_ops")
 HOOKS = {"_require_device", "_operators", "_quantize_activation_torch"}
 
 
@@ -33,15 +28,6 @@ def describe(fn) -> list:
 
 
 def main() -> None:
-    import sys
-    import types
-
-    # h3_weight_codec imports the zstandard module at import time; only its
-    # signatures are recorded here, so a placeholder stands in where it is absent
-    try:
-        import zstandard  # noqa: F401
-    except ImportError:
-        sys.modules["zstandard"] = types.ModuleType("zstandard")
     api = {}
     for short in MODULES:
         name = f"vflash.native.{short}"

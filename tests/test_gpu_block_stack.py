@@ -115,16 +115,6 @@ def test_stack_from_block_files_equals_in_memory(tmp_path):
     for host in stack.host_blocks:
         assert host.is_pinned()
     assert torch.equal(stack.forward(hidden, gate), want)
-    # the same blocks decoded from framed zstd sidecars
-    pa = pytest.importorskip("pyarrow")
-    if pa.Codec.is_available("zstd"):
-        from vflash_b200.native.h3_weight_codec import prepare
-
-        sidecars = [tmp_path / f"block_{i}.zst.d" for i in range(len(paths))]
-        for path, side in zip(paths, sidecars):
-            prepare(path, side, chunk_bytes=1 << 16)
-        from_sidecars = FP8BlockStack.from_files(paths, H, F, DEV, chunk_bytes=1 << 20, sidecars=sidecars)
-        assert torch.equal(from_sidecars.forward(hidden, gate), want)
 
 
 def test_graph_replay_of_a_resident_stack_equals_eager():

@@ -3,8 +3,7 @@
 Each property is what a kernel or a copy assumes: 256-byte aligned, disjoint
 fields inside a packed block that splits evenly between ranks; row
 partitions that cover every token once; chunk plans that cover every row once
-with aligned starts; weight shards that reassemble the matrix in branch order;
-sidecar frames that reassemble the payload whatever the chunk size.
+with aligned starts; weight shards that reassemble the matrix in branch order.
 """
 
 from __future__ import annotations
@@ -78,26 +77,3 @@ def test_weight_shards_reassemble_in_branch_order(world, parts, piece, other, ax
     for b in range(parts):
         pieces = [s.narrow(axis, b * piece, piece) for s in shards]
         assert torch.equal(torch.cat(pieces, dim=axis), matrix.narrow(axis, b * width, width))
-
-
-@settings(max_examples=25, deadline=None)
-@given(st.binary(min_size=1, max_size=40000), st.sampled_from([4096, 5000, 8192, 65536]))
-def test_sidecar_frames_reassemble_the_payload(tmp_path_factory, payload, chunk):
-    pa = pytest.importorskip("pyarrow")
-    if not pa.Codec.is_available("zstd"):
-        pytest.skip("pyarrow without zstd")
-    from safetensors.torch import save_file
-
-    from vflash_b200.native.h3_weight_codec import prepare, read_into
-    from vflash_b200.native.h3_weight_files import read_header
-
-    root = tmp_path_factory.mktemp("side")
-    path = root / "w.safetensors"
-    save_file({"blob": torch.frombuffer(bytearray(payload), dtype=torch.uint8)}, str(path))
-    manifest = prepare(path, root / "sidecar", chunk_bytes=chunk)
-    offset, _ = read_header(path)
-    target = bytearray(path.stat().st_size - offset)
-    read_into(root / "sidecar", memoryview(target), source_name=path.name, source_size=path.stat().st_size,
-              header_bytes=offset)
-    assert bytes(target) == path.read_bytes()[offset:]
-    assert all(decoded <= chunk for _, _, decoded in manifest["frames"])

@@ -1,6 +1,7 @@
 // Error reporting, device checks and the device status word of the C ABI.
 #include <cstdarg>
 #include <cstdio>
+#include <atomic>
 #include <cstring>
 #include <mutex>
 
@@ -15,7 +16,8 @@ thread_local char g_last_error[512] = "";
 constexpr int kMaxDevices = 64;
 std::mutex g_mutex;
 int g_sm_count[kMaxDevices];          // 0 = not queried yet
-int *g_status_ptr[kMaxDevices];       // device address of g_device_status
+int *g_status_ptr[kMaxDevices];       // device address of g_device_status ...
+uint64_t g_status_ctx[kMaxDevices];   // ... in the context with this id
 
 }  // namespace
 
@@ -56,17 +58,69 @@ int check_device(int *sm_count) {
   return VFB_OK;
 }
 
-// Device address of this device's status word (looked up once per device).
+// Unique id (never 0) of the calling thread's current CUDA context, or 0 if
+// it cannot be read.  Device addresses of the library's __device__ variables
+// and the kernels' shared-memory opt-ins belong to one context: a
+// cudaDeviceReset ends it and the next runtime call creates a new primary
+// context with a new id, so every per-device cache below is keyed by this id.
+uint64_t current_context_id() {
+  static PFN_cuCtxGetCurrent_v4000 get_current = nullptr;
+  static PFN_cuCtxGetId_v12000 get_id = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void *ptr = nullptr;
+    cudaDriverEntryPointQueryResult qres;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &ptr, cudaEnableDefault, &qres) == cudaSuccess &&
+        qres == cudaDriverEntryPointSuccess)
+      get_current = reinterpret_cast<PFN_cuCtxGetCurrent_v4000>(ptr);
+    ptr = nullptr;
+    if (cudaGetDriverEntryPoint("cuCtxGetId", &ptr, cudaEnableDefault, &qres) == cudaSuccess &&
+        qres == cudaDriverEntryPointSuccess)
+      get_id = reinterpret_cast<PFN_cuCtxGetId_v12000>(ptr);
+  });
+  if (get_current == nullptr || get_id == nullptr) return 0;
+  CUcontext ctx = nullptr;
+  if (get_current(&ctx) != CUDA_SUCCESS || ctx == nullptr) {
+    // no context is current yet: make the current device's primary context
+    // current (cudaSetDevice initialises it) and read it again
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || cudaSetDevice(dev) != cudaSuccess) return 0;
+    if (get_current(&ctx) != CUDA_SUCCESS || ctx == nullptr) return 0;
+  }
+  unsigned long long id = 0;
+  if (get_id(ctx, &id) != CUDA_SUCCESS) return 0;
+  return static_cast<uint64_t>(id) + 1;
+}
+
+// Device address of this device's status word, looked up once per device and
+// context (again after a device reset).
 int *device_status_ptr() {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return nullptr;
+  const uint64_t ctx = current_context_id();
   std::lock_guard<std::mutex> lock(g_mutex);
-  if (g_status_ptr[dev] == nullptr) {
+  if (g_status_ptr[dev] == nullptr || ctx == 0 || g_status_ctx[dev] != ctx) {
     void *ptr = nullptr;
     if (cudaGetSymbolAddress(&ptr, g_device_status) != cudaSuccess) return nullptr;
     g_status_ptr[dev] = static_cast<int *>(ptr);
+    g_status_ctx[dev] = ctx;
   }
   return g_status_ptr[dev];
+}
+
+// Sets the dynamic shared-memory opt-in of `kernel` once per device and
+// context; `done` holds, per device, the context id it was last set in.
+int ensure_smem_optin(const void *kernel, int bytes, std::atomic<uint64_t> *done) {
+  int dev = 0;
+  cudaError_t err = cudaGetDevice(&dev);
+  if (err != cudaSuccess) return set_error(VFB_ECUDA, "cudaGetDevice: %s", cudaGetErrorString(err));
+  const uint64_t ctx = current_context_id();
+  const bool cached = dev >= 0 && dev < kMaxAttrDevices && ctx != 0;
+  if (cached && done[dev].load(std::memory_order_acquire) == ctx) return VFB_OK;
+  err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (err != cudaSuccess) return set_error(VFB_ECUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(err));
+  if (cached) done[dev].store(ctx, std::memory_order_release);
+  return VFB_OK;
 }
 
 // cuTensorMapEncodeTiled from the driver, looked up once through the runtime

@@ -520,9 +520,13 @@ constexpr int kMaxAttrDevices = 64;
 
 // Host-side helpers implemented in capi.cu.
 #include <cudaTypedefs.h>
+
+#include <atomic>
 namespace vfb {
 int set_error(int code, const char *fmt, ...);
 int check_device(int *sm_count);
+uint64_t current_context_id();
 int *device_status_ptr();
+int ensure_smem_optin(const void *kernel, int bytes, std::atomic<uint64_t> *done);
 PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder();
 }  // namespace vfb

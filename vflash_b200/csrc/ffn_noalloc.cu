@@ -14,7 +14,9 @@
 // intermediates need more are rejected.  Host code reaches it only through
 // cudaGetSymbolAddress (the host-side name is a stand-in, not a device
 // address), looked up once per device, with that device current, on the
-// first call made on that device.
+// first call made on that device -- and again on the first call after a
+// cudaDeviceReset, whose new context places the array at a new address (the
+// cached address is kept with the id of the context it belongs to).
 //
 // All calls on a device share the array.  Two calls whose kernels overlap on
 // the GPU (different streams, or different host threads without ordering)
@@ -36,8 +38,10 @@ static __device__ __align__(256) uint8_t g_ffn_scratch[kScratchBytes];
 
 std::mutex g_scratch_mutex;
 void *g_scratch_ptr[kMaxAttrDevices] = {};
+uint64_t g_scratch_ctx[kMaxAttrDevices] = {};  // id of the context g_scratch_ptr[dev] belongs to
 
-// Device address of the array on the current device (looked up once).
+// Device address of the array on the current device, looked up once per
+// device and context.
 int scratch_address(void **out) {
   int dev = 0;
   cudaError_t err = cudaGetDevice(&dev);
@@ -45,13 +49,15 @@ int scratch_address(void **out) {
   if (dev < 0 || dev >= kMaxAttrDevices)
     return set_error(VFB_EINVAL, "vfb_fp8_ffn_noalloc: device %d is beyond the supported %d", dev,
                      kMaxAttrDevices);
+  const uint64_t ctx = current_context_id();
   std::lock_guard<std::mutex> lock(g_scratch_mutex);
-  if (g_scratch_ptr[dev] == nullptr) {
+  if (g_scratch_ptr[dev] == nullptr || ctx == 0 || g_scratch_ctx[dev] != ctx) {
     void *ptr = nullptr;
     err = cudaGetSymbolAddress(&ptr, g_ffn_scratch);
     if (err != cudaSuccess || ptr == nullptr)
       return set_error(VFB_ECUDA, "vfb_fp8_ffn_noalloc: cudaGetSymbolAddress: %s", cudaGetErrorString(err));
     g_scratch_ptr[dev] = ptr;
+    g_scratch_ctx[dev] = ctx;
   }
   *out = g_scratch_ptr[dev];
   return VFB_OK;
@@ -66,8 +72,14 @@ extern "C" int vfb_fp8_ffn_noalloc(const void *x, int64_t M, int64_t H, int64_t 
                                    const void *residual, int64_t ldr, const void *gate, int64_t gate_token_stride,
                                    int64_t tokens, void *out, int64_t ldo, void *stream) {
   using namespace vfb;
+  if (activation != VFB_EPI_GELU_TANH && activation != VFB_EPI_SWIGLU)
+    return set_error(VFB_EINVAL, "vfb_fp8_ffn_noalloc: activation must be VFB_EPI_GELU_TANH or VFB_EPI_SWIGLU");
   const int64_t width = activation == VFB_EPI_SWIGLU ? n_up / 2 : n_up;
   const int64_t need = vfb_fp8_ffn_workspace_bytes(M, H, width);
+  if (need < 0 || (activation == VFB_EPI_SWIGLU && n_up % 2))
+    return set_error(VFB_EINVAL, "vfb_fp8_ffn_noalloc: need 16 <= H <= 32768 and 32 <= F <= 32768, both "
+                                 "multiples of 32 (F = n_up, or n_up / 2 for SWIGLU), M >= 0 (M=%lld H=%lld "
+                                 "n_up=%lld)", (long long)M, (long long)H, (long long)n_up);
   if (need > kScratchBytes)
     return set_error(VFB_EINVAL,
                      "vfb_fp8_ffn_noalloc: these shapes need %lld bytes of intermediates, more than the "

@@ -664,17 +664,10 @@ template <int EPI, int OPS = OPS_E4M3>
 int launch(const CUtensorMap &a, const CUtensorMap &b, const CUtensorMap &b2, const CUtensorMap &o,
            const GemmParams &p, int sm_count, cudaStream_t stream) {
   auto kernel = fp8_gemm_kernel<EPI, OPS>;
-  // the shared-memory opt-in is a per-device function attribute: set it once
-  static std::atomic<bool> smem_set[kMaxAttrDevices];
-  int dev = 0;
-  cudaError_t err = cudaGetDevice(&dev);
-  if (err != cudaSuccess) return set_error(VFB_ECUDA, "cudaGetDevice: %s", cudaGetErrorString(err));
-  if (dev < 0 || dev >= kMaxAttrDevices || !smem_set[dev].load(std::memory_order_acquire)) {
-    err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
-    if (err != cudaSuccess)
-      return set_error(VFB_ECUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(err));
-    if (dev >= 0 && dev < kMaxAttrDevices) smem_set[dev].store(true, std::memory_order_release);
-  }
+  // the shared-memory opt-in is a function attribute of the device's context: set it once per context
+  static std::atomic<uint64_t> smem_set[kMaxAttrDevices];
+  int rc = ensure_smem_optin(reinterpret_cast<const void *>(kernel), static_cast<int>(SMEM_BYTES), smem_set);
+  if (rc != VFB_OK) return rc;
   // Persistent grid of CTA pairs, one CTA per SM.
   const int tiles = p.num_m_tiles * p.num_n_tiles;
   const int max_pairs = sm_count / 2;
@@ -691,7 +684,7 @@ int launch(const CUtensorMap &a, const CUtensorMap &b, const CUtensorMap &b2, co
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  err = cudaLaunchKernelEx(&cfg, kernel, a, b, b2, o, p);
+  cudaError_t err = cudaLaunchKernelEx(&cfg, kernel, a, b, b2, o, p);
   if (err != cudaSuccess)
     return set_error(VFB_ECUDA, "vfb_fp8_gemm launch: %s", cudaGetErrorString(err));
   return VFB_OK;

@@ -400,16 +400,11 @@ extern "C" int vfb_nvfp4_gemm(const void *A, const void *sfa, const void *W, con
                    CU_TENSOR_MAP_SWIZZLE_NONE)) != VFB_OK)
     return rc;
   if ((rc = map_out(&to, out, N / planes, M, planes)) != VFB_OK) return rc;
-  // the shared-memory opt-in is a per-device function attribute: set it once
-  static std::atomic<bool> smem_set[kMaxAttrDevices];
-  int dev = 0;
-  cudaError_t err = cudaGetDevice(&dev);
-  if (err != cudaSuccess) return set_error(VFB_ECUDA, "cudaGetDevice: %s", cudaGetErrorString(err));
-  if (dev < 0 || dev >= kMaxAttrDevices || !smem_set[dev].load(std::memory_order_acquire)) {
-    err = cudaFuncSetAttribute(nvfp4_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
-    if (err != cudaSuccess) return set_error(VFB_ECUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(err));
-    if (dev >= 0 && dev < kMaxAttrDevices) smem_set[dev].store(true, std::memory_order_release);
-  }
+  // the shared-memory opt-in is a function attribute of the device's context: set it once per context
+  static std::atomic<uint64_t> smem_set[kMaxAttrDevices];
+  if ((rc = ensure_smem_optin(reinterpret_cast<const void *>(nvfp4_gemm_kernel), static_cast<int>(SMEM_BYTES),
+                              smem_set)) != VFB_OK)
+    return rc;
   const int tiles = p.num_m_tiles * p.num_n_tiles;
   const int max_pairs = sms / 2;
   const int pairs = tiles < max_pairs ? tiles : max_pairs;
@@ -425,7 +420,7 @@ extern "C" int vfb_nvfp4_gemm(const void *A, const void *sfa, const void *W, con
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  err = cudaLaunchKernelEx(&cfg, nvfp4_gemm_kernel, ta, tb, tsa, tsb, to, p);
+  cudaError_t err = cudaLaunchKernelEx(&cfg, nvfp4_gemm_kernel, ta, tb, tsa, tsb, to, p);
   if (err != cudaSuccess) return set_error(VFB_ECUDA, "vfb_nvfp4_gemm launch: %s", cudaGetErrorString(err));
   return VFB_OK;
 }

@@ -86,20 +86,14 @@ class FP8BlockStack:
 
     @classmethod
     def from_files(cls, paths, hidden: int, ffn: int, device, *, group=None, resident: bool = False,
-                   chunk_bytes: int = 2 * 1024**3, execution: RowFP8Execution | None = None,
-                   sidecars=None) -> FP8BlockStack:
+                   chunk_bytes: int = 2 * 1024**3, execution: RowFP8Execution | None = None) -> FP8BlockStack:
         """A stack whose blocks are read from the reference's per-block safetensors files.
 
         Each rank reads only its share of every block, straight into pinned
-        memory (``h3_weight_files.pin_fp8_block_files``).  With ``sidecars``
-        (one framed-zstd sidecar directory per file, as
-        ``h3_weight_codec.prepare`` writes them) the bytes are decoded from
-        the sidecars instead, only the frames of this rank's share
-        (``h3_weight_codec.pin_fp8_block_sidecars``).
+        memory (``h3_weight_files.pin_fp8_block_files``).
         """
         import torch.distributed as dist
 
-        from .h3_weight_codec import pin_fp8_block_sidecars
         from .h3_weight_files import pin_fp8_block_files
 
         self = cls.__new__(cls)
@@ -109,14 +103,7 @@ class FP8BlockStack:
         self.layout = BlockLayout.for_shapes(block_shapes(hidden, ffn), multiple=ALIGN * world)
         chunk = self.layout.nbytes // world
         self.arena = PinnedHostArena(max(chunk_bytes, 1 << (chunk - 1).bit_length()))
-        if sidecars is None:
-            self.host_blocks = pin_fp8_block_files(paths, self.layout, self.arena, rank=rank, world=world)
-        else:
-            paths, sidecars = list(paths), list(sidecars)
-            if len(paths) != len(sidecars):
-                raise ValueError("one sidecar per block file")
-            self.host_blocks = pin_fp8_block_sidecars(zip(paths, sidecars), self.layout, self.arena, rank=rank,
-                                                      world=world)
+        self.host_blocks = pin_fp8_block_files(paths, self.layout, self.arena, rank=rank, world=world)
         self.arena.close()
         self.ring = FP8BlockRing(self.layout, self.host_blocks, device, group=group, resident=resident)
         self.execution = execution or RowFP8Execution("w8a8")
