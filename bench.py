@@ -392,6 +392,17 @@ def _timed(fn, flush, stream, reps: int = 50, warmup: int = 10) -> list[float]:
     return [a.elapsed_time(b) for a, b in times]
 
 
+def _chain_output(x, up, ups, down, downs, m):
+    """Config 2's FFN as four separate launches (quantiser, up GEMM + GELU, requantiser, down GEMM + residual)."""
+    from vflash_b200 import _lib
+    from vflash_b200.kernels import Epilogue, fp8_gemm, quantize_fp8_rows
+
+    c, s = quantize_fp8_rows(x)
+    mid = fp8_gemm(c, s, m, up, ups, Epilogue(kind=_lib.EPI_GELU_TANH))
+    mc, ms_ = quantize_fp8_rows(mid)
+    return fp8_gemm(mc, ms_, m, down, downs, Epilogue(kind=_lib.EPI_RESIDUAL, residual=x))
+
+
 def nvfp4_cpu_baseline(ac, asf, wp, wsc, alpha, seconds: float) -> dict:
     """NVFP4 has no reference CPU path: the oracle's dequantise-then-fp32-matmul on a row sample."""
     from oracle.nvfp4 import dequant_matmul_f32
@@ -582,14 +593,22 @@ def other_configs(device, flush, stream, cpu_seconds: float = 0.0) -> dict:
                 "QKV epilogue; vs planar QKV then per branch cuBLAS linear(linear(x, down), up) * s + add"}
     del xq, wq, wqs, rc, rs, ang, residuals
 
-    # c2: fused FFN, GELU-tanh, per-token requant of the intermediate, residual
+    # c2: fused FFN, GELU-tanh, per-token requant of the intermediate, residual:
+    # the one-kernel FFN (vfb_fp8_ffn: quantiser + fused up/requant/down launch)
+    # and, for comparison, the same chain as four separate launches
+    from vflash_b200.kernels import fp8_ffn
+
     m, h, f = 32760, 4096, 16384
     x = seeded(m, h, 1002)
     up, ups = quantize_fp8_rows(seeded(f, h, 2020, std=0.02), pad_to=1)
     down, downs = quantize_fp8_rows(seeded(h, f, 2021, std=0.02), pad_to=1)
     ev = [torch.cuda.Event(enable_timing=True) for _ in range(5)]
+    ffn_flop = 2.0 * m * f * h * 2
 
-    def c2():
+    def c2_fused():
+        fp8_ffn(x, up, ups, down, downs, activation=_lib.EPI_GELU_TANH, residual=x)
+
+    def c2_chain():
         ev[0].record(stream)
         c, s = quantize_fp8_rows(x)
         ev[1].record(stream)
@@ -600,14 +619,19 @@ def other_configs(device, flush, stream, cpu_seconds: float = 0.0) -> dict:
         fp8_gemm(mc, ms_, m, down, downs, Epilogue(kind=_lib.EPI_RESIDUAL, residual=x))
         ev[4].record(stream)
 
-    ms = _timed(c2, flush, stream)
+    fused_ms = _timed(c2_fused, flush, stream)
+    chain_ms = statistics.median(_timed(c2_chain, flush, stream))
     parts = [ev[i].elapsed_time(ev[i + 1]) for i in range(4)]
+    same = bool(torch.equal(fp8_ffn(x, up, ups, down, downs, activation=_lib.EPI_GELU_TANH, residual=x),
+                            _chain_output(x, up, ups, down, downs, m)))
     out["c2_fp8_ffn_gelu"] = summary(
-        ms, 2.0 * m * f * h * 2, fp8_peak,
-        {"step": "quant X, up GEMM + GELU-tanh epilogue, per-token requant of the bf16 intermediate, "
-                 "down GEMM + residual epilogue (four launches; intermediate round-trips HBM)",
-         "last_step_ms": {"quant_x": round(parts[0], 4), "up_gemm_gelu": round(parts[1], 4),
-                          "requant_mid": round(parts[2], 4), "down_gemm_residual": round(parts[3], 4)}})
+        fused_ms, ffn_flop, fp8_peak,
+        {"step": "vfb_fp8_ffn: quant X, then ONE kernel: up GEMM + GELU-tanh epilogue, per-token requant of "
+                 "the bf16 intermediate in L2, down GEMM + residual epilogue",
+         "four_launch_chain_ms": round(chain_ms, 4),
+         "four_launch_last_step_ms": {"quant_x": round(parts[0], 4), "up_gemm_gelu": round(parts[1], 4),
+                                      "requant_mid": round(parts[2], 4), "down_gemm_residual": round(parts[3], 4)},
+         "equals_four_launch_chain": same})
     del up, ups
 
     # c2 SwiGLU variant (the reference model's packed FFN input [2F, H]) through
@@ -623,8 +647,8 @@ def other_configs(device, flush, stream, cpu_seconds: float = 0.0) -> dict:
     ms = _timed(c2_swiglu, flush, stream)
     out["c2_fp8_ffn_swiglu"] = summary(
         ms, 2.0 * m * (2 * f) * h + 2.0 * m * f * h, fp8_peak,
-        {"step": "RowFP8Execution.ffn(activation='swiglu'): quant X, packed up GEMM [2F,H] with "
-                 "value * bf16(silu(gate)) epilogue, requant, down GEMM + residual"})
+        {"step": "RowFP8Execution.ffn(activation='swiglu'): quant X, then one kernel: packed up GEMM [2F,H] "
+                 "with value * bf16(silu(gate)), requant in L2, down GEMM + residual"})
     del x, packed, packeds, down, downs
 
     # c3: NVFP4 linear, M = 32760, K = 4096, N in {4096, 16384}
@@ -720,6 +744,14 @@ def stack_config(args, device, rank: int, world: int, barrier, max_over_ranks) -
     steps = args.stack_steps
     streamed_ms, out = timed(stack.forward, steps)
     finite = bool(torch.isfinite(out[:valid].float()).all())
+    # one more streamed step with CUDA events around each block's host copy and
+    # all-gather on the copy stream (the weight path's own cost per block)
+    stack.ring.profile = True
+    stack.forward(shard, gate)
+    torch.cuda.synchronize(device)
+    h2d_ms, gather_ms, profiled = stack.ring.copy_times()
+    stack.ring.profile = False
+    h2d_ms, gather_ms = max_over_ranks(h2d_ms), max_over_ranks(gather_ms)
     resident_ring = FP8BlockRing(stack.layout, stack.host_blocks, device, group=group, resident=True)
     resident_ms, out2 = timed(
         lambda h, g: resident_ring.run(h, lambda w, x: block_linears(stack.execution, w, x, g)), steps)
@@ -742,6 +774,7 @@ def stack_config(args, device, rank: int, world: int, barrier, max_over_ranks) -
     return {
         "workload": f"c4: {blocks} blocks x FP8 linears (QKV [12288,4096], out [4096,4096], up [16384,4096] "
                     f"GELU-tanh, down [4096,16384]); M={STACK_TOKENS} tokens, {rows} per rank",
+        "scaling": "strong (the M=65520 tokens are split over the ranks, weights replicated)",
         "streamed_ms_per_step": round(streamed_ms, 2),
         "resident_ms_per_step": round(resident_ms, 2),
         "resident_graph_ms_per_step": round(graph_ms, 2),
@@ -752,6 +785,10 @@ def stack_config(args, device, rank: int, world: int, barrier, max_over_ranks) -
         "frac_of_sustained_peak": round(per_gpu_tflops / fp8_peak, 4),
         "weight_bytes_per_block": stack.weight_bytes_per_block,
         "h2d_bytes_per_rank_per_step": blocks * stack.ring.chunk,
+        "copy_stream_per_block_ms": {"host_copy": round(h2d_ms, 4), "all_gather": round(gather_ms, 4),
+                                     "blocks_profiled": profiled,
+                                     "note": "CUDA events on the copy stream, max over ranks; overlapped "
+                                             "with the compute stream"},
         "weight_path": "pinned arena -> copy stream (two slots)" + (
             f", each rank copies 1/{world} of a block and NCCL all-gathers the rest" if world > 1 else ""),
         "output_finite": finite,

@@ -213,23 +213,41 @@ VFB_API int vfb_fp8_gemm(const void *A, int64_t lda, const float *sa,
 VFB_API int vfb_bf16_gemm(const void *A, int64_t lda, const void *W, int64_t ldw,
                   int64_t M, int64_t N, int64_t K, const vfb_epilogue *ep, void *stream);
 
-/* Fused FP8 FFN in one call: replaces RowFP8Execution.ffn's sequence (the
- * FFN input and output linears of the H3 block, src/vflash/native/
- * h3_native_denoiser.py:561-576, with the reference's per-token activation
- * quantiser before each, h3_fp8_linear.py:92-121): vfb_fp8_quant_rows(x) ->
- * vfb_fp8_gemm(activation = VFB_EPI_GELU_TANH with w_up [F, H], or
- * VFB_EPI_SWIGLU with the packed w_up [2F, H]; bias_up) -> vfb_fp8_quant_rows
- * of the bf16 intermediate [M, F] -> vfb_fp8_gemm(w_down [H, F]; bias_down;
- * RESIDUAL with residual [M, H] (row stride ldr) and optional gate [tokens, H]
- * (row stride gate_token_stride), else STORE) into out [M, H] (row stride
- * ldo).  Same kernels and bits as the separate calls.  x: bf16 [M, H], row
- * stride ldx; s_up [n_up], s_down [H] fp32.  H and F multiples of 32, at most
- * 32768.  The intermediates live in `workspace` (256-byte aligned, at least
- * vfb_fp8_ffn_workspace_bytes(M, H, F) bytes, F = intermediate width); the
- * call allocates nothing.  vfb_fp8_ffn_workspace_bytes returns -1 for an
- * invalid shape. */
+/* Fused FP8 FFN in one call: replaces the FFN input and output linears of
+ * the H3 block (src/vflash/native/h3_native_denoiser.py:561-576) with the
+ * reference's per-token activation quantiser before each
+ * (h3_fp8_linear.py:92-121):
+ *   vfb_fp8_quant_rows(x)
+ *   -> up GEMM with the activation epilogue (VFB_EPI_GELU_TANH with w_up
+ *      [F, H], or VFB_EPI_SWIGLU with the packed w_up [2F, H]; bias_up)
+ *   -> per-token e4m3 requantisation of the bf16 intermediate [M, F] over
+ *      its full row (the quantiser's arithmetic, h3_fp8_activation.py:16-19)
+ *   -> down GEMM (w_down [H, F]; bias_down; RESIDUAL with residual [M, H]
+ *      (row stride ldr) and optional gate [tokens, H] (row stride
+ *      gate_token_stride), else STORE) into out [M, H] (row stride ldo).
+ * The same bits as vfb_fp8_gemm / vfb_fp8_quant_rows called step by step.
+ * When F % 256 == 0 (GELU) or F % 128 == 0 (SwiGLU) the three steps after
+ * the input quantiser are one persistent kernel whose bf16 intermediate is
+ * requantised in place in L2 and never round-trips HBM; other widths run
+ * the three launches.  x: bf16 [M, H], row stride ldx; s_up [n_up], s_down
+ * [H] fp32.  H and F multiples of 32, at most 32768.  The intermediates live
+ * in `workspace` (256-byte aligned, at least vfb_fp8_ffn_workspace_bytes(M,
+ * H, F) bytes, F = intermediate width); the call allocates nothing.
+ * vfb_fp8_ffn_workspace_bytes returns -1 for an invalid shape. */
 VFB_API int64_t vfb_fp8_ffn_workspace_bytes(int64_t M, int64_t H, int64_t F);
 VFB_API int vfb_fp8_ffn(const void *x, int64_t M, int64_t H, int64_t ldx,
+                const void *w_up, const float *s_up, int64_t n_up,
+                const void *w_down, const float *s_down, int32_t activation,
+                const void *bias_up, const void *bias_down,
+                const void *residual, int64_t ldr,
+                const void *gate, int64_t gate_token_stride, int64_t tokens,
+                void *out, int64_t ldo, void *workspace, int64_t workspace_bytes, void *stream);
+
+/* vfb_fp8_ffn on an input that is already quantised per token: x_codes e4m3
+ * [M, H] (row stride H, 16-byte aligned), x_scales fp32 [>= M], e.g. the
+ * output of vfb_fp8_norm_modulate_quant (the block's RMSNorm + AdaLN
+ * modulate fused into the quantiser).  Everything else as vfb_fp8_ffn. */
+VFB_API int vfb_fp8_ffn_quantized(const void *x_codes, const float *x_scales, int64_t M, int64_t H,
                 const void *w_up, const float *s_up, int64_t n_up,
                 const void *w_down, const float *s_down, int32_t activation,
                 const void *bias_up, const void *bias_down,
@@ -285,6 +303,25 @@ VFB_API int vfb_nvfp4_quant_rows(const void *x, int32_t dtype, int64_t M, int64_
 VFB_API int vfb_nvfp4_gemm(const void *A, const void *sfa, const void *W, const void *sfw,
                            const float *alpha, int64_t M, int64_t N, int64_t K, const void *bias,
                            void *out, int64_t planes, void *stream);
+
+/* vfb_nvfp4_gemm with the fused epilogues of vfb_fp8_gemm, for the QAD visual
+ * linears (src/vflash/adapters/h3_qad.py:206-218) whose outputs go through
+ * the same strict-BF16 steps as the FP8 block's:
+ *   y = bf16(alpha * sum_k A(m,k) W(n,k)), alpha = alpha[0] / alpha_div[0]
+ *       (one IEEE fp32 division on the device, as NVFP4Execution.linear's
+ *       weight.alpha / weight.input_scale, h3_nvfp4_linear.py:124-125;
+ *       alpha_div NULL: alpha[0] as is)
+ *   y = bf16(y + bias[n])  if ep->bias != NULL   (h3_nvfp4_linear.py:139)
+ * then ep->kind as for vfb_fp8_gemm: VFB_EPI_STORE (planes via plane_width /
+ * plane_stride / ldo, optional LoRA branches merged per plane:
+ * triton_strict_bf16_qkv_direct_merge), VFB_EPI_GELU_TANH, VFB_EPI_SWIGLU
+ * (packed W [2F, K/2] with F % 128 == 0: value rows first, their scales the
+ * first F/128 blocks of the 128x4 layout; out [M, F]) or VFB_EPI_RESIDUAL
+ * (gate optional).  No wire layout and no QK-norm epilogue.  Operands as
+ * vfb_nvfp4_gemm; K % 64 == 0, N % 128 == 0. */
+VFB_API int vfb_nvfp4_gemm_ex(const void *A, const void *sfa, const void *W, const void *sfw,
+                              const float *alpha, const float *alpha_div, int64_t M, int64_t N, int64_t K,
+                              const vfb_epilogue *ep, void *stream);
 
 /* ---- strict-BF16 elementwise steps -----------------------------------------
  * Standalone versions of the epilogues above, for callers whose GEMM is not

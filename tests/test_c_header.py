@@ -26,7 +26,7 @@ PROGRAM = r"""
 int main(void) {
   const char *version = vfb_version();
   if (version == NULL || strlen(version) == 0) return 10;
-  if (vfb_fp8_ffn_workspace_bytes(10, 64, 64) != 3840) return 11;
+  if (vfb_fp8_ffn_workspace_bytes(10, 64, 64) != 4096) return 11;
   if (vfb_fp8_ffn_workspace_bytes(10, 48, 64) != -1) return 12;
   vfb_epilogue ep;
   memset(&ep, 0, sizeof ep);

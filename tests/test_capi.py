@@ -152,16 +152,18 @@ def test_bf16_gemm_rejects_bad_arguments_before_any_launch():
 
 def test_ffn_workspace_and_argument_checks_before_any_launch():
     lib = _lib.load()
-    # x codes, x scales, mid, mid codes, mid scales; 256-byte aligned regions
-    assert lib.vfb_fp8_ffn_workspace_bytes(10, 64, 64) == 1024 + 256 + 1280 + 1024 + 256
+    # x codes, x scales, mid, mid codes, mid scales, then the fused kernel's row
+    # maxima and counters (1 + 2 per 256-row block); 256-byte aligned regions
+    assert lib.vfb_fp8_ffn_workspace_bytes(10, 64, 64) == 1024 + 256 + 1280 + 1024 + 256 + 256
     assert lib.vfb_fp8_ffn_workspace_bytes(32760, 4096, 16384) == (
-        32768 * 4096 + 32768 * 4 + 32760 * 16384 * 2 + 32768 * 16384 + 32768 * 4)
+        32768 * 4096 + 32768 * 4 + 32760 * 16384 * 2 + 32768 * 16384 + 32768 * 4
+        + (32760 * 4 + (1 + 2 * 128) * 4 + 255) // 256 * 256)
     for bad in ((10, 48, 64), (10, 64, 40), (-1, 64, 64), (10, 65536, 64)):
         assert lib.vfb_fp8_ffn_workspace_bytes(*bad) == -1
     buf = ctypes.create_string_buffer(8192)
     ptr = (ctypes.addressof(buf) + 255) // 256 * 256
     args = [ptr, 10, 64, 64, ptr, ptr, 64, ptr, ptr, _lib.EPI_GELU_TANH, None, None, None, 0, None, 0, 0,
-            ptr, 64, ptr, 3840, None]
+            ptr, 64, ptr, 4096, None]
     bad_activation = list(args)
     bad_activation[9] = _lib.EPI_RESIDUAL
     assert lib.vfb_fp8_ffn(*bad_activation) == _lib.VFB_EINVAL and "activation" in _lib.last_error()
@@ -169,7 +171,7 @@ def test_ffn_workspace_and_argument_checks_before_any_launch():
     odd_swiglu[9], odd_swiglu[6] = _lib.EPI_SWIGLU, 66
     assert lib.vfb_fp8_ffn(*odd_swiglu) == _lib.VFB_EINVAL
     short = list(args)
-    short[20] = 3839
+    short[20] = 4095
     assert lib.vfb_fp8_ffn(*short) == _lib.VFB_EINVAL and "workspace" in _lib.last_error()
     misaligned = list(args)
     misaligned[19] = ptr + 16

@@ -1,9 +1,14 @@
-"""The fused FP8 FFN through its single C entry point (vfb_fp8_ffn) equals RowFP8Execution.ffn bit for bit.
+"""The fused FP8 FFN (vfb_fp8_ffn, RowFP8Execution.ffn) equals the step-by-step composition bit for bit.
 
-Both run the same four kernels (quantiser, up GEMM + activation, requantiser,
-down GEMM + bias / gated residual); the C entry sequences them on the
-caller's stream with its intermediates in a caller-owned workspace.  The
-Python path is itself checked against the oracle in test_gpu_fp8_gemm.py.
+The composition is the chain the reference runs for the block's FFN, each
+step through this library's own separately tested entry points: the
+per-token quantiser, the up GEMM with the activation epilogue (GELU-tanh or
+SwiGLU), the quantiser again on the bf16 intermediate, and the down GEMM
+with bias / gated residual.  The fused kernel (one launch; the intermediate
+is requantised in L2) must give the same bits: the same MMA tiles in the same
+K order, the same epilogue arithmetic and the same quotient per code.  Shapes
+cover several row-block groups of its schedule, ragged rows, partial down
+tiles, and widths the fused kernel does not tile (the three-launch path).
 """
 
 from __future__ import annotations
@@ -13,8 +18,9 @@ import torch
 
 from tests.helpers import fp8_weight, outlier_activations
 from vflash_b200 import _lib
-from vflash_b200.kernels import KernelInputError, fp8_ffn
-from vflash_b200.native.h3_fp8_linear import RowFP8Execution
+from vflash_b200.kernels import (Epilogue, KernelInputError, fp8_ffn, fp8_gemm, quantize_fp8_norm_modulate,
+                                 quantize_fp8_rows)
+from vflash_b200.native.h3_fp8_linear import NormModulate, RowFP8Execution
 
 pytestmark = pytest.mark.gpu
 DEV = "cuda"
@@ -24,26 +30,81 @@ def bf16(shape, seed, std=1.0):
     return (torch.randn(*shape, generator=torch.Generator().manual_seed(seed)) * std).to(torch.bfloat16).to(DEV)
 
 
-@pytest.mark.parametrize("rows,hidden,width", [(150, 256, 512), (17, 512, 1024), (1000, 1024, 4096)])
-@pytest.mark.parametrize("activation", ["gelu_tanh", "swiglu"])
-@pytest.mark.parametrize("with_residual", [False, True])
-def test_c_entry_equals_python_composition(rows, hidden, width, activation, with_residual):
+def composition(codes, scales, rows, up, up_s, down, down_s, kind, up_bias, down_bias, residual, gate):
+    mid = fp8_gemm(codes, scales, rows, up, up_s, Epilogue(kind=kind, bias=up_bias))
+    mid_codes, mid_scales = quantize_fp8_rows(mid)
+    if residual is None:
+        ep = Epilogue(bias=down_bias)
+    else:
+        ep = Epilogue(kind=_lib.EPI_RESIDUAL, bias=down_bias, residual=residual, gate=gate,
+                      tokens=0 if gate is None else gate.shape[0])
+    return fp8_gemm(mid_codes, mid_scales, rows, down, down_s, ep)
+
+
+def case(rows, hidden, width, activation, with_residual, seed=7):
     x = outlier_activations(rows, hidden, rows + hidden).to(DEV)
     n_up = 2 * width if activation == "swiglu" else width
-    up, up_s = fp8_weight(n_up, hidden, 7)
-    down, down_s = fp8_weight(hidden, width, 8)
-    up, up_s, down, down_s = up.to(DEV), up_s.to(DEV), down.to(DEV), down_s.to(DEV)
-    up_bias, down_bias = bf16((n_up,), 9, 0.01), bf16((hidden,), 10, 0.01)
-    residual = bf16((rows, hidden), 11) if with_residual else None
-    gate = bf16((rows % 7 + 1, hidden), 12, 0.5) if with_residual else None
-    ex = RowFP8Execution("w8a8")
-    want = ex.ffn(x, up, up_s, down, down_s, activation=activation, up_bias=up_bias, down_bias=down_bias,
-                  residual=residual, gate=gate)
+    up, up_s = fp8_weight(n_up, hidden, seed)
+    down, down_s = fp8_weight(hidden, width, seed + 1)
+    return dict(x=x, up=up.to(DEV), up_s=up_s.to(DEV), down=down.to(DEV), down_s=down_s.to(DEV),
+                up_bias=bf16((n_up,), seed + 2, 0.01), down_bias=bf16((hidden,), seed + 3, 0.01),
+                residual=bf16((rows, hidden), seed + 4) if with_residual else None,
+                gate=bf16((rows % 7 + 1, hidden), seed + 5, 0.5) if with_residual else None)
+
+
+SHAPES = [
+    (150, 256, 512),     # one row block
+    (17, 512, 1024),     # fewer rows than a tile
+    (1000, 1024, 4096),  # one group of four row blocks
+    (2100, 512, 768),    # three groups, the last partial; three up tiles per row block
+    (4500, 672, 1024),   # five groups; H = 672: a partial down tile
+    (300, 256, 288),     # widths the fused kernel does not tile: the three-launch path
+]
+
+
+@pytest.mark.parametrize("rows,hidden,width", SHAPES)
+@pytest.mark.parametrize("activation", ["gelu_tanh", "swiglu"])
+@pytest.mark.parametrize("with_residual", [False, True])
+def test_fused_ffn_equals_step_by_step_composition(rows, hidden, width, activation, with_residual):
+    c = case(rows, hidden, width, activation, with_residual)
     kind = _lib.EPI_SWIGLU if activation == "swiglu" else _lib.EPI_GELU_TANH
-    got = fp8_ffn(x, up, up_s, down, down_s, activation=kind, up_bias=up_bias, down_bias=down_bias,
-                  residual=residual, gate=gate)
+    codes, scales = quantize_fp8_rows(c["x"])
+    want = composition(codes, scales, rows, c["up"], c["up_s"], c["down"], c["down_s"], kind, c["up_bias"],
+                       c["down_bias"], c["residual"], c["gate"])
+    got = fp8_ffn(c["x"], c["up"], c["up_s"], c["down"], c["down_s"], activation=kind, up_bias=c["up_bias"],
+                  down_bias=c["down_bias"], residual=c["residual"], gate=c["gate"])
     assert torch.equal(got, want)
+    ex = RowFP8Execution("w8a8")
+    via_api = ex.ffn(c["x"], c["up"], c["up_s"], c["down"], c["down_s"], activation=activation,
+                     up_bias=c["up_bias"], down_bias=c["down_bias"], residual=c["residual"], gate=c["gate"])
+    assert torch.equal(via_api, want)
+    assert ex.calls["w8a8"] == 2
     assert _lib.device_status(clear=True) == _lib.VFB_OK
+
+
+@pytest.mark.parametrize("activation", ["gelu_tanh", "swiglu"])
+def test_fused_ffn_after_the_norm_modulate_prologue(activation):
+    rows, hidden, width, tokens = 1100, 512, 1024, 275
+    c = case(rows, hidden, width, activation, with_residual=True, seed=30)
+    norm_w = bf16((hidden,), 40, 0.1) + 1
+    scale, shift = bf16((tokens, hidden), 41, 0.3), bf16((tokens, hidden), 42, 0.3)
+    kind = _lib.EPI_SWIGLU if activation == "swiglu" else _lib.EPI_GELU_TANH
+    codes, scales = quantize_fp8_norm_modulate(c["x"], norm_w, 1e-6, scale, shift)
+    want = composition(codes, scales, rows, c["up"], c["up_s"], c["down"], c["down_s"], kind, c["up_bias"],
+                       c["down_bias"], c["residual"], c["gate"])
+    got = RowFP8Execution("w8a8").ffn(
+        c["x"], c["up"], c["up_s"], c["down"], c["down_s"], activation=activation, up_bias=c["up_bias"],
+        down_bias=c["down_bias"], residual=c["residual"], gate=c["gate"],
+        prologue=NormModulate(norm_w, scale, shift, 1e-6))
+    assert torch.equal(got, want)
+
+
+def test_fused_ffn_repeats_bit_for_bit():
+    """The work order is dynamic (pairs take items from a counter); the results are not."""
+    c = case(3000, 512, 2048, "gelu_tanh", with_residual=True, seed=50)
+    runs = [fp8_ffn(c["x"], c["up"], c["up_s"], c["down"], c["down_s"], residual=c["residual"])
+            for _ in range(3)]
+    assert torch.equal(runs[0], runs[1]) and torch.equal(runs[0], runs[2])
 
 
 def test_c_entry_rejects_a_short_workspace():

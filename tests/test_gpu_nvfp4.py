@@ -2,13 +2,17 @@
 
 Bars:
 * quantiser codes and 128x4 scales bit-exact against FlashInfer's own
-  nvfp4_quantize (the reference's NVFP4 backend), when its prebuilt module is
-  present (tests/golden/build_flashinfer_reference.py); against the CPU oracle
-  (exact reciprocals instead of rcp.approx) at least 99.9 % identical, every
-  difference one code step;
+  nvfp4_quantize (the reference's NVFP4 backend), frozen on a B200 by
+  tests/golden/make_nvfp4_golden.py into tests/golden/nvfp4_flashinfer.npz
+  (bf16 and fp16; config 3 rows, the H3 width, ragged rows, outliers and
+  edge blocks); against the CPU oracle (exact reciprocals instead of
+  rcp.approx) at least 99.5 % identical, every difference one code step;
+* GEMM on FlashInfer's own codes vs FlashInfer mm_fp4 from the same file:
+  rel-L2 <= 1e-2, and NVFP4Execution.linear vs the reference's composition
+  (nvfp4_quantize, mm_fp4 with alpha / input_scale, + bias) rel-L2 <= 1e-2;
 * GEMM vs the exact fp64 emulation of mm_fp4 on the same codes: identical
   bf16 except rare one-ulp flips; vs the fp32 dequantise-then-matmul
-  rel-L2 <= 2e-2; vs FlashInfer mm_fp4 (when built) rel-L2 <= 1e-2.
+  rel-L2 <= 2e-2.
 """
 
 from __future__ import annotations
@@ -19,23 +23,22 @@ import numpy as np
 import pytest
 import torch
 
+from oracle import epilogues as ep
 from oracle import fp8, nvfp4
+from tests.golden.make_nvfp4_golden import DTYPES, LINEAR_CASE, QUANT_CASES, case_input, linear_inputs
 from tests.helpers import bf16_close, bits_of, outlier_activations
-from vflash_b200.kernels import nvfp4_gemm, nvfp4_quantize
+from vflash_b200 import _lib
+from vflash_b200.kernels import Epilogue, nvfp4_gemm, nvfp4_quantize
 from vflash_b200.native.h3_nvfp4_linear import NVFP4Execution, NVFP4Weight
 
 pytestmark = pytest.mark.gpu
 DEV = "cuda"
-FI_CACHE = Path(__file__).resolve().parent / ".flashinfer_ref"
+GOLDEN = Path(__file__).resolve().parent / "golden" / "nvfp4_flashinfer.npz"
 
 
-def flashinfer_module(kind: str):
-    built = list(FI_CACHE.glob(f"**/cached_ops/{kind}*/*.so"))
-    if not built:
-        pytest.skip(f"FlashInfer {kind} module not prebuilt (tests/golden/build_flashinfer_reference.py)")
-    import flashinfer
-
-    return flashinfer
+@pytest.fixture(scope="module")
+def flashinfer_golden():
+    return dict(np.load(GOLDEN))
 
 
 def global_scale(x: torch.Tensor) -> torch.Tensor:
@@ -76,20 +79,18 @@ def test_quantizer_agrees_with_oracle(rows, cols):
     assert (sf.cpu().numpy().reshape(-1) != want_sf).mean() < 5e-3
 
 
-@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
-def test_quantizer_bit_exact_against_flashinfer(dtype):
-    fi = flashinfer_module("fp4_quantization")
-    x = outlier_activations(333, 4096, 11).to(DEV).to(dtype)
-    # edge blocks: all-zero, tiny (subnormal in bf16) and exact ties
-    x[0, :16] = 0
-    x[1, :16] = torch.tensor(2.0**-130, dtype=torch.float32).to(dtype)
-    x[2, :32] = torch.tensor([6, 0.25, 0.75, 1.25, 1.75, 2.5, 3.5, 5.0] * 4, dtype=dtype)
-    gsf = global_scale(x)
+@pytest.mark.parametrize("case,tag", [(c[0], t) for c in QUANT_CASES for t in c[-1]])
+def test_quantizer_bit_exact_against_flashinfer(flashinfer_golden, case, tag):
+    name, rows, cols, seed, std, outliers, edges, _tags = next(c for c in QUANT_CASES if c[0] == case)
+    x = case_input(rows, cols, seed, std, outliers, edges).to(DEV).to(DTYPES[tag])
+    gsf = torch.from_numpy(flashinfer_golden[f"{name}.{tag}.gsf"]).to(DEV).reshape(())
+    assert torch.equal(gsf, global_scale(x))  # the same global scale FlashInfer was given
     codes, sf = nvfp4_quantize(x, gsf)
-    ref_codes, ref_sf = fi.nvfp4_quantize(x, gsf, sfLayout=fi.SfLayout.layout_128x4, do_shuffle=False)
-    ref_codes = ref_codes.contiguous().view(torch.uint8)
-    assert torch.equal(codes, ref_codes.view(codes.shape))
-    assert torch.equal(sf.reshape(-1), ref_sf.contiguous().view(torch.uint8).reshape(-1))
+    want_codes = flashinfer_golden[f"{name}.{tag}.codes"]
+    want_sf = flashinfer_golden[f"{name}.{tag}.sf"]
+    assert codes.shape == want_codes.shape
+    np.testing.assert_array_equal(codes.cpu().numpy(), want_codes)
+    np.testing.assert_array_equal(sf.reshape(-1).cpu().numpy(), want_sf)
 
 
 SHAPES = [(1, 128, 64), (100, 256, 256), (257, 384, 320), (300, 512, 4096), (64, 1024, 1024)]
@@ -156,19 +157,139 @@ def test_c3_shapes_vs_fp32_dequant(n):
     assert rel <= 2e-2, rel
 
 
-def test_gemm_vs_flashinfer_mm_fp4():
-    fi = flashinfer_module("fp4_gemm")
-    m, n, k = 1000, 1024, 2048
-    x = outlier_activations(m, k, 21).to(DEV)
+def test_gemm_on_flashinfer_codes_vs_mm_fp4(flashinfer_golden):
+    g = flashinfer_golden
+    n, k = LINEAR_CASE["n"], LINEAR_CASE["k"]
+    a_codes = torch.from_numpy(g["linear.a_codes"]).to(DEV)
+    a_sf = torch.from_numpy(g["linear.a_sf"]).to(DEV)
+    w_codes = torch.from_numpy(g["linear.w_codes"]).to(DEV)
+    w_sf = torch.from_numpy(g["linear.w_sf"]).to(DEV).view(n, k // 16)
+    alpha = torch.from_numpy(g["linear.alpha"]).to(DEV).reshape(())
+    y = nvfp4_gemm(a_codes, a_sf, w_codes, w_sf, alpha).float()
+    ref = torch.from_numpy(g["linear.mm_fp4"].view(np.int16)).view(torch.bfloat16).to(DEV).float()
+    rel = ((y - ref).norm() / ref.norm()).item()
+    assert rel <= 1e-2, rel
+
+
+def test_execution_linear_vs_reference_composition(flashinfer_golden):
+    """NVFP4Execution.linear against nvfp4_quantize -> mm_fp4(alpha / input_scale) -> + bias (FlashInfer)."""
+    g = flashinfer_golden
+    n, k = LINEAR_CASE["n"], LINEAR_CASE["k"]
+    x, _w, bias = (t.to(DEV) for t in linear_inputs())
+    weight = NVFP4Weight(torch.from_numpy(g["linear.w_codes"]).to(DEV),
+                         torch.from_numpy(g["linear.w_sf"]).to(DEV).view(n, k // 16),
+                         torch.from_numpy(g["linear.alpha_w"]).to(DEV).reshape(()),
+                         torch.from_numpy(g["linear.input_scale"]).to(DEV).reshape(()))
+    y = NVFP4Execution().linear(x, weight, bias).float()
+    ref = torch.from_numpy(g["linear.out"].view(np.int16)).view(torch.bfloat16).to(DEV).float()
+    rel = ((y - ref).norm() / ref.norm()).item()
+    assert rel <= 1e-2, rel
+    # the activation codes it ran on are FlashInfer's own
+    codes, sf = nvfp4_quantize(x, weight.input_scale)
+    np.testing.assert_array_equal(codes.cpu().numpy(), g["linear.a_codes"])
+    np.testing.assert_array_equal(sf.reshape(-1).cpu().numpy(), g["linear.a_sf"].reshape(-1))
+
+
+def nvfp4_case(m, n, k, seed):
+    x = outlier_activations(m, k, seed).to(DEV)
     gsf = global_scale(x)
     a_codes, a_sf = nvfp4_quantize(x, gsf)
-    _w, w_packed, w_scales, w_alpha = weight_case(n, k, 22)
+    _w, w_packed, w_scales, w_alpha = weight_case(n, k, seed + 1)
+    bias = (torch.randn(n, generator=torch.Generator().manual_seed(seed + 2)) * 0.01).to(torch.bfloat16).to(DEV)
+    return a_codes, a_sf, w_packed, w_scales, w_alpha, gsf, bias
+
+
+def test_alpha_divided_on_the_device_equals_the_divided_scalar():
+    a_codes, a_sf, wp, ws, w_alpha, gsf, bias = nvfp4_case(300, 384, 512, 61)
+    want = nvfp4_gemm(a_codes, a_sf, wp, ws, (w_alpha / gsf).to(torch.float32), bias)
+    got = nvfp4_gemm(a_codes, a_sf, wp, ws, w_alpha.reshape(()), alpha_div=gsf, epilogue=Epilogue(bias=bias))
+    assert torch.equal(got, want)
+
+
+def test_qkv_planes_and_direct_merge_bit_exact_nvfp4():
+    m, h, k = 200, 256, 512
+    a_codes, a_sf, wp, ws, w_alpha, gsf, bias = nvfp4_case(m, 3 * h, k, 71)
     alpha = (w_alpha / gsf).to(torch.float32)
-    y = nvfp4_gemm(a_codes, a_sf, w_packed, w_scales, alpha)
-    ref = fi.mm_fp4(a_codes, w_packed.T, a_sf, w_scales.T, alpha, torch.bfloat16, None,
-                    block_size=16, use_8x4_sf_layout=False, backend="cutlass", use_nvfp4=True)
-    rel = ((y.float() - ref.float()).norm() / ref.float().norm()).item()
-    assert rel <= 1e-2, rel
+    base = nvfp4_gemm(a_codes, a_sf, wp, ws, alpha, bias)
+    gen = torch.Generator().manual_seed(5)
+    adapters = tuple(torch.randn(m, h, generator=gen).to(torch.bfloat16).to(DEV) for _ in range(3))
+    scalings = (0.0625, 0.5, -1.25)
+    merged = nvfp4_gemm(a_codes, a_sf, wp, ws, alpha,
+                        epilogue=Epilogue(bias=bias, planes=3, adapters=adapters, scalings=scalings))
+    want = ep.qkv_direct_merge(bits_of(base), np.stack([bits_of(a) for a in adapters]), scalings)
+    for i in range(3):
+        np.testing.assert_array_equal(bits_of(merged[i]), want[:, i * h:(i + 1) * h])
+
+
+def test_gelu_epilogue_vs_oracle_nvfp4():
+    a_codes, a_sf, wp, ws, w_alpha, gsf, bias = nvfp4_case(257, 512, 384 + 128, 81)
+    alpha = (w_alpha / gsf).to(torch.float32)
+    base = nvfp4_gemm(a_codes, a_sf, wp, ws, alpha, bias)
+    fused = nvfp4_gemm(a_codes, a_sf, wp, ws, alpha, epilogue=Epilogue(kind=_lib.EPI_GELU_TANH, bias=bias))
+    want = fp8.bf16_value(ep.gelu_tanh(bits_of(base)))
+    got = fp8.bf16_value(bits_of(fused))
+    np.testing.assert_allclose(got, want, rtol=2.0**-7, atol=1e-6)
+    assert (got != want).mean() < 1e-2
+
+
+@pytest.mark.parametrize("f", [128, 384])
+def test_swiglu_epilogue_vs_oracle_nvfp4(f):
+    m, k = 301, 256
+    a_codes, a_sf, wp, ws, w_alpha, gsf, bias = nvfp4_case(m, 2 * f, k, 91 + f)
+    alpha = (w_alpha / gsf).to(torch.float32)
+    packed = nvfp4_gemm(a_codes, a_sf, wp, ws, alpha, bias)
+    fused = nvfp4_gemm(a_codes, a_sf, wp, ws, alpha, epilogue=Epilogue(kind=_lib.EPI_SWIGLU, bias=bias))
+    assert fused.shape == (m, f)
+    want = fp8.bf16_value(ep.silu_mul(bits_of(packed)))
+    got = fp8.bf16_value(bits_of(fused))
+    np.testing.assert_allclose(got, want, rtol=2.0**-7, atol=1e-6)
+    assert (got != want).mean() < 1e-2
+
+
+@pytest.mark.parametrize("with_gate", [True, False])
+def test_residual_epilogue_bit_exact_nvfp4(with_gate):
+    batch, tokens, n, k = 2, 75, 256, 256
+    m = batch * tokens
+    a_codes, a_sf, wp, ws, w_alpha, gsf, bias = nvfp4_case(m, n, k, 101)
+    alpha = (w_alpha / gsf).to(torch.float32)
+    base = nvfp4_gemm(a_codes, a_sf, wp, ws, alpha, bias)
+    gen = torch.Generator().manual_seed(23)
+    residual = torch.randn(m, n, generator=gen).to(torch.bfloat16).to(DEV)
+    gate = torch.randn(tokens, n, generator=gen).to(torch.bfloat16).to(DEV) if with_gate else None
+    fused = nvfp4_gemm(a_codes, a_sf, wp, ws, alpha,
+                       epilogue=Epilogue(kind=_lib.EPI_RESIDUAL, bias=bias, residual=residual, gate=gate,
+                                         tokens=tokens))
+    if with_gate:
+        want = ep.gate_residual(bits_of(residual).reshape(batch, tokens, n), bits_of(gate),
+                                bits_of(base).reshape(batch, tokens, n)).reshape(m, n)
+    else:
+        want = fp8.bf16_bits(fp8.bf16_value(bits_of(residual)) + fp8.bf16_value(bits_of(base)))
+    np.testing.assert_array_equal(bits_of(fused), want)
+
+
+def test_execution_fused_entry_points_equal_linear_then_step():
+    n, k = 384, 512
+    _w, packed, scales, w_alpha = weight_case(n, k, 111)
+    x = outlier_activations(2 * 75, k, 112).to(DEV).view(2, 75, k)
+    weight = NVFP4Weight(packed, scales, w_alpha.reshape(()), global_scale(x))
+    bias = (torch.randn(n, generator=torch.Generator().manual_seed(113)) * 0.01).to(torch.bfloat16).to(DEV)
+    engine = NVFP4Execution()
+    y = engine.linear(x, weight, bias)
+    # GELU
+    g = engine.gelu_linear(x, weight, bias)
+    want = fp8.bf16_value(ep.gelu_tanh(bits_of(y.reshape(-1, n))))
+    np.testing.assert_allclose(fp8.bf16_value(bits_of(g.reshape(-1, n))), want, rtol=2.0**-7, atol=1e-6)
+    # gated residual
+    residual = outlier_activations(150, n, 114).to(DEV).view(2, 75, n)
+    gate = outlier_activations(75, n, 115).to(DEV)
+    r = engine.gate_residual_linear(x, weight, residual, gate, bias)
+    want = ep.gate_residual(bits_of(residual), bits_of(gate), bits_of(y))
+    np.testing.assert_array_equal(bits_of(r), want)
+    # merged QKV planes = chunk(3) of the plain output
+    q, kk, v = engine.qkv_linear(x, weight, bias)
+    for plane, ref in zip((q, kk, v), y.chunk(3, dim=-1)):
+        assert torch.equal(plane, ref)
+    assert engine.calls == 4 and engine.rows == 4 * 150
 
 
 def test_execution_linear_end_to_end():

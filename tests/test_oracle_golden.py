@@ -189,3 +189,71 @@ def test_oracle_f64_to_bf16_rounds_once():
     np.testing.assert_array_equal(f64_to_bf16_bits(mid + step * 1e-9), (b + 1).astype(np.uint16))
     np.testing.assert_array_equal(f64_to_bf16_bits(mid - step * 1e-9), b)
     np.testing.assert_array_equal(f64_to_bf16_bits(-mid - step * 1e-9), (b + 1).astype(np.uint16) | 0x8000)
+
+
+# --- NVFP4: the CPU restatement against FlashInfer's own outputs -------------
+# tests/golden/nvfp4_flashinfer.npz holds FlashInfer's nvfp4_quantize and
+# mm_fp4 results for seeded inputs, recorded on a B200 by
+# tests/golden/make_nvfp4_golden.py (the reference's NVFP4 backend,
+# h3_nvfp4_linear.py:102, 118-130).  The restatement uses exact reciprocals
+# where FlashInfer uses rcp.approx, so it is held to >= 99.5 % of codes and
+# scales identical, every differing code one e2m1 step away.
+
+def _nvfp4_golden():
+    import numpy as np
+
+    from tests.conftest import GOLDEN
+
+    return dict(np.load(GOLDEN / "nvfp4_flashinfer.npz"))
+
+
+@pytest.mark.parametrize("case_name", ["c3_act", "c3_weight", "outliers_edges", "h3_width"])
+def test_nvfp4_oracle_agrees_with_flashinfer_codes(case_name):
+    import numpy as np
+
+    from oracle import nvfp4
+    from tests.golden.make_nvfp4_golden import DTYPES, QUANT_CASES, case_input, global_scale
+
+    golden = _nvfp4_golden()
+    name, rows, cols, seed, std, outliers, edges, tags = next(c for c in QUANT_CASES if c[0] == case_name)
+    x = case_input(rows, cols, seed, std, outliers, edges)
+    for tag in tags:
+        values = x.to(DTYPES[tag]).float().numpy()
+        gsf = float(golden[f"{name}.{tag}.gsf"])
+        assert np.float32(gsf) == global_scale(x.to(DTYPES[tag])).numpy()  # the same expression on the host
+        codes, sf = nvfp4.quantize(values, gsf)
+        got = nvfp4.unpack(codes)
+        want = nvfp4.unpack(golden[f"{name}.{tag}.codes"])
+        assert got.shape == want.shape
+        assert (got != want).mean() <= 5e-3
+        step = np.abs(nvfp4.e2m1_decode(got) - nvfp4.e2m1_decode(want))
+        assert step.max() <= 2.0  # one e2m1 step at most (the widest is 4 -> 6)
+        assert (sf != golden[f"{name}.{tag}.sf"]).mean() <= 5e-3
+        # the padding of the 128x4 layout is zero in both
+        offsets = nvfp4.sf_offsets(*nvfp4.sf_padded_shape(rows, cols // 16))
+        pad = np.ones(offsets.shape, bool)
+        pad[:rows, : cols // 16] = False
+        assert (golden[f"{name}.{tag}.sf"][offsets[pad]] == 0).all()
+
+
+def test_nvfp4_oracle_emulates_mm_fp4_on_flashinfer_codes():
+    import numpy as np
+
+    from oracle import fp8, nvfp4
+    from tests.golden.make_nvfp4_golden import LINEAR_CASE
+
+    g = _nvfp4_golden()
+    want = fp8.bf16_value(g["linear.mm_fp4"])
+    got = nvfp4.w4a4_reference(g["linear.a_codes"], g["linear.a_sf"].reshape(-1), g["linear.w_codes"],
+                               g["linear.w_sf"].reshape(-1), float(g["linear.alpha"]))
+    assert got.shape == (LINEAR_CASE["rows"], LINEAR_CASE["n"])
+    assert fp8.rel_l2(got, want) <= 1e-2
+    # the exact emulation rounds once; the library kernel's fp32 accumulation order differs
+    assert (got == want).mean() >= 0.95
+    # the reference adds the bias as a separate bf16 op
+    from tests.golden.make_nvfp4_golden import linear_inputs
+
+    _x, _w, bias = linear_inputs()
+    bias_bits = fp8.bf16_bits(bias.float().numpy())
+    composed = fp8.bf16_round(want + fp8.bf16_value(bias_bits))
+    np.testing.assert_array_equal(composed, fp8.bf16_value(g["linear.out"]))

@@ -93,6 +93,11 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         [_vp, _c_int64, _c_int64, _c_int64, _vp, _vp, _c_int64, _vp, _vp, ctypes.c_int32, _vp, _vp, _vp,
          _c_int64, _vp, _c_int64, _c_int64, _vp, _c_int64, _vp, _c_int64, _vp],
     ),
+    "vfb_fp8_ffn_quantized": (
+        ctypes.c_int,
+        [_vp, _vp, _c_int64, _c_int64, _vp, _vp, _c_int64, _vp, _vp, ctypes.c_int32, _vp, _vp, _vp,
+         _c_int64, _vp, _c_int64, _c_int64, _vp, _c_int64, _vp, _c_int64, _vp],
+    ),
     "vfb_fp8_ffn_noalloc": (
         ctypes.c_int,
         [_vp, _c_int64, _c_int64, _c_int64, _vp, _vp, _c_int64, _vp, _vp, ctypes.c_int32, _vp, _vp, _vp,
@@ -107,6 +112,10 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "vfb_nvfp4_gemm": (
         ctypes.c_int,
         [_vp, _vp, _vp, _vp, _vp, _c_int64, _c_int64, _c_int64, _vp, _vp, _c_int64, _vp]),
+    "vfb_nvfp4_gemm_ex": (
+        ctypes.c_int,
+        [_vp, _vp, _vp, _vp, _vp, _vp, _c_int64, _c_int64, _c_int64, ctypes.POINTER(Epilogue), _vp],
+    ),
     "vfb_silu_mul": (ctypes.c_int, [_vp, _c_int64, _c_int64, _vp, _c_int64, _vp]),
     "vfb_ffn_adapter_silu": (
         ctypes.c_int, [_vp, _vp, _c_int64, _c_int64, ctypes.c_float, _vp, _c_int64, _vp]),

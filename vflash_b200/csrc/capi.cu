@@ -139,6 +139,48 @@ PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
   return fn;
 }
 
+// Tensor map over an 8-bit [rows, cols] matrix (row stride ld bytes) with a
+// 128-byte-swizzled box of box_rows x 128 bytes (one K stage of the GEMMs).
+int make_map_u8(CUtensorMap *map, const void *base, int64_t rows, int64_t cols, int64_t ld,
+                int box_rows) {
+  auto encode = tensor_map_encoder();
+  if (encode == nullptr) return set_error(VFB_ECUDA, "cuTensorMapEncodeTiled is unavailable");
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld)};
+  cuuint32_t box[2] = {128, static_cast<cuuint32_t>(box_rows)};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void *>(base), dims,
+                      strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                      CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                      CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return set_error(VFB_ECUDA, "cuTensorMapEncodeTiled failed (%d) rows=%lld cols=%lld ld=%lld",
+                     static_cast<int>(r), (long long)rows, (long long)cols, (long long)ld);
+  return VFB_OK;
+}
+
+// Tensor map over the bf16 output viewed as [planes][rows][width] (row stride
+// ld elements, plane stride plane_stride elements), 32 x 32 boxes with the
+// 64-byte swizzle the epilogue writes its staging boxes in.
+int make_map_out(CUtensorMap *map, void *base, int64_t width, int64_t rows, int64_t planes,
+                 int64_t ld, int64_t plane_stride) {
+  auto encode = tensor_map_encoder();
+  if (encode == nullptr) return set_error(VFB_ECUDA, "cuTensorMapEncodeTiled is unavailable");
+  cuuint64_t dims[3] = {static_cast<cuuint64_t>(width), static_cast<cuuint64_t>(rows),
+                        static_cast<cuuint64_t>(planes)};
+  cuuint64_t strides[2] = {static_cast<cuuint64_t>(ld) * 2, static_cast<cuuint64_t>(plane_stride) * 2};
+  cuuint32_t box[3] = {32, 32, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, base, dims, strides, box, estr,
+                      CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B,
+                      CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return set_error(VFB_ECUDA, "cuTensorMapEncodeTiled (output) failed (%d)", static_cast<int>(r));
+  return VFB_OK;
+}
+
+bool aligned16(const void *ptr) { return reinterpret_cast<uintptr_t>(ptr) % 16 == 0; }
+
 }  // namespace vfb
 
 extern "C" const char *vfb_last_error(void) { return g_last_error; }

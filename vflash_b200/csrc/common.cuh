@@ -62,6 +62,21 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
   return done != 0;
 }
 
+// try_wait with acquire semantics at cluster scope: for a barrier whose
+// arrivals come from the peer CTA of the pair along with data it wrote into
+// this CTA's shared memory.
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t *bar, uint32_t parity) {
+  uint32_t done;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(done)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return done != 0;
+}
+
 // Record the first error code of this device (kept until the host clears it).
 __device__ __forceinline__ void record_status(int *status, int code) {
   if (status != nullptr) atomicCAS(status, 0, code);
@@ -89,6 +104,53 @@ __device__ __forceinline__ bool mbar_wait_for(uint64_t *bar, uint32_t parity, vo
 __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, volatile int *abort_flag,
                                           int *status) {
   return mbar_wait_for(bar, parity, abort_flag, status, VFB_WAIT_TIMEOUT_NS);
+}
+
+// mbar_wait with cluster-scope acquire (see mbar_try_wait_cluster).
+__device__ __forceinline__ bool mbar_wait_cluster(uint64_t *bar, uint32_t parity, volatile int *abort_flag,
+                                                  int *status) {
+  if (mbar_try_wait_cluster(bar, parity)) return true;
+  const uint64_t start = global_timer_ns();
+  for (uint32_t spin = 1;; ++spin) {
+    if (mbar_try_wait_cluster(bar, parity)) return true;
+    if ((spin & 255u) == 0) {
+      if (*abort_flag) return false;
+      if (global_timer_ns() - start > VFB_WAIT_TIMEOUT_NS) {
+        *abort_flag = 1;
+        record_status(status, VFB_ETIMEOUT);
+        return false;
+      }
+    }
+  }
+}
+
+// ---- global-memory flags between CTAs ----------------------------------------
+__device__ __forceinline__ int ld_acquire_gpu(const int *p) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ void red_release_gpu_add(int *p, int v) {
+  asm volatile("red.release.gpu.global.add.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// Orders this thread's generic-proxy accesses of global memory with async-proxy
+// (TMA) accesses: data written by plain stores and then read by a TMA load
+// elsewhere, or written by a TMA store and then read by plain loads.
+__device__ __forceinline__ void fence_proxy_async_global() {
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+
+// Drops one 128-byte L2 line without writing it back (its contents become
+// undefined): for scratch data that is dead once read.
+__device__ __forceinline__ void discard_l2_line(const void *p) {
+  asm volatile("discard.global.L2 [%0], 128;" ::"l"(p) : "memory");
+}
+
+// 32-bit store into the shared memory of a CTA of this cluster (shared::cluster address).
+__device__ __forceinline__ void st_shared_cluster_u32(uint32_t cluster_addr, uint32_t v) {
+  asm volatile("st.shared::cluster.u32 [%0], %1;" ::"r"(cluster_addr), "r"(v) : "memory");
 }
 
 // ---- TMA ------------------------------------------------------------------
@@ -529,4 +591,12 @@ uint64_t current_context_id();
 int *device_status_ptr();
 int ensure_smem_optin(const void *kernel, int bytes, std::atomic<uint64_t> *done);
 PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder();
+// Tensor map over an 8-bit [rows, cols] matrix (row stride ld bytes), boxes of
+// box_rows x 128 bytes with the 128-byte swizzle.
+int make_map_u8(CUtensorMap *map, const void *base, int64_t rows, int64_t cols, int64_t ld, int box_rows);
+// Tensor map over a bf16 output [planes][rows][width] (strides in elements),
+// 32 x 32 boxes with the 64-byte swizzle of the epilogue's staging boxes.
+int make_map_out(CUtensorMap *map, void *base, int64_t width, int64_t rows, int64_t planes, int64_t ld,
+                 int64_t plane_stride);
+bool aligned16(const void *ptr);
 }  // namespace vfb

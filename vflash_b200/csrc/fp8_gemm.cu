@@ -27,8 +27,11 @@
 //               staged in 64-byte-swizzled shared memory and written by TMA
 //               stores (evict_first).  The second accumulator lets the epilogue
 //               of tile i overlap the main loop of tile i+1.
-// Tiles are visited with the N index fastest so that the pairs running at the
-// same time share one A row-block and stream the weight through L2.
+// Tiles are visited in bands of band_n weight tiles (the weight slab of a band,
+// band_n x 256 rows x K bytes, is sized on the host to stay in L2), M-block by
+// M-block inside a band with the N index fastest: the pairs running at the
+// same time share one A row-block, and each band's weights are fetched from
+// DRAM once instead of once per row-block.
 // No TMA multicast is used: every CTA loads its own operands.
 #include <cudaTypedefs.h>
 
@@ -37,6 +40,7 @@
 #include <mutex>
 
 #include "common.cuh"
+#include "epilogue.cuh"
 
 namespace vfb {
 namespace {
@@ -69,7 +73,6 @@ constexpr int TMEM_COLS = 512;
 constexpr int EPI_BOXES = 4;  // with four epilogue warps; two with eight (same shared memory)
 template <int EPI, int OPS = OPS_E4M3>
 __host__ __device__ constexpr int epi_boxes() { return 16 / epi_warps<EPI, OPS>(); }
-constexpr int EPI_BOX_BYTES = 32 * 32 * 2;
 constexpr int EPI_SMEM_BYTES = 4 * EPI_BOXES * EPI_BOX_BYTES;
 static_assert(8 * 2 * EPI_BOX_BYTES == EPI_SMEM_BYTES, "eight-warp epilogue staging must fit");
 constexpr size_t SMEM_BYTES =
@@ -106,81 +109,11 @@ struct GemmParams {
   const float *sw;
   int num_m_tiles;
   int num_n_tiles;
+  int band_n;  // weight tiles per band of the tile order
   int num_kb;
   int *status;
   EpiParams ep;
 };
-
-__device__ __forceinline__ float gelu_tanh(float y) {
-  // 0.5 y (1 + tanh(sqrt(2/pi) (y + 0.044715 y^3)))
-  const float k_beta = 0.7978845608028654f;
-  const float k_kappa = 0.044715f;
-  const float cube = y * y * y;
-  const float inner = k_beta * (y + k_kappa * cube);
-  return 0.5f * y * (1.0f + tanhf(inner));
-}
-
-__device__ __forceinline__ float silu(float g) { return g / (1.0f + expf(-g)); }
-
-__device__ __forceinline__ void load_f32x32(const float *__restrict__ p, float (&r)[32]) {
-  const float4 *q = reinterpret_cast<const float4 *>(p);
-#pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    float4 t = __ldg(q + i);
-    r[4 * i] = t.x;
-    r[4 * i + 1] = t.y;
-    r[4 * i + 2] = t.z;
-    r[4 * i + 3] = t.w;
-  }
-}
-
-__device__ __forceinline__ void load_bf16x32(const __nv_bfloat16 *p, float (&r)[32]) {
-  const uint4 *q = reinterpret_cast<const uint4 *>(p);
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    uint4 t = __ldg(q + i);
-    const __nv_bfloat162 *h = reinterpret_cast<const __nv_bfloat162 *>(&t);
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      float2 f = __bfloat1622float2(h[j]);
-      r[8 * i + 2 * j] = f.x;
-      r[8 * i + 2 * j + 1] = f.y;
-    }
-  }
-}
-
-// Writes one 32 x 32 output box: lane i holds row i of the warp's 32 rows.
-// The rows go to shared memory in the 64-byte swizzle the output tensor map
-// uses (conflict-free 16-byte stores), then lane 0 issues one TMA store.
-// Each warp cycles through EPI_BOXES staging boxes; a box is rewritten only
-// after the store issued from it EPI_BOXES chunks earlier has read it.
-template <int BOXES = EPI_BOXES>
-__device__ __forceinline__ void store_box(uint8_t *warp_smem, int &box, const CUtensorMap *map,
-                                          const float (&y)[32], int lane, int32_t col, int32_t row0,
-                                          int32_t plane, bool any_row) {
-  uint8_t *buf = warp_smem + box * EPI_BOX_BYTES;
-  if (lane == 0) bulk_wait_group_read<BOXES - 1>();
-  __syncwarp();
-  uint4 *row = reinterpret_cast<uint4 *>(buf + lane * 64);
-  const int sw = (lane >> 1) & 3;
-#pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    uint4 t;
-    t.x = pack_bf16x2(y[8 * j + 0], y[8 * j + 1]);
-    t.y = pack_bf16x2(y[8 * j + 2], y[8 * j + 3]);
-    t.z = pack_bf16x2(y[8 * j + 4], y[8 * j + 5]);
-    t.w = pack_bf16x2(y[8 * j + 6], y[8 * j + 7]);
-    row[j ^ sw] = t;
-  }
-  fence_proxy_async_smem();
-  __syncwarp();
-  if (lane == 0 && any_row) {
-    // outputs are not re-read by this kernel: evict them first from L2
-    tma_store_3d_hint(map, buf, col, row0, plane, l2_policy_evict_first());
-    bulk_commit_group();
-  }
-  box = box + 1 == BOXES ? 0 : box + 1;
-}
 
 // Output coordinate (column, plane index of the tensor map) of a 32-column
 // box that starts at column col of plane `plane`.  Without the wire layout the
@@ -203,28 +136,6 @@ __device__ __forceinline__ void out_coord(const EpiParams &ep, int32_t plane, in
   const int32_t dest = g / ep.wire_chunks;
   ocol = col - g * ep.wire_width;
   oplane = (chunk * 2 + dest) * 3 + plane;
-}
-
-// y = bf16(acc * sa * sw) then bf16(y + bias): the _scaled_mm output followed
-// by the separate bias add of the reference.  Unscaled (bf16 operands):
-// y = bf16(acc), the F.linear output, then the bias the same way.
-template <bool SCALED = true>
-__device__ __forceinline__ void scale_bias(float (&v)[32], float sa, const float *sw,
-                                           const __nv_bfloat16 *bias) {
-  if constexpr (SCALED) {
-    float w[32];
-    load_f32x32(sw, w);
-#pragma unroll
-    for (int j = 0; j < 32; ++j) v[j] = v[j] * sa * w[j];
-  }
-  bf16r_x32(v);
-  if (bias != nullptr) {
-    float b[32];
-    load_bf16x32(bias, b);
-#pragma unroll
-    for (int j = 0; j < 32; ++j) v[j] = v[j] + b[j];
-    bf16r_x32(v);
-  }
 }
 
 // STORE value of 32 columns: scale_bias, then the plane's LoRA branch if any.
@@ -359,8 +270,8 @@ __global__ void __launch_bounds__(num_threads<EPI, OPS>(), 1)
       for (int i = 0; i < STAGES; ++i) issued[i] = false;
       bool ok = true;
       for (int tile = pair; tile < num_tiles && ok; tile += num_pairs) {
-        const int m_tile = tile / p.num_n_tiles;
-        const int n_tile = tile % p.num_n_tiles;
+        int m_tile, n_tile;
+        band_coords(tile, p.num_m_tiles, p.num_n_tiles, p.band_n, m_tile, n_tile);
         const int32_t a_row = m_tile * (2 * BM) + static_cast<int32_t>(rank) * BM;
         for (int kb = 0; kb < p.num_kb; ++kb) {
           if (!mbar_wait(&empty_bar[s], ph ^ 1, abort_flag, p.status)) {
@@ -465,8 +376,8 @@ __global__ void __launch_bounds__(num_threads<EPI, OPS>(), 1)
       const uint32_t acc_ph = (t >> 1) & 1;
       if (!mbar_wait(&tfull_bar[acc], acc_ph, abort_flag, p.status)) break;
       tc_fence_after();
-      const int m_tile = tile / p.num_n_tiles;
-      const int n_tile = tile % p.num_n_tiles;
+      int m_tile, n_tile;
+      band_coords(tile, p.num_m_tiles, p.num_n_tiles, p.band_n, m_tile, n_tile);
       const int64_t row0 = static_cast<int64_t>(m_tile) * (2 * BM) + rank * BM + q * 32;
       const int64_t m = row0 + lane;
       const bool live = m < p.M;
@@ -618,47 +529,7 @@ __global__ void __launch_bounds__(num_threads<EPI, OPS>(), 1)
 
 // ---- host side ---------------------------------------------------------------
 
-// Tensor map over an 8-bit [rows, cols] matrix (row stride ld bytes) with a
-// 128-byte-swizzled box of box_rows x 128 bytes.
-int make_map_u8(CUtensorMap *map, const void *base, int64_t rows, int64_t cols, int64_t ld,
-                int box_rows) {
-  auto encode = tensor_map_encoder();
-  if (encode == nullptr) return set_error(VFB_ECUDA, "cuTensorMapEncodeTiled is unavailable");
-  cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
-  cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld)};
-  cuuint32_t box[2] = {static_cast<cuuint32_t>(BK), static_cast<cuuint32_t>(box_rows)};
-  cuuint32_t estr[2] = {1, 1};
-  CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void *>(base), dims,
-                      strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                      CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                      CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  if (r != CUDA_SUCCESS)
-    return set_error(VFB_ECUDA, "cuTensorMapEncodeTiled failed (%d) rows=%lld cols=%lld ld=%lld",
-                     static_cast<int>(r), (long long)rows, (long long)cols, (long long)ld);
-  return VFB_OK;
-}
 
-// Tensor map over the bf16 output viewed as [planes][rows][width] (row stride
-// ld elements, plane stride plane_stride elements), 32 x 32 boxes with the
-// 64-byte swizzle the epilogue writes its staging boxes in.
-int make_map_out(CUtensorMap *map, void *base, int64_t width, int64_t rows, int64_t planes,
-                 int64_t ld, int64_t plane_stride) {
-  auto encode = tensor_map_encoder();
-  if (encode == nullptr) return set_error(VFB_ECUDA, "cuTensorMapEncodeTiled is unavailable");
-  cuuint64_t dims[3] = {static_cast<cuuint64_t>(width), static_cast<cuuint64_t>(rows),
-                        static_cast<cuuint64_t>(planes)};
-  cuuint64_t strides[2] = {static_cast<cuuint64_t>(ld) * 2, static_cast<cuuint64_t>(plane_stride) * 2};
-  cuuint32_t box[3] = {32, 32, 1};
-  cuuint32_t estr[3] = {1, 1, 1};
-  CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, base, dims, strides, box, estr,
-                      CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B,
-                      CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  if (r != CUDA_SUCCESS)
-    return set_error(VFB_ECUDA, "cuTensorMapEncodeTiled (output) failed (%d)", static_cast<int>(r));
-  return VFB_OK;
-}
-
-bool aligned16(const void *ptr) { return reinterpret_cast<uintptr_t>(ptr) % 16 == 0; }
 
 template <int EPI, int OPS = OPS_E4M3>
 int launch(const CUtensorMap &a, const CUtensorMap &b, const CUtensorMap &b2, const CUtensorMap &o,
@@ -827,6 +698,7 @@ int gemm_impl(const char *fn, int ops, const void *A, int64_t lda, const float *
     }
   }
 
+  p.band_n = band_width(p.num_n_tiles, K);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (bf16) return launch<VFB_EPI_STORE, OPS_BF16>(ta, tb, tb2, to, p, sm_count, s);
   switch (kind) {

@@ -8,7 +8,8 @@
 //   out      = bf16(out + bias[n])                       if bias != NULL
 //
 // Structure: persistent CTA pairs (cta_group::2), 256 x 256 output tile per
-// pair, K staged 256 elements (128 bytes of codes) at a time.  Each CTA TMA-
+// pair in the banded order of the FP8 GEMM (epilogue.cuh: band_coords), K
+// staged 256 elements (128 bytes of codes) at a time.  Each CTA TMA-
 // loads its own 128 A rows and 128 of the tile's 256 weight rows (128-byte
 // swizzle, no multicast), its A rows' scale blocks and the scale blocks of all
 // 256 weight rows (512-byte blocks in the 128x4 layout, loaded through 2-D
@@ -26,6 +27,7 @@
 #include <atomic>
 
 #include "common.cuh"
+#include "epilogue.cuh"
 
 namespace vfb {
 namespace {
@@ -47,49 +49,52 @@ constexpr uint32_t ACC1_COL = 192;
 constexpr uint32_t SFA_COL = 448;          // 4 columns per K = 64 block
 constexpr uint32_t SFB_COL = 464;          // 8 columns per K = 64 block
 constexpr int EPI_BOXES = 2;
-constexpr int EPI_BOX_BYTES = 32 * 32 * 2;
 constexpr int EPI_SMEM = 4 * EPI_BOXES * EPI_BOX_BYTES;
 constexpr size_t SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + EPI_SMEM + 256;
 
 struct Params {
-  int64_t M, N, K;
+  int64_t M, N, K;  // N: GEMM output columns (the packed 2F for SWIGLU)
   const float *alpha;
+  const float *alpha_div;  // NULL, or alpha is divided by it (IEEE division, once per thread)
   const __nv_bfloat16 *bias;
   int32_t plane_width;
+  int32_t F;               // SWIGLU: output width
+  const __nv_bfloat16 *adapter[3];  // STORE: LoRA branch per plane (NULL = none)
+  int64_t adapter_ld;
+  float scaling[3];
+  const __nv_bfloat16 *residual;    // RESIDUAL
+  int64_t ldr;
+  const __nv_bfloat16 *gate;
+  int64_t gate_ts;
+  int64_t gate_hs;
+  int64_t tokens;
   int num_m_tiles, num_n_tiles, ktiles;  // ktiles = K / 64
+  int band_n;                            // weight tiles per band of the tile order
   int *status;
 };
 
-__device__ __forceinline__ void store_box(uint8_t *warp_smem, int &box, const CUtensorMap *map,
-                                          const float (&y)[32], int lane, int32_t col, int32_t row0,
-                                          int32_t plane, bool any_row) {
-  uint8_t *buf = warp_smem + box * EPI_BOX_BYTES;
-  if (lane == 0) bulk_wait_group_read<EPI_BOXES - 1>();
-  __syncwarp();
-  uint4 *row = reinterpret_cast<uint4 *>(buf + lane * 64);
-  const int sw = (lane >> 1) & 3;
+// y = bf16(alpha * acc) then bf16(y + bias): mm_fp4's output, then the
+// separate bias add of NVFP4Execution.linear (h3_nvfp4_linear.py:139).
+__device__ __forceinline__ void alpha_bias(float (&v)[32], float alpha, const __nv_bfloat16 *bias) {
 #pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    uint4 t;
-    t.x = pack_bf16x2(y[8 * j + 0], y[8 * j + 1]);
-    t.y = pack_bf16x2(y[8 * j + 2], y[8 * j + 3]);
-    t.z = pack_bf16x2(y[8 * j + 4], y[8 * j + 5]);
-    t.w = pack_bf16x2(y[8 * j + 6], y[8 * j + 7]);
-    row[j ^ sw] = t;
+  for (int j = 0; j < 32; ++j) v[j] = alpha * v[j];
+  bf16r_x32(v);
+  if (bias != nullptr) {
+    float b[32];
+    load_bf16x32(bias, b);
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] = v[j] + b[j];
+    bf16r_x32(v);
   }
-  fence_proxy_async_smem();
-  __syncwarp();
-  if (lane == 0 && any_row) {
-    tma_store_3d_hint(map, buf, col, row0, plane, l2_policy_evict_first());
-    bulk_commit_group();
-  }
-  box = box + 1 == EPI_BOXES ? 0 : box + 1;
 }
 
+template <int EPI>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     nvfp4_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                      const __grid_constant__ CUtensorMap tmSFA, const __grid_constant__ CUtensorMap tmSFB,
-                      const __grid_constant__ CUtensorMap tmOut, const Params p) {
+                      const __grid_constant__ CUtensorMap tmB2, const __grid_constant__ CUtensorMap tmSFA,
+                      const __grid_constant__ CUtensorMap tmSFB, const __grid_constant__ CUtensorMap tmOut,
+                      const Params p) {
+  constexpr bool kSwiglu = EPI == VFB_EPI_SWIGLU;
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                               ~static_cast<uintptr_t>(1023));
@@ -123,6 +128,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
+    if (kSwiglu) tma_prefetch_desc(&tmB2);
     tma_prefetch_desc(&tmSFA);
     tma_prefetch_desc(&tmSFB);
     tma_prefetch_desc(&tmOut);
@@ -150,8 +156,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       bool ok = true;
       const uint64_t keep = l2_policy_evict_last();
       for (int tile = pair; tile < num_tiles && ok; tile += num_pairs) {
-        const int m_tile = tile / p.num_n_tiles;
-        const int n_tile = tile % p.num_n_tiles;
+        int m_tile, n_tile;
+        band_coords(tile, p.num_m_tiles, p.num_n_tiles, p.band_n, m_tile, n_tile);
         const int m_block = 2 * m_tile + static_cast<int>(rank);  // this CTA's 128-row block
         for (int ks = 0; ks < kstages; ++ks) {
           if (!mbar_wait(&empty_bar[s], ph ^ 1, abort_flag, p.status)) {
@@ -163,14 +169,23 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           uint8_t *st = smem + s * STAGE_BYTES;
           const int32_t kt0 = ks * KB_PER_STAGE;
           tma_load_2d_pair(st, &tmA, full_leader, ks * BK_BYTES, m_block * BM);
-          tma_load_2d_pair_hint(st + A_STAGE, &tmB, full_leader, ks * BK_BYTES,
-                                n_tile * BN + static_cast<int32_t>(rank) * BN_HALF, keep);
+          if (kSwiglu) {
+            // leader: value rows [n*128, +128); peer: the matching gate rows (second half of W)
+            tma_load_2d_pair_hint(st + A_STAGE, rank == 0 ? &tmB : &tmB2, full_leader, ks * BK_BYTES,
+                                  n_tile * BN_HALF, keep);
+          } else {
+            tma_load_2d_pair_hint(st + A_STAGE, &tmB, full_leader, ks * BK_BYTES,
+                                  n_tile * BN + static_cast<int32_t>(rank) * BN_HALF, keep);
+          }
           // scale blocks: rows of 256 bytes, two per 512-byte block
           tma_load_2d_pair(st + A_STAGE + B_STAGE, &tmSFA, full_leader, 0,
                            (m_block * p.ktiles + kt0) * 2);
-          for (int h = 0; h < 2; ++h)
+          for (int h = 0; h < 2; ++h) {
+            // the 128-row weight block of each half of the tile's 256 B rows
+            const int w_block = kSwiglu ? (h == 0 ? n_tile : p.F / BN_HALF + n_tile) : 2 * n_tile + h;
             tma_load_2d_pair_hint(st + A_STAGE + B_STAGE + SFA_STAGE + h * (KB_PER_STAGE * 512), &tmSFB,
-                                  full_leader, 0, ((2 * n_tile + h) * p.ktiles + kt0) * 2, keep);
+                                  full_leader, 0, (w_block * p.ktiles + kt0) * 2, keep);
+          }
           issued[s] = true;
           issued_phase[s] = ph;
           if (++s == STAGES) {
@@ -259,57 +274,98 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     const int q = warp & 3;
     uint8_t *warp_smem = sEpi + q * EPI_BOXES * EPI_BOX_BYTES;
     int box = 0;
-    const float alpha = __ldg(p.alpha);
+    float alpha = __ldg(p.alpha);
+    if (p.alpha_div != nullptr) alpha = __fdiv_rn(alpha, __ldg(p.alpha_div));
     const uint32_t tfree_leader = map_to_rank(smem_u32(tfree_bar), 0);
+    // chunks of 32 columns per tile; SWIGLU pairs value chunk c with gate chunk c + 4
+    constexpr int kChunks = kSwiglu ? BN_HALF / 32 : BN / 32;
     int t = 0;
     for (int tile = pair; tile < num_tiles; tile += num_pairs, ++t) {
       if (!mbar_wait(tfull_bar, t & 1, abort_flag, p.status)) break;
       tc_fence_after();
-      const int m_tile = tile / p.num_n_tiles;
-      const int n_tile = tile % p.num_n_tiles;
+      int m_tile, n_tile;
+      band_coords(tile, p.num_m_tiles, p.num_n_tiles, p.band_n, m_tile, n_tile);
       const int64_t row0 = static_cast<int64_t>(m_tile) * (2 * BM) + rank * BM + q * 32;
-      const bool live = row0 + lane < p.M;
+      const int64_t m = row0 + lane;
+      const bool live = m < p.M;
       const bool any_row = row0 < p.M;
       const bool odd = t & 1;
       const uint32_t t_row = tmem_base + (odd ? ACC1_COL : 0u) + (static_cast<uint32_t>(q * 32) << 16);
+      // The 64 columns the two accumulators share are the last of an even
+      // tile and the first of an odd one: drain them first (even tiles in
+      // reverse chunk order), then release them to the next tile's MMAs.
+      // For SWIGLU they are gate chunks 2-3 (even) or value chunks 0-1 (odd).
 #pragma unroll 1
-      for (int i = 0; i < BN / 32; ++i) {
-        const int c = odd ? i : (BN / 32 - 1 - i);
-        const int32_t n = n_tile * BN + c * 32;
+      for (int i = 0; i < kChunks; ++i) {
+        const int c = odd ? i : (kChunks - 1 - i);
         float v[32];
-        tmem_ld_32x32b_x32(t_row + c * 32, v);
-        if (i == 1) {
-          // the 64 shared columns are in registers: release them to the MMA
-          tc_fence_before();
-          mbar_arrive_cluster(tfree_leader);
-        }
-        if (n >= p.N) continue;  // warp-uniform
-        const int32_t plane = n / p.plane_width;
-        const int32_t col = n - plane * p.plane_width;
-        if (live) {
-#pragma unroll
-          for (int j = 0; j < 32; ++j) v[j] = alpha * v[j];
-          bf16r_x32(v);
-          if (p.bias != nullptr) {
-            const uint4 *bq = reinterpret_cast<const uint4 *>(p.bias + n);
-#pragma unroll
-            for (int g = 0; g < 4; ++g) {
-              uint4 bt = __ldg(bq + g);
-              const __nv_bfloat162 *h = reinterpret_cast<const __nv_bfloat162 *>(&bt);
-#pragma unroll
-              for (int e = 0; e < 4; ++e) {
-                float2 f = __bfloat1622float2(h[e]);
-                v[8 * g + 2 * e] += f.x;
-                v[8 * g + 2 * e + 1] += f.y;
-              }
-            }
-            bf16r_x32(v);
+        if constexpr (kSwiglu) {
+          float g[32];
+          tmem_ld_32x32b_x32(t_row + c * 32, v);
+          tmem_ld_32x32b_x32(t_row + BN_HALF + c * 32, g);
+          if (i == 1) {
+            tc_fence_before();
+            mbar_arrive_cluster(tfree_leader);
           }
-        } else {
+          const int32_t f = n_tile * BN_HALF + c * 32;
+          if (f >= p.F) continue;  // warp-uniform
+          if (live) {
+            alpha_bias(v, alpha, p.bias ? p.bias + f : nullptr);
+            alpha_bias(g, alpha, p.bias ? p.bias + p.F + f : nullptr);
 #pragma unroll
-          for (int j = 0; j < 32; ++j) v[j] = 0.0f;
+            for (int j = 0; j < 32; ++j) v[j] = v[j] * bf16r(silu(g[j]));
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) v[j] = 0.0f;
+          }
+          store_box<EPI_BOXES>(warp_smem, box, &tmOut, v, lane, f, static_cast<int32_t>(row0), 0, any_row);
+        } else {
+          tmem_ld_32x32b_x32(t_row + c * 32, v);
+          if (i == 1) {
+            tc_fence_before();
+            mbar_arrive_cluster(tfree_leader);
+          }
+          const int32_t n = n_tile * BN + c * 32;
+          if (n >= p.N) continue;  // warp-uniform
+          const int32_t plane = n / p.plane_width;
+          const int32_t col = n - plane * p.plane_width;
+          if (live) {
+            alpha_bias(v, alpha, p.bias ? p.bias + n : nullptr);
+            if constexpr (EPI == VFB_EPI_STORE) {
+              // triton_strict_bf16_qkv_direct_merge (h3_fused_ops.py:901-949)
+              const __nv_bfloat16 *ad = plane < 3 ? p.adapter[plane] : nullptr;
+              if (ad != nullptr) {
+                float av[32];
+                load_bf16x32(ad + m * p.adapter_ld + col, av);
+                const float sc = p.scaling[plane];
+#pragma unroll
+                for (int j = 0; j < 32; ++j) av[j] = av[j] * sc;
+                bf16r_x32(av);
+#pragma unroll
+                for (int j = 0; j < 32; ++j) v[j] = v[j] + av[j];
+              }
+            } else if constexpr (EPI == VFB_EPI_GELU_TANH) {
+#pragma unroll
+              for (int j = 0; j < 32; ++j) v[j] = gelu_tanh(v[j]);
+            } else if constexpr (EPI == VFB_EPI_RESIDUAL) {
+              // triton_strict_bf16_gate_residual (h3_fused_ops.py:125-170)
+              if (p.gate != nullptr) {
+                const __nv_bfloat16 *gp = p.gate + (m % p.tokens) * p.gate_ts + n * p.gate_hs;
+#pragma unroll
+                for (int j = 0; j < 32; ++j) v[j] = __bfloat162float(gp[j * p.gate_hs]) * v[j];
+                bf16r_x32(v);
+              }
+              float r[32];
+              load_bf16x32(p.residual + m * p.ldr + n, r);
+#pragma unroll
+              for (int j = 0; j < 32; ++j) v[j] = r[j] + v[j];
+            }
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) v[j] = 0.0f;
+          }
+          store_box<EPI_BOXES>(warp_smem, box, &tmOut, v, lane, col, static_cast<int32_t>(row0), plane, any_row);
         }
-        store_box(warp_smem, box, &tmOut, v, lane, col, static_cast<int32_t>(row0), plane, any_row);
       }
     }
     if (lane == 0) bulk_wait_group_all();
@@ -340,39 +396,51 @@ int map_u8(CUtensorMap *map, const void *base, int64_t rows, int64_t row_bytes, 
   return VFB_OK;
 }
 
-int map_out(CUtensorMap *map, void *base, int64_t width, int64_t rows, int64_t planes) {
-  auto encode = tensor_map_encoder();
-  if (encode == nullptr) return set_error(VFB_ECUDA, "cuTensorMapEncodeTiled is unavailable");
-  cuuint64_t dims[3] = {static_cast<cuuint64_t>(width), static_cast<cuuint64_t>(rows),
-                        static_cast<cuuint64_t>(planes)};
-  cuuint64_t strides[2] = {static_cast<cuuint64_t>(width) * 2, static_cast<cuuint64_t>(width * rows) * 2};
-  cuuint32_t box[3] = {32, 32, 1};
-  cuuint32_t estr[3] = {1, 1, 1};
-  CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, base, dims, strides, box, estr,
-                      CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B,
-                      CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  if (r != CUDA_SUCCESS) return set_error(VFB_ECUDA, "cuTensorMapEncodeTiled (output) failed (%d)", (int)r);
+bool a16(const void *p) { return reinterpret_cast<uintptr_t>(p) % 16 == 0; }
+
+template <int EPI>
+int launch(const CUtensorMap &ta, const CUtensorMap &tb, const CUtensorMap &tb2, const CUtensorMap &tsa,
+           const CUtensorMap &tsb, const CUtensorMap &to, const Params &p, int sms, cudaStream_t stream) {
+  auto kernel = nvfp4_gemm_kernel<EPI>;
+  // the shared-memory opt-in is a function attribute of the device's context: set it once per context
+  static std::atomic<uint64_t> smem_set[kMaxAttrDevices];
+  int rc = ensure_smem_optin(reinterpret_cast<const void *>(kernel), static_cast<int>(SMEM_BYTES), smem_set);
+  if (rc != VFB_OK) return rc;
+  const int tiles = p.num_m_tiles * p.num_n_tiles;
+  const int max_pairs = sms / 2;
+  const int pairs = tiles < max_pairs ? tiles : max_pairs;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(2 * pairs, 1, 1);
+  cfg.blockDim = dim3(NUM_THREADS, 1, 1);
+  cfg.dynamicSmemBytes = SMEM_BYTES;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t err = cudaLaunchKernelEx(&cfg, kernel, ta, tb, tb2, tsa, tsb, to, p);
+  if (err != cudaSuccess) return set_error(VFB_ECUDA, "vfb_nvfp4_gemm launch: %s", cudaGetErrorString(err));
   return VFB_OK;
 }
 
-bool a16(const void *p) { return reinterpret_cast<uintptr_t>(p) % 16 == 0; }
-
-}  // namespace
-}  // namespace vfb
-
-extern "C" int vfb_nvfp4_gemm(const void *A, const void *sfa, const void *W, const void *sfw,
-                              const float *alpha, int64_t M, int64_t N, int64_t K, const void *bias,
-                              void *out, int64_t planes, void *stream) {
-  using namespace vfb;
-  if (M < 0 || N <= 0 || K <= 0 || K % 64 || N % 128 || planes < 1 || planes > 3 || N % planes ||
-      (N / planes) % 32)
-    return set_error(VFB_EINVAL,
-                     "vfb_nvfp4_gemm: need K %% 64 == 0, N %% 128 == 0, 1..3 planes of width %% 32");
+int nvfp4_impl(const char *fn, const void *A, const void *sfa, const void *W, const void *sfw, const float *alpha,
+               const float *alpha_div, int64_t M, int64_t N, int64_t K, const vfb_epilogue *ep, void *stream) {
+  if (ep == nullptr) return set_error(VFB_EINVAL, "%s: epilogue is NULL", fn);
+  const int kind = ep->kind;
+  if (kind != VFB_EPI_STORE && kind != VFB_EPI_GELU_TANH && kind != VFB_EPI_SWIGLU && kind != VFB_EPI_RESIDUAL)
+    return set_error(VFB_EINVAL, "%s: epilogue kind %d is not STORE, GELU_TANH, SWIGLU or RESIDUAL", fn, kind);
+  if (ep->wire_chunks != 0) return set_error(VFB_EINVAL, "%s: no wire layout for NVFP4 outputs", fn);
+  if (M < 0 || N <= 0 || K <= 0 || K % 64 || N % 128 || K > (int64_t)1 << 20 || N > (int64_t)1 << 24)
+    return set_error(VFB_EINVAL, "%s: need K %% 64 == 0 and N %% 128 == 0 (M=%lld N=%lld K=%lld)", fn,
+                     (long long)M, (long long)N, (long long)K);
   if (M == 0) return VFB_OK;
-  if (!A || !sfa || !W || !sfw || !alpha || !out)
-    return set_error(VFB_EINVAL, "vfb_nvfp4_gemm: NULL operand");
-  if (!a16(A) || !a16(W) || !a16(sfa) || !a16(sfw) || !a16(out) || (bias && !a16(bias)))
-    return set_error(VFB_EINVAL, "vfb_nvfp4_gemm: operands must be 16-byte aligned");
+  if (!A || !sfa || !W || !sfw || !alpha || !ep->out) return set_error(VFB_EINVAL, "%s: NULL operand", fn);
+  if (!a16(A) || !a16(W) || !a16(sfa) || !a16(sfw) || !a16(ep->out) || (ep->bias && !a16(ep->bias)) ||
+      ep->ldo % 8)
+    return set_error(VFB_EINVAL, "%s: operands must be 16-byte aligned, ldo %% 8 == 0", fn);
   int sms = 0;
   int rc = check_device(&sms);
   if (rc != VFB_OK) return rc;
@@ -381,17 +449,66 @@ extern "C" int vfb_nvfp4_gemm(const void *A, const void *sfa, const void *W, con
   p.N = N;
   p.K = K;
   p.alpha = alpha;
-  p.bias = static_cast<const __nv_bfloat16 *>(bias);
-  p.plane_width = static_cast<int32_t>(N / planes);
+  p.alpha_div = alpha_div;
+  p.bias = static_cast<const __nv_bfloat16 *>(ep->bias);
   p.num_m_tiles = static_cast<int>((M + 2 * BM - 1) / (2 * BM));
-  p.num_n_tiles = static_cast<int>((N + BN - 1) / BN);
   p.ktiles = static_cast<int>(K / 64);
   p.status = device_status_ptr();
   const int64_t a_blocks = (M + 127) / 128;  // 128-row scale blocks of the activation
   const int64_t w_blocks = N / 128;
-  CUtensorMap ta, tb, tsa, tsb, to;
+  CUtensorMap ta, tb, tb2, tsa, tsb, to;
   if ((rc = map_u8(&ta, A, M, K / 2, BK_BYTES, BM, CU_TENSOR_MAP_SWIZZLE_128B)) != VFB_OK) return rc;
-  if ((rc = map_u8(&tb, W, N, K / 2, BK_BYTES, BN_HALF, CU_TENSOR_MAP_SWIZZLE_128B)) != VFB_OK) return rc;
+  if (kind == VFB_EPI_SWIGLU) {
+    const int64_t F = N / 2;
+    if (F % 128 || ep->ldo < F)
+      return set_error(VFB_EINVAL, "%s: SWIGLU needs the packed N = 2F with F %% 128 == 0 and ldo >= F", fn);
+    p.F = static_cast<int32_t>(F);
+    p.plane_width = static_cast<int32_t>(F);
+    p.num_n_tiles = static_cast<int>(F / BN_HALF);
+    if ((rc = map_u8(&tb, W, F, K / 2, BK_BYTES, BN_HALF, CU_TENSOR_MAP_SWIZZLE_128B)) != VFB_OK) return rc;
+    if ((rc = map_u8(&tb2, static_cast<const uint8_t *>(W) + F * (K / 2), F, K / 2, BK_BYTES, BN_HALF,
+                     CU_TENSOR_MAP_SWIZZLE_128B)) != VFB_OK)
+      return rc;
+    if ((rc = make_map_out(&to, ep->out, F, M, 1, ep->ldo, M * ep->ldo)) != VFB_OK) return rc;
+  } else {
+    if (ep->plane_width < 0 || (ep->plane_width > 0 && (ep->plane_width % 32 || N % ep->plane_width)))
+      return set_error(VFB_EINVAL, "%s: plane_width must be 0 or a multiple of 32 dividing N", fn);
+    const int64_t width = ep->plane_width > 0 ? ep->plane_width : N;
+    const int64_t planes = N / width;
+    if (ep->ldo < width) return set_error(VFB_EINVAL, "%s: ldo smaller than the plane width", fn);
+    const int64_t plane_stride = planes > 1 ? ep->plane_stride : M * ep->ldo;
+    if (plane_stride % 8 || (planes > 1 && plane_stride < M * ep->ldo))
+      return set_error(VFB_EINVAL, "%s: plane_stride must be a multiple of 8 and >= M*ldo", fn);
+    p.plane_width = static_cast<int32_t>(width);
+    p.num_n_tiles = static_cast<int>((N + BN - 1) / BN);
+    if ((rc = map_u8(&tb, W, N, K / 2, BK_BYTES, BN_HALF, CU_TENSOR_MAP_SWIZZLE_128B)) != VFB_OK) return rc;
+    tb2 = tb;
+    if ((rc = make_map_out(&to, ep->out, width, M, planes, ep->ldo, plane_stride)) != VFB_OK) return rc;
+    if (kind == VFB_EPI_STORE) {
+      for (int i = 0; i < 3; ++i) {
+        p.adapter[i] = static_cast<const __nv_bfloat16 *>(ep->adapter[i]);
+        p.scaling[i] = ep->scaling[i];
+        if (p.adapter[i] != nullptr &&
+            (i >= planes || !a16(p.adapter[i]) || ep->adapter_ld % 8 || ep->adapter_ld < width))
+          return set_error(VFB_EINVAL, "%s: adapter %d misaligned or beyond the planes", fn, i);
+      }
+      p.adapter_ld = ep->adapter_ld;
+    }
+    if (kind == VFB_EPI_RESIDUAL) {
+      if (ep->residual == nullptr || !a16(ep->residual) || ep->ldr % 8 || ep->ldr < N || planes != 1)
+        return set_error(VFB_EINVAL, "%s: RESIDUAL needs a 16-byte aligned [M,N] residual and one plane", fn);
+      p.residual = static_cast<const __nv_bfloat16 *>(ep->residual);
+      p.ldr = ep->ldr;
+      p.gate = static_cast<const __nv_bfloat16 *>(ep->gate);
+      if (p.gate != nullptr) {
+        if (ep->tokens <= 0) return set_error(VFB_EINVAL, "%s: gate needs tokens > 0", fn);
+        p.gate_ts = ep->gate_token_stride;
+        p.gate_hs = ep->gate_hidden_stride;
+        p.tokens = ep->tokens;
+      }
+    }
+  }
+  p.band_n = band_width(p.num_n_tiles, K / 2);
   // scale buffers viewed as rows of 256 bytes (two rows per 512-byte block)
   if ((rc = map_u8(&tsa, sfa, a_blocks * p.ktiles * 2, 256, 256, 2 * KB_PER_STAGE,
                    CU_TENSOR_MAP_SWIZZLE_NONE)) != VFB_OK)
@@ -399,28 +516,40 @@ extern "C" int vfb_nvfp4_gemm(const void *A, const void *sfa, const void *W, con
   if ((rc = map_u8(&tsb, sfw, w_blocks * p.ktiles * 2, 256, 256, 2 * KB_PER_STAGE,
                    CU_TENSOR_MAP_SWIZZLE_NONE)) != VFB_OK)
     return rc;
-  if ((rc = map_out(&to, out, N / planes, M, planes)) != VFB_OK) return rc;
-  // the shared-memory opt-in is a function attribute of the device's context: set it once per context
-  static std::atomic<uint64_t> smem_set[kMaxAttrDevices];
-  if ((rc = ensure_smem_optin(reinterpret_cast<const void *>(nvfp4_gemm_kernel), static_cast<int>(SMEM_BYTES),
-                              smem_set)) != VFB_OK)
-    return rc;
-  const int tiles = p.num_m_tiles * p.num_n_tiles;
-  const int max_pairs = sms / 2;
-  const int pairs = tiles < max_pairs ? tiles : max_pairs;
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(2 * pairs, 1, 1);
-  cfg.blockDim = dim3(NUM_THREADS, 1, 1);
-  cfg.dynamicSmemBytes = SMEM_BYTES;
-  cfg.stream = static_cast<cudaStream_t>(stream);
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = 2;
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  cudaError_t err = cudaLaunchKernelEx(&cfg, nvfp4_gemm_kernel, ta, tb, tsa, tsb, to, p);
-  if (err != cudaSuccess) return set_error(VFB_ECUDA, "vfb_nvfp4_gemm launch: %s", cudaGetErrorString(err));
-  return VFB_OK;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  switch (kind) {
+    case VFB_EPI_GELU_TANH:
+      return launch<VFB_EPI_GELU_TANH>(ta, tb, tb2, tsa, tsb, to, p, sms, s);
+    case VFB_EPI_SWIGLU:
+      return launch<VFB_EPI_SWIGLU>(ta, tb, tb2, tsa, tsb, to, p, sms, s);
+    case VFB_EPI_RESIDUAL:
+      return launch<VFB_EPI_RESIDUAL>(ta, tb, tb2, tsa, tsb, to, p, sms, s);
+    default:
+      return launch<VFB_EPI_STORE>(ta, tb, tb2, tsa, tsb, to, p, sms, s);
+  }
+}
+
+}  // namespace
+}  // namespace vfb
+
+extern "C" int vfb_nvfp4_gemm(const void *A, const void *sfa, const void *W, const void *sfw,
+                              const float *alpha, int64_t M, int64_t N, int64_t K, const void *bias,
+                              void *out, int64_t planes, void *stream) {
+  using namespace vfb;
+  if (planes < 1 || planes > 3 || N <= 0 || N % planes || (N / planes) % 32)
+    return set_error(VFB_EINVAL, "vfb_nvfp4_gemm: need K %% 64 == 0, N %% 128 == 0, 1..3 planes of width %% 32");
+  vfb_epilogue ep{};
+  ep.kind = VFB_EPI_STORE;
+  ep.out = out;
+  ep.ldo = N / planes;
+  ep.plane_width = planes > 1 ? N / planes : 0;
+  ep.plane_stride = M * (N / planes);
+  ep.bias = bias;
+  return nvfp4_impl("vfb_nvfp4_gemm", A, sfa, W, sfw, alpha, nullptr, M, N, K, &ep, stream);
+}
+
+extern "C" int vfb_nvfp4_gemm_ex(const void *A, const void *sfa, const void *W, const void *sfw,
+                                 const float *alpha, const float *alpha_div, int64_t M, int64_t N, int64_t K,
+                                 const vfb_epilogue *ep, void *stream) {
+  return vfb::nvfp4_impl("vfb_nvfp4_gemm_ex", A, sfa, W, sfw, alpha, alpha_div, M, N, K, ep, stream);
 }

@@ -152,35 +152,8 @@ class Epilogue:
     wire_chunks: int = 0
 
 
-def fp8_gemm(a_codes: torch.Tensor, a_scales: torch.Tensor, rows: int, weight: torch.Tensor,
-             w_scales: torch.Tensor, epilogue: Epilogue | None = None,
-             out: torch.Tensor | None = None) -> torch.Tensor:
-    """Row-scaled e4m3 GEMM ``bf16(sa * sw * A @ W^T)`` with a fused epilogue.
-
-    ``a_codes`` e4m3 ``[>=rows, K]``, ``a_scales`` fp32 (>= rows entries),
-    ``weight`` e4m3 ``[N, K]`` row-major, ``w_scales`` fp32 ``[N, 1]``.
-    Returns bf16 ``[rows, N]`` (``[rows, N/2]`` for SWIGLU, ``[planes, rows,
-    N/planes]`` when the output is split into planes, ``[chunks, 2, 3, rows,
-    N/(6 chunks)]`` in the wire layout).
-    """
-    ep = epilogue or Epilogue()
-    n, k = weight.shape
-    device = a_codes.device
-    if (a_codes.dtype != FP8 or weight.dtype != FP8 or a_codes.ndim != 2 or a_codes.shape[1] != k
-            or a_codes.stride(1) != 1 or weight.stride(1) != 1 or a_codes.shape[0] < rows):
-        raise KernelInputError("FP8 GEMM operands differ from the declared e4m3 layout")
-    if a_scales.dtype != torch.float32 or w_scales.dtype != torch.float32 or not w_scales.is_contiguous():
-        raise KernelInputError("FP8 GEMM scales must be contiguous fp32")
-    if not a_scales.is_contiguous() or a_scales.numel() < rows or w_scales.numel() != n:
-        raise KernelInputError("FP8 GEMM scale vectors have the wrong length")
-    if k % 16 or n % 32:
-        raise KernelInputError("FP8 GEMM needs K % 16 == 0 and N % 32 == 0")
-    for t in (a_codes, weight, w_scales):
-        if t.device != device:
-            raise KernelInputError("FP8 GEMM operands must share one device")
-    if not (_aligned(a_codes) and _aligned(weight) and _aligned(w_scales)):
-        raise KernelInputError("FP8 GEMM operands must be 16-byte aligned")
-
+def _build_epilogue(ep: Epilogue, rows: int, n: int, device, out: torch.Tensor | None):
+    """The ``vfb_epilogue`` of ``ep`` for a GEMM with ``rows`` x ``n`` outputs, and its output tensor."""
     e = _lib.Epilogue()
     e.kind = ep.kind
     if ep.bias is not None:
@@ -261,6 +234,39 @@ def fp8_gemm(a_codes: torch.Tensor, a_scales: torch.Tensor, rows: int, weight: t
             e.gate_token_stride = g.stride(0)
             e.gate_hidden_stride = g.stride(1)
             e.tokens = ep.tokens
+    return e, out
+
+
+def fp8_gemm(a_codes: torch.Tensor, a_scales: torch.Tensor, rows: int, weight: torch.Tensor,
+             w_scales: torch.Tensor, epilogue: Epilogue | None = None,
+             out: torch.Tensor | None = None) -> torch.Tensor:
+    """Row-scaled e4m3 GEMM ``bf16(sa * sw * A @ W^T)`` with a fused epilogue.
+
+    ``a_codes`` e4m3 ``[>=rows, K]``, ``a_scales`` fp32 (>= rows entries),
+    ``weight`` e4m3 ``[N, K]`` row-major, ``w_scales`` fp32 ``[N, 1]``.
+    Returns bf16 ``[rows, N]`` (``[rows, N/2]`` for SWIGLU, ``[planes, rows,
+    N/planes]`` when the output is split into planes, ``[chunks, 2, 3, rows,
+    N/(6 chunks)]`` in the wire layout).
+    """
+    ep = epilogue or Epilogue()
+    n, k = weight.shape
+    device = a_codes.device
+    if (a_codes.dtype != FP8 or weight.dtype != FP8 or a_codes.ndim != 2 or a_codes.shape[1] != k
+            or a_codes.stride(1) != 1 or weight.stride(1) != 1 or a_codes.shape[0] < rows):
+        raise KernelInputError("FP8 GEMM operands differ from the declared e4m3 layout")
+    if a_scales.dtype != torch.float32 or w_scales.dtype != torch.float32 or not w_scales.is_contiguous():
+        raise KernelInputError("FP8 GEMM scales must be contiguous fp32")
+    if not a_scales.is_contiguous() or a_scales.numel() < rows or w_scales.numel() != n:
+        raise KernelInputError("FP8 GEMM scale vectors have the wrong length")
+    if k % 16 or n % 32:
+        raise KernelInputError("FP8 GEMM needs K % 16 == 0 and N % 32 == 0")
+    for t in (a_codes, weight, w_scales):
+        if t.device != device:
+            raise KernelInputError("FP8 GEMM operands must share one device")
+    if not (_aligned(a_codes) and _aligned(weight) and _aligned(w_scales)):
+        raise KernelInputError("FP8 GEMM operands must be 16-byte aligned")
+
+    e, out = _build_epilogue(ep, rows, n, device, out)
     if rows == 0:
         return out
     lib = _lib.load()
@@ -281,28 +287,22 @@ def nvfp4_sf_shape(rows: int, cols: int) -> tuple[int, int]:
     return (-(-rows // 128) * 128, -(-(cols // 16) // 4) * 4)
 
 
-def fp8_ffn(x: torch.Tensor, up: torch.Tensor, up_scales: torch.Tensor, down: torch.Tensor,
-            down_scales: torch.Tensor, *, activation: int = _lib.EPI_GELU_TANH, up_bias=None, down_bias=None,
-            residual=None, gate=None) -> torch.Tensor:
-    """The whole FP8 FFN through ``vfb_fp8_ffn`` (one C call, workspace from torch's allocator).
-
-    ``x`` bf16 ``[M, H]`` (unit column stride), ``up`` e4m3 ``[F or 2F, H]``,
-    ``down`` e4m3 ``[H, F]``, scales fp32 ``[N, 1]``; ``residual`` bf16
-    ``[M, H]`` and ``gate`` bf16 ``[tokens, H]`` as the down GEMM's RESIDUAL
-    epilogue.  Returns bf16 ``[M, H]``.
-    """
-    rows, hidden = x.shape
+def _ffn_operands(rows, hidden, device, up, up_scales, down, down_scales, activation, up_bias, down_bias,
+                  residual, gate):
     n_up = up.shape[0]
     width = n_up // 2 if activation == _lib.EPI_SWIGLU else n_up
-    device = x.device
-    if (x.dtype != BF16 or x.stride(1) != 1 or up.dtype != FP8 or down.dtype != FP8
-            or up.shape[1] != hidden or down.shape != (hidden, width) or not up.is_contiguous()
-            or not down.is_contiguous() or up_scales.numel() != n_up or down_scales.numel() != hidden
-            or up_scales.dtype != torch.float32 or down_scales.dtype != torch.float32):
+    if (up.dtype != FP8 or down.dtype != FP8 or up.ndim != 2 or up.shape[1] != hidden
+            or down.shape != (hidden, width) or not up.is_contiguous() or not down.is_contiguous()
+            or up_scales.numel() != n_up or down_scales.numel() != hidden
+            or up_scales.dtype != torch.float32 or down_scales.dtype != torch.float32
+            or not up_scales.is_contiguous() or not down_scales.is_contiguous()):
         raise KernelInputError("FP8 FFN operands differ from the declared layouts")
     for t in (up, down, up_scales, down_scales, up_bias, down_bias, residual, gate):
         if t is not None and t.device != device:
             raise KernelInputError("FP8 FFN operands must share one device")
+    for name, b, n in (("up", up_bias, n_up), ("down", down_bias, hidden)):
+        if b is not None and (b.dtype != BF16 or b.shape != (n,) or not b.is_contiguous()):
+            raise KernelInputError(f"FP8 FFN {name} bias must be contiguous bf16 [{n}]")
     if residual is not None and (residual.dtype != BF16 or residual.shape != (rows, hidden)
                                  or residual.stride(1) != 1):
         raise KernelInputError("FP8 FFN residual must be bf16 [M, H] with unit column stride")
@@ -313,19 +313,63 @@ def fp8_ffn(x: torch.Tensor, up: torch.Tensor, up_scales: torch.Tensor, down: to
     need = lib.vfb_fp8_ffn_workspace_bytes(rows, hidden, width)
     if need < 0:
         raise KernelInputError("FP8 FFN shape is outside the supported range")
-    out = torch.empty((rows, hidden), device=device, dtype=BF16)
     workspace = torch.empty(need + 256, device=device, dtype=torch.uint8)
     base = workspace.data_ptr() + (-workspace.data_ptr()) % 256
+    ptr = lambda t: None if t is None else t.data_ptr()  # noqa: E731
+    tail = [up.data_ptr(), up_scales.data_ptr(), n_up, down.data_ptr(), down_scales.data_ptr(), activation,
+            ptr(up_bias), ptr(down_bias), ptr(residual), 0 if residual is None else residual.stride(0),
+            ptr(gate), 0 if gate is None else gate.stride(0), 0 if gate is None else gate.shape[0]]
+    return lib, need, workspace, base, tail
+
+
+def fp8_ffn(x: torch.Tensor, up: torch.Tensor, up_scales: torch.Tensor, down: torch.Tensor,
+            down_scales: torch.Tensor, *, activation: int = _lib.EPI_GELU_TANH, up_bias=None, down_bias=None,
+            residual=None, gate=None) -> torch.Tensor:
+    """The whole FP8 FFN through ``vfb_fp8_ffn`` (one C call, workspace from torch's allocator).
+
+    ``x`` bf16 ``[M, H]`` (unit column stride), ``up`` e4m3 ``[F or 2F, H]``,
+    ``down`` e4m3 ``[H, F]``, scales fp32 ``[N, 1]``; ``residual`` bf16
+    ``[M, H]`` and ``gate`` bf16 ``[tokens, H]`` as the down GEMM's RESIDUAL
+    epilogue.  Returns bf16 ``[M, H]``.
+    """
+    if x.dtype != BF16 or x.ndim != 2 or x.stride(1) != 1:
+        raise KernelInputError("FP8 FFN input must be bf16 [M, H] with unit column stride")
+    rows, hidden = x.shape
+    device = x.device
+    lib, need, workspace, base, tail = _ffn_operands(rows, hidden, device, up, up_scales, down, down_scales,
+                                                     activation, up_bias, down_bias, residual, gate)
+    out = torch.empty((rows, hidden), device=device, dtype=BF16)
     with torch.cuda.device(device):
-        rc = lib.vfb_fp8_ffn(
-            x.data_ptr(), rows, hidden, x.stride(0), up.data_ptr(), up_scales.data_ptr(), n_up,
-            down.data_ptr(), down_scales.data_ptr(), activation,
-            None if up_bias is None else up_bias.data_ptr(), None if down_bias is None else down_bias.data_ptr(),
-            None if residual is None else residual.data_ptr(), 0 if residual is None else residual.stride(0),
-            None if gate is None else gate.data_ptr(), 0 if gate is None else gate.stride(0),
-            0 if gate is None else gate.shape[0], out.data_ptr(), hidden, base, need,
-            _lib.stream_handle(device))
+        rc = lib.vfb_fp8_ffn(x.data_ptr(), rows, hidden, x.stride(0), *tail, out.data_ptr(), hidden, base, need,
+                             _lib.stream_handle(device))
     _lib.check(rc, "vfb_fp8_ffn")
+    return out
+
+
+def fp8_ffn_quantized(codes: torch.Tensor, scales: torch.Tensor, rows: int, up: torch.Tensor,
+                      up_scales: torch.Tensor, down: torch.Tensor, down_scales: torch.Tensor, *,
+                      activation: int = _lib.EPI_GELU_TANH, up_bias=None, down_bias=None, residual=None,
+                      gate=None) -> torch.Tensor:
+    """``fp8_ffn`` on an input already quantised per token (``vfb_fp8_ffn_quantized``).
+
+    ``codes`` e4m3 ``[>= rows, H]`` contiguous and ``scales`` fp32 (``>= rows``
+    entries), e.g. from ``quantize_fp8_norm_modulate``.
+    """
+    if (codes.dtype != FP8 or codes.ndim != 2 or not codes.is_contiguous() or codes.shape[0] < rows
+            or scales.dtype != torch.float32 or not scales.is_contiguous() or scales.numel() < rows
+            or scales.device != codes.device):
+        raise KernelInputError("FP8 FFN codes must be contiguous e4m3 [>= M, H] with fp32 scales")
+    hidden = codes.shape[1]
+    device = codes.device
+    lib, need, workspace, base, tail = _ffn_operands(rows, hidden, device, up, up_scales, down, down_scales,
+                                                     activation, up_bias, down_bias, residual, gate)
+    out = torch.empty((rows, hidden), device=device, dtype=BF16)
+    if rows == 0:
+        return out
+    with torch.cuda.device(device):
+        rc = lib.vfb_fp8_ffn_quantized(codes.data_ptr(), scales.data_ptr(), rows, hidden, *tail, out.data_ptr(),
+                                       hidden, base, need, _lib.stream_handle(device))
+    _lib.check(rc, "vfb_fp8_ffn_quantized")
     return out
 
 
@@ -391,38 +435,50 @@ def nvfp4_quantize(matrix: torch.Tensor, global_scale: torch.Tensor):
 
 def nvfp4_gemm(a_codes: torch.Tensor, a_sf: torch.Tensor, w_packed: torch.Tensor,
                w_scales: torch.Tensor, alpha: torch.Tensor, bias: torch.Tensor | None = None,
-               planes: int = 1) -> torch.Tensor:
-    """``bf16(alpha * A @ W^T)`` (+ bias) for NVFP4 operands in the 128x4 scale layout."""
+               planes: int = 1, *, alpha_div: torch.Tensor | None = None,
+               epilogue: Epilogue | None = None) -> torch.Tensor:
+    """``bf16(alpha * A @ W^T)`` (+ bias, + epilogue) for NVFP4 operands in the 128x4 scale layout.
+
+    ``alpha`` (and ``alpha_div``, when given: the GEMM uses ``alpha / alpha_div``
+    computed on the device) are fp32 scalar tensors.  ``epilogue`` selects the
+    fused step after the bias (``Epilogue`` kinds STORE with planes and LoRA
+    adapters, GELU_TANH, SWIGLU over the packed ``[2F, K/2]`` weight, or
+    RESIDUAL); ``bias`` / ``planes`` are the plain-store shorthand.
+    """
     rows, half_k = a_codes.shape
     n = w_packed.shape[0]
     k = 2 * half_k
     if (a_codes.dtype != torch.uint8 or w_packed.dtype != torch.uint8 or w_packed.shape[1] != half_k
             or not a_codes.is_contiguous() or not w_packed.is_contiguous()):
         raise KernelInputError("NVFP4 GEMM codes must be contiguous uint8 [M,K/2] and [N,K/2]")
-    if k % 64 or n % 128 or n % planes or (n // planes) % 32:
+    ep = epilogue or Epilogue(bias=bias, planes=planes)
+    if epilogue is not None and (bias is not None or planes != 1):
+        raise KernelInputError("pass bias and planes inside the epilogue")
+    if k % 64 or n % 128 or n % ep.planes or (n // ep.planes) % 32:
         raise KernelInputError("NVFP4 GEMM needs K % 64 == 0, N % 128 == 0")
+    if ep.kind == _lib.EPI_SWIGLU and (n // 2) % 128:
+        raise KernelInputError("NVFP4 SwiGLU needs the packed [2F, K/2] weight with F % 128 == 0")
+    if ep.kind == _lib.EPI_QKV_NORM_ROPE or ep.wire_chunks:
+        raise KernelInputError("NVFP4 GEMM has no QK-norm or wire-layout epilogue")
     pr, pc = nvfp4_sf_shape(rows, k)
     if (a_sf.dtype != torch.uint8 or a_sf.numel() != pr * pc or not a_sf.is_contiguous()
             or w_scales.dtype != torch.uint8 or w_scales.numel() != n * (k // 16)
             or not w_scales.is_contiguous()):
         raise KernelInputError("NVFP4 GEMM scales differ from the 128x4 layout")
-    if alpha.dtype != torch.float32 or alpha.numel() != 1:
-        raise KernelInputError("NVFP4 GEMM alpha must be an fp32 scalar tensor")
+    for name, scalar in (("alpha", alpha), ("alpha_div", alpha_div)):
+        if scalar is not None and (scalar.dtype != torch.float32 or scalar.numel() != 1):
+            raise KernelInputError(f"NVFP4 GEMM {name} must be an fp32 scalar tensor")
     device = a_codes.device
-    for t in (a_sf, w_packed, w_scales, alpha):
-        if t.device != device:
+    for t in (a_sf, w_packed, w_scales, alpha, alpha_div):
+        if t is not None and t.device != device:
             raise KernelInputError("NVFP4 GEMM operands must share one device")
-    if bias is not None and (bias.dtype != BF16 or bias.shape != (n,) or not bias.is_contiguous()):
-        raise KernelInputError("NVFP4 GEMM bias must be contiguous bf16 [N]")
-    shape = (rows, n) if planes == 1 else (planes, rows, n // planes)
-    out = torch.empty(shape, device=device, dtype=BF16)
+    e, out = _build_epilogue(ep, rows, n, device, None)
     if rows == 0:
         return out
     lib = _lib.load()
     with torch.cuda.device(device):
-        rc = lib.vfb_nvfp4_gemm(a_codes.data_ptr(), a_sf.data_ptr(), w_packed.data_ptr(),
-                                w_scales.data_ptr(), alpha.data_ptr(), rows, n, k,
-                                None if bias is None else bias.data_ptr(), out.data_ptr(), planes,
-                                _lib.stream_handle(device))
-    _lib.check(rc, "vfb_nvfp4_gemm")
+        rc = lib.vfb_nvfp4_gemm_ex(a_codes.data_ptr(), a_sf.data_ptr(), w_packed.data_ptr(), w_scales.data_ptr(),
+                                   alpha.data_ptr(), None if alpha_div is None else alpha_div.data_ptr(), rows, n,
+                                   k, ctypes.byref(e), _lib.stream_handle(device))
+    _lib.check(rc, "vfb_nvfp4_gemm_ex")
     return out

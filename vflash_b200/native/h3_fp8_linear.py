@@ -38,7 +38,8 @@ from typing import Any
 import torch
 
 from .. import _lib
-from ..kernels import Epilogue, bf16_gemm, fp8_gemm, quantize_fp8_norm_modulate, quantize_fp8_rows
+from ..kernels import (Epilogue, bf16_gemm, fp8_ffn, fp8_ffn_quantized, fp8_gemm, quantize_fp8_norm_modulate,
+                       quantize_fp8_rows)
 
 
 @dataclass(frozen=True)
@@ -359,14 +360,17 @@ class RowFP8Execution:
 
     def ffn(self, value, up_weight, up_scale, down_weight, down_scale, *, activation="gelu_tanh",
             up_bias=None, down_bias=None, residual=None, gate=None, prologue: NormModulate | None = None):
-        """Fused FFN: up GEMM + activation epilogue -> per-token e4m3 requant -> down GEMM.
+        """Fused FFN: up GEMM + activation -> per-token e4m3 requant -> down GEMM.
 
         ``activation`` is ``"gelu_tanh"`` (up weight ``[F, H]``) or ``"swiglu"``
         (packed up weight ``[2F, H]``).  The down GEMM's epilogue adds
         ``residual`` (and multiplies by ``gate`` first) when given.  The
-        bf16 intermediate is requantised per token over its full row, exactly
-        as the reference quantises the activation of the next linear
-        (src/vflash/native/h3_fp8_activation.py:16-19).
+        intermediate is requantised per token over its full row, exactly as
+        the reference quantises the activation of the next linear
+        (src/vflash/native/h3_fp8_activation.py:16-19).  One native call
+        (``vfb_fp8_ffn``, or ``vfb_fp8_ffn_quantized`` after a fused
+        ``prologue``): the up GEMM, the requantisation and the down GEMM run
+        as one kernel whose bf16 intermediate stays in L2.
         """
         if (
             down_weight.ndim != 2
@@ -383,34 +387,27 @@ class RowFP8Execution:
             or down_bias.dtype != value.dtype
         ):
             raise ValueError("FP8 bias differs from the declared output")
+        if activation not in ("gelu_tanh", "swiglu"):
+            raise ValueError("unknown FFN activation")
         shape, matrix, rows = self._fused_prologue(value, up_weight, up_scale, up_bias)
         hidden = down_weight.shape[0]
-        codes, act_scale = self._quantize(matrix, prologue, shape)
-        with self.measure("linear.fp8_gemm"):
-            if activation == "gelu_tanh":
-                mid = fp8_gemm(codes, act_scale, rows, up_weight, up_scale,
-                               Epilogue(kind=_lib.EPI_GELU_TANH, bias=up_bias))
-            elif activation == "swiglu":
-                mid = fp8_gemm(codes, act_scale, rows, up_weight, up_scale,
-                               Epilogue(kind=_lib.EPI_SWIGLU, bias=up_bias))
-            else:
-                raise ValueError("unknown FFN activation")
-        if mid.shape[1] != down_weight.shape[1]:
+        width = up_weight.shape[0] // 2 if activation == "swiglu" else up_weight.shape[0]
+        if width != down_weight.shape[1]:
             raise ValueError("FFN down weight differs from the intermediate width")
-        mid_codes, mid_scale = self._quantize(mid)
-        self.calls["w8a8"] += 1
-        with self.measure("linear.fp8_gemm"):
-            if residual is None:
-                out = fp8_gemm(mid_codes, mid_scale, rows, down_weight, down_scale,
-                               Epilogue(bias=down_bias))
-            else:
-                if residual.dtype != torch.bfloat16 or residual.shape != (*shape[:-1], hidden):
-                    raise ValueError("FP8 residual differs from the declared output")
-                tokens = 0 if gate is None else gate.shape[0]
-                out = fp8_gemm(mid_codes, mid_scale, rows, down_weight, down_scale,
-                               Epilogue(kind=_lib.EPI_RESIDUAL, bias=down_bias,
-                                        residual=residual.reshape(rows, hidden), gate=gate,
-                                        tokens=tokens))
+        if residual is not None and (residual.dtype != torch.bfloat16 or residual.shape != (*shape[:-1], hidden)):
+            raise ValueError("FP8 residual differs from the declared output")
+        kind = _lib.EPI_SWIGLU if activation == "swiglu" else _lib.EPI_GELU_TANH
+        args = dict(activation=kind, up_bias=up_bias, down_bias=down_bias,
+                    residual=None if residual is None else residual.reshape(rows, hidden), gate=gate)
+        self.calls["w8a8"] += 1  # the FFN's second linear
+        if prologue is None:
+            with self.measure("linear.fp8_gemm"):
+                out = fp8_ffn(matrix, up_weight, up_scale, down_weight, down_scale, **args)
+        else:
+            codes, act_scale = self._quantize(matrix, prologue, shape)
+            with self.measure("linear.fp8_gemm"):
+                out = fp8_ffn_quantized(codes, act_scale, rows, up_weight, up_scale, down_weight, down_scale,
+                                        **args)
         return out.reshape(*shape[:-1], hidden)
 
 

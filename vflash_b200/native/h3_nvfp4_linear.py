@@ -18,7 +18,8 @@ from functools import cache
 
 import torch
 
-from ..kernels import nvfp4_gemm, nvfp4_quantize
+from .. import _lib
+from ..kernels import Epilogue, nvfp4_gemm, nvfp4_quantize
 
 SF_LAYOUT_128x4 = "128x4"
 
@@ -97,6 +98,17 @@ class NVFP4Execution:
         self._ops = None
 
     def linear(self, values, weight: NVFP4Weight, bias=None):
+        """``bf16(mm_fp4(nvfp4_quantize(values), W) * alpha / input_scale) + bias``.
+
+        With the native operators the division of the two calibration scalars
+        and the bias add run inside the GEMM's epilogue (one quantiser launch
+        and one GEMM launch per call); operators supplied through
+        ``_operators`` (e.g. a test's fakes) get the reference's call
+        sequence and arguments (h3_nvfp4_linear.py:100-139).
+        """
+        return self._run(values, weight, bias, Epilogue(bias=bias))
+
+    def _run(self, values, weight: NVFP4Weight, bias, epilogue: Epilogue, out_features=None):
         if (
             values.ndim < 1
             or values.shape[-1] != weight.in_features
@@ -132,6 +144,19 @@ class NVFP4Execution:
             raise ValueError("The quantizer omitted the required 128x4 scale padding")
         if codes.dtype != torch.uint8 or codes.shape != (matrix.shape[0], weight.in_features // 2):
             raise ValueError("The quantizer returned a different packed layout")
+        width = out_features or weight.out_features
+        if matmul is _matmul:
+            output = nvfp4_gemm(codes, scales, weight.packed, weight.scales, weight.alpha,
+                                alpha_div=weight.input_scale, epilogue=epilogue)
+            self.calls += 1
+            self.rows += matrix.shape[0]
+            if isinstance(output, torch.Tensor) and output.ndim == 3:  # Q, K, V planes
+                return tuple(output[i].reshape(*shape[:-1], output.shape[-1]) for i in range(output.shape[0]))
+            if output.dtype != torch.bfloat16 or output.shape != (matrix.shape[0], width):
+                raise ValueError("The NVFP4 kernel returned a different output layout")
+            return output.reshape(*shape[:-1], width)
+        if epilogue.kind != _lib.EPI_STORE or epilogue.planes != 1 or epilogue.adapters is not None:
+            raise ValueError("fused NVFP4 epilogues need the native operators")
         output = matmul(
             codes,
             weight.packed.T,
@@ -151,3 +176,55 @@ class NVFP4Execution:
         self.rows += matrix.shape[0]
         output = output.reshape(*shape[:-1], weight.out_features)
         return output if bias is None else output + bias
+
+    # -- fused entry points (opt-in): the strict-BF16 step after the linear runs
+    # in the GEMM's epilogue, as for RowFP8Execution
+    def _check_bias(self, values, bias, n):
+        if bias is not None and (bias.shape != (n,) or bias.device != values.device
+                                 or bias.dtype != torch.bfloat16):
+            raise ValueError("NVFP4 bias must match its BF16 output")
+
+    def gelu_linear(self, values, weight: NVFP4Weight, bias=None):
+        """``F.gelu(linear(values, weight, bias), approximate="tanh")`` with the GELU in the epilogue."""
+        self._check_bias(values, bias, weight.out_features)
+        return self._run(values, weight, bias, Epilogue(kind=_lib.EPI_GELU_TANH, bias=bias))
+
+    def swiglu_linear(self, values, weight: NVFP4Weight, bias=None):
+        """Packed FFN input ``[2F, K]`` with ``value * bf16(silu(gate))`` fused (h3_fused_ops.py:185-224)."""
+        if weight.out_features % 256:
+            raise ValueError("packed NVFP4 SwiGLU weight needs 2F rows with F % 128 == 0")
+        self._check_bias(values, bias, weight.out_features)
+        return self._run(values, weight, bias, Epilogue(kind=_lib.EPI_SWIGLU, bias=bias),
+                         out_features=weight.out_features // 2)
+
+    def gate_residual_linear(self, values, weight: NVFP4Weight, residual, gate=None, bias=None):
+        """``residual + bf16(gate * linear(...))`` fused (h3_fused_ops.py:125-170); gate ``[tokens, N]``."""
+        self._check_bias(values, bias, weight.out_features)
+        n = weight.out_features
+        if (residual.dtype != torch.bfloat16 or residual.shape != (*values.shape[:-1], n)
+                or residual.device != values.device):
+            raise ValueError("NVFP4 residual differs from the declared output")
+        if gate is not None and (gate.dtype != torch.bfloat16 or gate.ndim != 2 or gate.shape[1] != n):
+            raise ValueError("NVFP4 gate must be bf16 [tokens, N]")
+        ep = Epilogue(kind=_lib.EPI_RESIDUAL, bias=bias, residual=residual.reshape(-1, n), gate=gate,
+                      tokens=0 if gate is None else gate.shape[0])
+        return self._run(values, weight, bias, ep)
+
+    def qkv_linear(self, values, weight: NVFP4Weight, bias=None, *, adapters=None, scalings=None):
+        """Merged QKV: the Q, K, V planes of one GEMM, optionally each merged with its LoRA branch.
+
+        ``adapters`` (three bf16 ``[..., N/3]`` tensors or None) and
+        ``scalings`` follow triton_strict_bf16_qkv_direct_merge
+        (h3_fused_ops.py:901-979): plane = bf16(plane + bf16(adapter * s)).
+        """
+        n = weight.out_features
+        if n % 96:
+            raise ValueError("merged NVFP4 QKV needs three planes of a multiple of 32 columns")
+        self._check_bias(values, bias, n)
+        flat = None
+        if adapters is not None:
+            if scalings is None or len(adapters) != 3 or len(scalings) != 3:
+                raise ValueError("QKV adapters need three branches and three scalings")
+            flat = tuple(None if a is None else a.reshape(-1, n // 3) for a in adapters)
+        ep = Epilogue(bias=bias, planes=3, adapters=flat, scalings=tuple(scalings or (0.0, 0.0, 0.0)))
+        return self._run(values, weight, bias, ep)

@@ -176,7 +176,8 @@ class FP8BlockRing:
     """
 
     def __init__(self, layout: BlockLayout, host_blocks: list[torch.Tensor], device: torch.device, *,
-                 group=None, resident: bool = False, resident_blocks: int = 0, slots: int = 2) -> None:
+                 group=None, resident: bool = False, resident_blocks: int = 0, slots: int = 2,
+                 profile: bool = False) -> None:
         import torch.distributed as dist
 
         self.layout = layout
@@ -210,13 +211,21 @@ class FP8BlockRing:
         self.done = [torch.cuda.Event() for _ in range(count)]
         self.loaded = [False] * count
         self.h2d_bytes = 0
+        # profile=True: CUDA events around each block's host copy and all-gather on the copy stream
+        self.profile = profile
+        self.marks: list[tuple[torch.cuda.Event, torch.cuda.Event, torch.cuda.Event]] = []
 
     def _fetch(self, index: int, slot: int) -> None:
         """Queue block ``index`` into ``slot`` on the copy stream (after the slot's last use)."""
         with torch.cuda.stream(self.copy_stream):
             self.copy_stream.wait_event(self.done[slot])
+            marks = None
+            if self.profile:
+                marks = tuple(torch.cuda.Event(enable_timing=True) for _ in range(3))
+                marks[0].record(self.copy_stream)
+                self.marks.append(marks)
             assemble_block(self.slots[slot], self.host_blocks[index], rank=self.rank, world=self.world,
-                           group=self.group)
+                           group=self.group, marks=marks)
             self.h2d_bytes += self.chunk
             self.ready[slot].record(self.copy_stream)
 
@@ -250,26 +259,51 @@ class FP8BlockRing:
                 self._fetch(i + depth, slot)
         return hidden
 
+    def copy_times(self) -> tuple[float, float, int]:
+        """Mean milliseconds per profiled block of the host copy and of the all-gather, and the block count.
+
+        Synchronises the copy stream; clears the recorded events.
+        """
+        self.copy_stream.synchronize()
+        h2d = [a.elapsed_time(b) for a, b, _ in self.marks]
+        gather = [b.elapsed_time(c) for _, b, c in self.marks]
+        count = len(self.marks)
+        self.marks = []
+        if not count:
+            return 0.0, 0.0, 0
+        return sum(h2d) / count, sum(gather) / count, count
+
 
 def assemble_block(dest: torch.Tensor, host_chunk: torch.Tensor, *, rank: int = 0, world: int = 1,
-                   group=None) -> None:
+                   group=None, marks=None) -> None:
     """Copy this rank's byte range of a packed block into ``dest``, then all-gather the rest.
 
     ``dest`` is the whole packed block on this rank's device; rank r's range
     is ``[r*chunk, (r+1)*chunk)``.  The all-gather is in place (the input is
     the output's own range), so it moves only the other ranks' bytes.
+    ``marks`` (three timing events, the first already recorded) get the end
+    of the host copy and the end of the all-gather recorded on the current
+    stream.
     """
     import torch.distributed as dist
 
     chunk = host_chunk.numel()
     if dest.numel() != chunk * world:
         raise ValueError("block chunk sizes differ from the destination")
+    stream = torch.cuda.current_stream(dest.device) if marks is not None else None
     if world == 1:
         dest.copy_(host_chunk, non_blocking=True)
+        if marks is not None:
+            marks[1].record(stream)
+            marks[2].record(stream)
         return
     mine = dest.narrow(0, rank * chunk, chunk)
     mine.copy_(host_chunk, non_blocking=True)
+    if marks is not None:
+        marks[1].record(stream)
     dist.all_gather_into_tensor(dest, mine, group=group)
+    if marks is not None:
+        marks[2].record(stream)
 
 
 def pin_blocks(layout: BlockLayout, blocks: Iterable[dict[str, FP8Weight]], arena: PinnedHostArena, *,
