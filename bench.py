@@ -292,9 +292,10 @@ def run_gpu(args) -> None:
     if not args.no_stack:
         stack = stack_config(args, device, rank, world, barrier, max_over_ranks)
 
-    library = None
+    library = same_shape = None
     if rank == 0 and not args.no_library_probe:
         library = library_fp8_probe(device)
+        same_shape = library_same_shape(device, flush, stream)
     other = None
     if rank == 0 and not args.no_other_configs:
         other = other_configs(device, flush, stream,
@@ -369,6 +370,8 @@ def run_gpu(args) -> None:
         line["stack_c4"] = stack
     if library is not None:
         line["library_fp8_tflops"] = library
+    if same_shape is not None:
+        line["library_same_shape"] = same_shape
     if other is not None:
         line["other_configs"] = other
     if cpu is not None:
@@ -799,6 +802,41 @@ def stack_config(args, device, rank: int, world: int, barrier, max_over_ranks) -
     }
 
 
+def library_same_shape(device, flush, stream) -> dict:
+    """The reference's W8A8 call at config 1's exact shape on this box: the per-token quantiser then
+    rowwise ``torch._scaled_mm`` (cuBLASLt) + bias (src/vflash/native/h3_fp8_linear.py:109-121), with the
+    quantiser's codes from this library (bit-identical to the reference's), median of 20 calls with L2
+    flushed before each."""
+    try:
+        from vflash_b200.kernels import quantize_fp8_rows
+
+        x_host, w_codes, w_scales, bias = synthetic_workload(device, 0, M)
+        x = x_host.to(device)
+        codes, scales = quantize_fp8_rows(x)
+
+        def gemm():
+            out = torch._scaled_mm(codes, w_codes.t(), scale_a=scales, scale_b=w_scales.t(),
+                                   out_dtype=torch.bfloat16)
+            out = out[0] if isinstance(out, tuple) else out
+            return out[:M] + bias
+
+        def step():
+            c, s = quantize_fp8_rows(x)
+            out = torch._scaled_mm(c, w_codes.t(), scale_a=s, scale_b=w_scales.t(), out_dtype=torch.bfloat16)
+            out = out[0] if isinstance(out, tuple) else out
+            return out[:M] + bias
+
+        flop = 2.0 * M * N_QKV * K
+        gemm_ms = statistics.median(_timed(gemm, flush, stream, reps=20, warmup=3))
+        step_ms = statistics.median(_timed(step, flush, stream, reps=20, warmup=3))
+        return {"gemm_plus_bias_ms": round(gemm_ms, 4),
+                "gemm_plus_bias_tflops": round(flop / (gemm_ms * 1e-3) / 1e12, 1),
+                "step_ms": round(step_ms, 4), "step_tflops": round(flop / (step_ms * 1e-3) / 1e12, 1),
+                "call": "rowwise torch._scaled_mm(codes, W.t(), scale_a [M,1], scale_b [1,N], bf16)[:M] + bias"}
+    except Exception as exc:  # pragma: no cover - diagnostic only
+        return {"error": str(exc)[:200]}
+
+
 def library_fp8_probe(device) -> dict:
     """cuBLASLt FP8 GEMM throughput (torch._scaled_mm, tensorwise) on this box, for context."""
     try:
@@ -920,7 +958,8 @@ def main() -> None:
     parser.add_argument("--warmup", type=int, default=5)
     parser.add_argument("--impl", choices=["vflash_b200", "reference"], default="vflash_b200")
     parser.add_argument("--cpu-seconds", type=float, default=10.0)
-    parser.add_argument("--reference-rows", type=int, default=1024)
+    parser.add_argument("--reference-rows", type=int, default=M,
+                        help="rows of X per reference step (default: all of config 1's 32760)")
     parser.add_argument("--no-cpu-baseline", action="store_true")
     parser.add_argument("--no-library-probe", action="store_true")
     parser.add_argument("--no-e2e", action="store_true")

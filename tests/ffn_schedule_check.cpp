@@ -2,7 +2,7 @@
 // shape given on the command line, every up and down tile appears exactly
 // once, and every down tile of a row block comes after all of that row
 // block's up tiles.  Prints "ok <items>" or the first violation.
-//   usage: ffn_schedule_check R ju jd group band_up band_down lead
+//   usage: ffn_schedule_check R ju jd group band_up band_down lead lag
 #include <cstdio>
 #include <cstdlib>
 #include <vector>
@@ -10,7 +10,7 @@
 #include "ffn_plan.h"
 
 int main(int argc, char **argv) {
-  if (argc != 8) return 2;
+  if (argc != 9) return 2;
   vfb::FfnPlan p{};
   p.rows_blocks = atoi(argv[1]);
   p.ju = atoi(argv[2]);
@@ -19,6 +19,7 @@ int main(int argc, char **argv) {
   p.band_up = atoi(argv[5]);
   p.band_down = atoi(argv[6]);
   p.lead = atoi(argv[7]);
+  p.lag = atoi(argv[8]);
   p.groups = (p.rows_blocks + p.group - 1) / p.group;
   p.total = p.rows_blocks * (p.ju + p.jd);
   std::vector<int> seen_up(static_cast<size_t>(p.rows_blocks) * p.ju, -1);

@@ -179,3 +179,19 @@ def test_ffn_workspace_and_argument_checks_before_any_launch():
     gate_alone = list(args)
     gate_alone[14], gate_alone[15], gate_alone[16] = ptr, 64, 1
     assert lib.vfb_fp8_ffn(*gate_alone) == _lib.VFB_EINVAL and "gate" in _lib.last_error()
+
+
+def test_noalloc_row_limit_at_the_h3_ffn_shape():
+    """vfb_fp8_ffn_noalloc's fixed 64 MiB array holds the intermediates of at most 1,382 rows at
+    the H3 FFN shape (hidden 5376, F 14336); one more row is refused before any device work."""
+    lib = _lib.load()
+    scratch = 64 << 20
+    assert lib.vfb_fp8_ffn_workspace_bytes(1382, 5376, 14336) <= scratch
+    assert lib.vfb_fp8_ffn_workspace_bytes(1383, 5376, 14336) > scratch
+    rc = lib.vfb_fp8_ffn_noalloc(None, 1383, 5376, 5376, None, None, 14336, None, None, _lib.EPI_GELU_TANH, None,
+                                 None, None, 0, None, 0, 0, None, 5376, None)
+    assert rc == _lib.VFB_EINVAL and "scratch" in _lib.last_error()
+    # a wrong activation is reported as such, before the size check
+    rc = lib.vfb_fp8_ffn_noalloc(None, 1383, 5376, 5376, None, None, 14336, None, None, _lib.EPI_RESIDUAL, None,
+                                 None, None, 0, None, 0, 0, None, 5376, None)
+    assert rc == _lib.VFB_EINVAL and "activation" in _lib.last_error()

@@ -29,7 +29,7 @@ def checker(tmp_path_factory):
     return exe
 
 
-CASES = [
+BASE = [
     # R, ju, jd, group, band_up, band_down, lead
     (128, 64, 16, 4, 12, 3, 148),    # config 2 GELU: M = 32760, F = 16384, H = 4096
     (128, 128, 16, 4, 12, 3, 148),   # config 2 SwiGLU (128 value + 128 gate columns per up tile)
@@ -40,6 +40,8 @@ CASES = [
     (10, 3, 5, 2, 8, 8, 1),          # bands wider than the grid
     (17, 4, 4, 1, 1, 1, 2),          # groups of one row block
 ]
+# every case with the down tiles one, two and three groups behind their up tiles
+CASES = [(*c, lag) for c in BASE for lag in (1, 2, 3)]
 
 
 @pytest.mark.parametrize("case", CASES, ids=[str(c) for c in CASES])

@@ -79,9 +79,18 @@ __device__ __forceinline__ void load_bf16x32(const __nv_bfloat16 *p, float (&r)[
 // uses (conflict-free 16-byte stores), then lane 0 issues one TMA store.
 // Each warp cycles through EPI_BOXES staging boxes; a box is rewritten only
 // after the store issued from it EPI_BOXES chunks earlier has read it.
+// Exact packing of two bf16-representable floats (their low 16 bits are zero).
+__device__ __forceinline__ uint32_t pack_exact_bf16x2(float lo, float hi) {
+  return __byte_perm(__float_as_uint(lo), __float_as_uint(hi), 0x7632);
+}
+
+
 // KEEP = true stores with an evict_last L2 policy (data this kernel reads back
 // soon, e.g. the FFN intermediate); otherwise evict_first (final outputs).
-template <int BOXES, bool KEEP = false>
+// ROUNDED = true: every y is already a bf16 value, so the halves are packed by
+// a byte permute instead of a conversion (the conversion pipe is the busiest
+// unit of the activation epilogues).
+template <int BOXES, bool KEEP = false, bool ROUNDED = false>
 __device__ __forceinline__ void store_box(uint8_t *warp_smem, int &box, const CUtensorMap *map,
                                           const float (&y)[32], int lane, int32_t col, int32_t row0,
                                           int32_t plane, bool any_row) {
@@ -93,10 +102,17 @@ __device__ __forceinline__ void store_box(uint8_t *warp_smem, int &box, const CU
 #pragma unroll
   for (int j = 0; j < 4; ++j) {
     uint4 t;
-    t.x = pack_bf16x2(y[8 * j + 0], y[8 * j + 1]);
-    t.y = pack_bf16x2(y[8 * j + 2], y[8 * j + 3]);
-    t.z = pack_bf16x2(y[8 * j + 4], y[8 * j + 5]);
-    t.w = pack_bf16x2(y[8 * j + 6], y[8 * j + 7]);
+    if constexpr (ROUNDED) {
+      t.x = pack_exact_bf16x2(y[8 * j + 0], y[8 * j + 1]);
+      t.y = pack_exact_bf16x2(y[8 * j + 2], y[8 * j + 3]);
+      t.z = pack_exact_bf16x2(y[8 * j + 4], y[8 * j + 5]);
+      t.w = pack_exact_bf16x2(y[8 * j + 6], y[8 * j + 7]);
+    } else {
+      t.x = pack_bf16x2(y[8 * j + 0], y[8 * j + 1]);
+      t.y = pack_bf16x2(y[8 * j + 2], y[8 * j + 3]);
+      t.z = pack_bf16x2(y[8 * j + 4], y[8 * j + 5]);
+      t.w = pack_bf16x2(y[8 * j + 6], y[8 * j + 7]);
+    }
     row[j ^ sw] = t;
   }
   fence_proxy_async_smem();

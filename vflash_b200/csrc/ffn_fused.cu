@@ -60,8 +60,15 @@ constexpr int TMEM_COLS = 512;
 constexpr int BOXES = 2;         // staging boxes per epilogue warp
 constexpr int EPI_SMEM = EPI_WARPS * BOXES * EPI_BOX_BYTES;
 constexpr int RING = 8;          // published work items in flight
-constexpr int PENDING = 16;      // stored regions awaiting conversion, per epilogue warp
-constexpr size_t SMEM_BYTES = 1024 + STAGES * (A_STAGE + B_STAGE) + EPI_SMEM + 512;
+// Stored regions awaiting conversion, per epilogue warp, kept in shared memory.
+// A warp holds one entry per up tile from the first tile of a row block until
+// that row block is complete; the FIFO must never fill in practice, because a
+// full FIFO makes the warp wait for its oldest row block, whose last up tile
+// may be queued behind this very warp (the wait is bounded, not a hang, but
+// it costs the time limit).  64 entries cover many groups of row blocks.
+constexpr int PENDING = 64;
+constexpr int PENDING_SMEM = EPI_WARPS * PENDING * 4;
+constexpr size_t SMEM_BYTES = 1024 + STAGES * (A_STAGE + B_STAGE) + EPI_SMEM + PENDING_SMEM + 512;
 
 struct FfnParams {
   int64_t M, H, F;
@@ -113,12 +120,16 @@ __device__ __forceinline__ uint32_t abs_bits_max32(const float (&v)[32], uint32_
 }
 
 // Per epilogue warp: the regions it stored whose row blocks were not complete
-// yet, in the order stored (row blocks complete in about that order).
+// yet, in the order stored (row blocks complete in about that order).  The
+// entries (row block << 9 | tile; a row block has at most 256 up tiles) live
+// in shared memory; head and count are warp-uniform registers, and lane 0
+// writes the entries.
 struct Pending {
-  int r[PENDING];
-  int t[PENDING];
+  uint32_t *entry;  // PENDING entries of this warp
   int head = 0;
   int count = 0;
+  __device__ __forceinline__ int r() const { return static_cast<int>(entry[head] >> 9); }
+  __device__ __forceinline__ int t() const { return static_cast<int>(entry[head] & 0x1ffu); }
 };
 
 template <int ACT>
@@ -186,7 +197,7 @@ struct Ffn {
 
   static __device__ __forceinline__ bool front_ready(const FfnParams &p, const Pending &pend, int lane) {
     int ready = 0;
-    if (lane == 0) ready = ld_acquire_gpu(p.up_done + pend.r[pend.head]) >= p.done_target;
+    if (lane == 0) ready = ld_acquire_gpu(p.up_done + pend.r()) >= p.done_target;
     ready = __shfl_sync(0xffffffffu, ready, 0);
     __syncwarp();
     return ready != 0;
@@ -194,7 +205,7 @@ struct Ffn {
 
   static __device__ __forceinline__ void pop_convert(const FfnParams &p, Pending &pend, int rank, int quarter,
                                                      int group, int lane) {
-    convert(p, pend.r[pend.head], pend.t[pend.head], rank, quarter, group, lane);
+    convert(p, pend.r(), pend.t(), rank, quarter, group, lane);
     pend.head = (pend.head + 1) % PENDING;
     --pend.count;
   }
@@ -209,7 +220,7 @@ struct Ffn {
   static __device__ bool convert_oldest(const FfnParams &p, Pending &pend, int rank, int quarter, int group,
                                         int lane, volatile int *abort_flag) {
     bool ok = true;
-    if (lane == 0) ok = wait_flag(p.up_done + pend.r[pend.head], p.done_target, abort_flag, p.status);
+    if (lane == 0) ok = wait_flag(p.up_done + pend.r(), p.done_target, abort_flag, p.status);
     ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
     __syncwarp();
     if (!ok) return false;
@@ -218,10 +229,8 @@ struct Ffn {
   }
 
   // Waits (bounded) for an mbarrier phase; while it is not complete, converts
-  // pending regions whose row blocks are done.  The row-block counters are
-  // polled only every 16th spin: every epilogue warp of the grid waits here
-  // during the long down tiles, and an acquire load per spin from each of
-  // them would load L2 for nothing.
+  // pending regions whose row blocks are done (the row-block counter is
+  // polled every 4th spin).
   static __device__ bool wait_converting(uint64_t *bar, uint32_t parity, bool cluster_acquire,
                                          const FfnParams &p, Pending &pend, int rank, int quarter, int group,
                                          int lane, volatile int *abort_flag) {
@@ -234,7 +243,7 @@ struct Ffn {
                                         : mbar_wait(bar, parity, abort_flag, p.status);
         return __all_sync(0xffffffffu, ok);
       }
-      if ((spin & 15u) == 0 && pend.count > 0 && front_ready(p, pend, lane)) {
+      if ((spin & 3u) == 0 && pend.count > 0 && front_ready(p, pend, lane)) {
         pop_convert(p, pend, rank, quarter, group, lane);
         continue;
       }
@@ -268,7 +277,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   uint8_t *sA = smem;
   uint8_t *sB = smem + STAGES * A_STAGE;
   uint8_t *sEpi = sB + STAGES * B_STAGE;
-  uint64_t *full_bar = reinterpret_cast<uint64_t *>(sEpi + EPI_SMEM);
+  uint64_t *full_bar = reinterpret_cast<uint64_t *>(sEpi + EPI_SMEM + PENDING_SMEM);
   uint64_t *empty_bar = full_bar + STAGES;
   uint64_t *tfull_bar = empty_bar + STAGES;
   uint64_t *tempty_bar = tfull_bar + 2;
@@ -467,6 +476,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     uint8_t *warp_smem = sEpi + ew * BOXES * EPI_BOX_BYTES;
     const uint32_t tempty_leader = map_to_rank(smem_u32(&tempty_bar[0]), 0);
     Pending pend;
+    pend.entry = reinterpret_cast<uint32_t *>(sEpi + EPI_SMEM) + ew * PENDING;
     int box = 0;
     int t = 0;
     for (int i = 0;; ++i) {
@@ -517,7 +527,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 #pragma unroll
               for (int j = 0; j < 32; ++j) v[j] = 0.0f;
             }
-            store_box<BOXES, true>(warp_smem, box, &tmMid, v, lane, static_cast<int32_t>(f),
+            store_box<BOXES, true, true>(warp_smem, box, &tmMid, v, lane, static_cast<int32_t>(f),
                                    static_cast<int32_t>(row0), 0, any_row);
           }
         } else {
@@ -537,7 +547,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 #pragma unroll
               for (int j = 0; j < 32; ++j) v[j] = 0.0f;
             }
-            store_box<BOXES, true>(warp_smem, box, &tmMid, v, lane, static_cast<int32_t>(n),
+            store_box<BOXES, true, true>(warp_smem, box, &tmMid, v, lane, static_cast<int32_t>(n),
                                    static_cast<int32_t>(row0), 0, any_row);
           }
         }
@@ -549,9 +559,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         __syncwarp();
         if (lane == 0) red_release_gpu_add(p.up_done + r, 1);
         if (pend.count == PENDING && !F::convert_oldest(p, pend, rank, quarter, group, lane, abort_flag)) break;
-        const int back = (pend.head + pend.count) % PENDING;
-        pend.r[back] = r;
-        pend.t[back] = tt;
+        if (lane == 0) pend.entry[(pend.head + pend.count) % PENDING] = (static_cast<uint32_t>(r) << 9) | tt;
+        __syncwarp();
         ++pend.count;
       } else {
         // the row block's maxima are final (its conversions are published)
@@ -643,6 +652,7 @@ int launch_ffn_fused(const FfnFusedArgs &a, void *stream) {
   pl.band_down = a.band_down > 0 ? a.band_down : band_width(pl.jd, 2 * a.F);
   const int pairs_max = sm_count / 2;
   pl.lead = a.lead >= 0 ? a.lead : 2 * pairs_max;
+  pl.lag = a.lag > 0 ? a.lag : 1;
   pl.total = pl.rows_blocks * (pl.ju + pl.jd);
   p.done_target = pl.ju * 2 * EPI_WARPS;
   p.x_scales = a.x_scales;

@@ -34,6 +34,7 @@ struct FfnFusedArgs {
   int band_up;
   int band_down;
   int lead;
+  int lag;
 };
 
 // Whether the fused kernel handles these widths (GELU: F % 256 == 0; SwiGLU: F % 128 == 0; H % 32 == 0).

@@ -16,10 +16,11 @@
 //     inside a band, tile fastest), so one band of the up weight serves the
 //     whole group from L2;
 //   * the down tiles of group g, in bands of `band_down`, are interleaved
-//     with the up tiles of group g + 1 after a lead of `lead` up items, which
-//     gives the last up tiles of group g time to finish and convert.  The mix
-//     also balances the up tiles' heavy epilogues (activation, row maxima,
-//     conversion) against the down tiles' long main loops.
+//     with the up tiles of group g + `lag` after a lead of `lead` up items;
+//     the lag and the lead give the last up tiles of group g time to finish
+//     and convert before its down tiles are taken.  The mix balances the up
+//     tiles' heavy epilogues (activation, row maxima, conversion) against the
+//     down tiles' long main loops.
 #pragma once
 
 #include <stdint.h>
@@ -40,7 +41,8 @@ struct FfnPlan {
   int groups;       // ceil(R / group)
   int band_up;      // up weight tiles per band
   int band_down;    // down weight tiles per band
-  int lead;         // up items of group g + 1 before the first down item of group g
+  int lead;         // up items of group g + lag before the first down item of group g
+  int lag;          // groups between a group's up tiles and its down tiles (>= 1)
   int total;        // R * (ju + jd)
 };
 
@@ -60,7 +62,7 @@ VFB_HD void ffn_band_coords(int i, int rows, int cols, int band, int &row, int &
 
 VFB_HD int ffn_group_rows(const FfnPlan &p, int g) { return ffn_min(p.group, p.rows_blocks - g * p.group); }
 
-// Item `s` of the merge of up(g + 1) (n_up items) with down(g) (n_down items).
+// Item `s` of the merge of up(g + lag) (n_up items) with down(g) (n_down items).
 VFB_HD void ffn_merge_item(const FfnPlan &p, int g, int s, int n_up, int n_down, int &kind, int &r, int &t) {
   const int lead = ffn_min(p.lead, n_up);
   int up_index = -1, down_index = -1;
@@ -84,11 +86,11 @@ VFB_HD void ffn_merge_item(const FfnPlan &p, int g, int s, int n_up, int n_down,
     }
   }
   if (up_index >= 0) {
-    const int gr = ffn_group_rows(p, g + 1);
+    const int gr = ffn_group_rows(p, g + p.lag);
     int row, col;
     ffn_band_coords(up_index, gr, p.ju, p.band_up, row, col);
     kind = kFfnUp;
-    r = (g + 1) * p.group + row;
+    r = (g + p.lag) * p.group + row;
     t = col;
   } else {
     const int gr = ffn_group_rows(p, g);
@@ -102,20 +104,24 @@ VFB_HD void ffn_merge_item(const FfnPlan &p, int g, int s, int n_up, int n_down,
 
 // Decodes work item q (0 <= q < total) into its kind, row block and tile.
 VFB_HD void ffn_item(const FfnPlan &p, int q, int &kind, int &r, int &t) {
-  const int n_up0 = ffn_group_rows(p, 0) * p.ju;
-  if (q < n_up0) {
-    int row, col;
-    ffn_band_coords(q, ffn_group_rows(p, 0), p.ju, p.band_up, row, col);
-    kind = kFfnUp;
-    r = row;
-    t = col;
-    return;
+  int s = q;
+  // the up tiles of the first `lag` groups come first
+  for (int g0 = 0; g0 < p.lag && g0 < p.groups; ++g0) {
+    const int gr = ffn_group_rows(p, g0);
+    if (s < gr * p.ju) {
+      int row, col;
+      ffn_band_coords(s, gr, p.ju, p.band_up, row, col);
+      kind = kFfnUp;
+      r = g0 * p.group + row;
+      t = col;
+      return;
+    }
+    s -= gr * p.ju;
   }
-  int s = q - n_up0;
   int g = 0;
-  // merges 0 .. groups - 3 all hold a full group of up items and of down items
-  if (p.groups >= 3) {
-    const int full = p.groups - 2;
+  // merges 0 .. groups - lag - 2 hold a full group of up items and of down items
+  const int full = p.groups - p.lag - 1;
+  if (full > 0) {
     const int size = p.group * (p.ju + p.jd);
     if (s < full * size) {
       g = s / size;
@@ -126,7 +132,7 @@ VFB_HD void ffn_item(const FfnPlan &p, int q, int &kind, int &r, int &t) {
     g = full;
   }
   for (; g < p.groups; ++g) {
-    const int n_up = g + 1 < p.groups ? ffn_group_rows(p, g + 1) * p.ju : 0;
+    const int n_up = g + p.lag < p.groups ? ffn_group_rows(p, g + p.lag) * p.ju : 0;
     const int n_down = ffn_group_rows(p, g) * p.jd;
     if (s < n_up + n_down) {
       ffn_merge_item(p, g, s, n_up, n_down, kind, r, t);

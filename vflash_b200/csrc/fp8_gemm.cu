@@ -153,6 +153,7 @@ __device__ __forceinline__ void store_value(float (&v)[32], float sa, const floa
     bf16r_x32(a);
 #pragma unroll
     for (int j = 0; j < 32; ++j) v[j] = v[j] + a[j];
+    bf16r_x32(v);  // the merge's own rounding (the store then packs exact bf16 values)
   }
 }
 
@@ -161,10 +162,6 @@ __device__ __forceinline__ uint2 ld4(const __nv_bfloat16 *p) { return __ldg(rein
 
 __device__ __forceinline__ __nv_bfloat162 as_bf162(uint32_t u) { return *reinterpret_cast<__nv_bfloat162 *>(&u); }
 
-// Exact packing of two bf16-representable floats (their low 16 bits are zero).
-__device__ __forceinline__ uint32_t pack_exact_bf16x2(float lo, float hi) {
-  return __byte_perm(__float_as_uint(lo), __float_as_uint(hi), 0x7632);
-}
 
 // QK-norm + rotary output of one 32-column chunk of a head (k in 0..3) from
 // the head's 128 bf16 values packed in hp[64] (hp[i] = columns 2i, 2i+1):
@@ -407,7 +404,8 @@ __global__ void __launch_bounds__(num_threads<EPI, OPS>(), 1)
               }
               int32_t oc, op;
               out_coord(ep, plane, col0 + 32 * k, oc, op);
-              store_box<kBoxes>(warp_smem, box, &tmOut, v, lane, oc, static_cast<int32_t>(row0), op, any_row);
+              store_box<kBoxes, false, true>(warp_smem, box, &tmOut, v, lane, oc, static_cast<int32_t>(row0), op,
+                                             any_row);
             }
         } else {
           // pass 1: this thread's row of the head (bf16 values, packed), sum of squares in fp32
@@ -508,7 +506,9 @@ __global__ void __launch_bounds__(num_threads<EPI, OPS>(), 1)
           }
           int32_t oc, op;
           out_coord(ep, plane, col, oc, op);
-          store_box<kBoxes>(warp_smem, box, &tmOut, v, lane, oc, static_cast<int32_t>(row0), op, any_row);
+          // STORE values are bf16 already (scale_bias / the merge rounded them)
+          store_box<kBoxes, false, EPI == VFB_EPI_STORE>(warp_smem, box, &tmOut, v, lane, oc,
+                                                         static_cast<int32_t>(row0), op, any_row);
         }
       }
       tc_fence_before();
