@@ -596,9 +596,11 @@ def other_configs(device, flush, stream, cpu_seconds: float = 0.0) -> dict:
                 "QKV epilogue; vs planar QKV then per branch cuBLAS linear(linear(x, down), up) * s + add"}
     del xq, wq, wqs, rc, rs, ang, residuals
 
-    # c2: fused FFN, GELU-tanh, per-token requant of the intermediate, residual:
-    # the one-kernel FFN (vfb_fp8_ffn: quantiser + fused up/requant/down launch)
-    # and, for comparison, the same chain as four separate launches
+    # c2: FFN, GELU-tanh, per-token requant of the intermediate, residual:
+    # vfb_fp8_ffn (quantiser, up GEMM + GELU, requantiser, down GEMM + residual;
+    # per-launch times from the same chain issued step by step) and, for
+    # comparison, vfb_fp8_ffn_one_kernel (the three steps after the quantiser
+    # in one persistent launch)
     from vflash_b200.kernels import fp8_ffn
 
     m, h, f = 32760, 4096, 16384
@@ -608,8 +610,11 @@ def other_configs(device, flush, stream, cpu_seconds: float = 0.0) -> dict:
     ev = [torch.cuda.Event(enable_timing=True) for _ in range(5)]
     ffn_flop = 2.0 * m * f * h * 2
 
-    def c2_fused():
+    def c2_ffn():
         fp8_ffn(x, up, ups, down, downs, activation=_lib.EPI_GELU_TANH, residual=x)
+
+    def c2_one_kernel():
+        fp8_ffn(x, up, ups, down, downs, activation=_lib.EPI_GELU_TANH, residual=x, one_kernel=True)
 
     def c2_chain():
         ev[0].record(stream)
@@ -622,19 +627,24 @@ def other_configs(device, flush, stream, cpu_seconds: float = 0.0) -> dict:
         fp8_gemm(mc, ms_, m, down, downs, Epilogue(kind=_lib.EPI_RESIDUAL, residual=x))
         ev[4].record(stream)
 
-    fused_ms = _timed(c2_fused, flush, stream)
-    chain_ms = statistics.median(_timed(c2_chain, flush, stream))
+    ffn_ms = _timed(c2_ffn, flush, stream)
+    one_kernel_ms = statistics.median(_timed(c2_one_kernel, flush, stream))
+    _timed(c2_chain, flush, stream, reps=10, warmup=3)
     parts = [ev[i].elapsed_time(ev[i + 1]) for i in range(4)]
-    same = bool(torch.equal(fp8_ffn(x, up, ups, down, downs, activation=_lib.EPI_GELU_TANH, residual=x),
-                            _chain_output(x, up, ups, down, downs, m)))
+    chain = _chain_output(x, up, ups, down, downs, m)
+    same = bool(torch.equal(fp8_ffn(x, up, ups, down, downs, activation=_lib.EPI_GELU_TANH, residual=x), chain)
+                and torch.equal(fp8_ffn(x, up, ups, down, downs, activation=_lib.EPI_GELU_TANH, residual=x,
+                                        one_kernel=True), chain))
+    del chain
     out["c2_fp8_ffn_gelu"] = summary(
-        fused_ms, ffn_flop, fp8_peak,
-        {"step": "vfb_fp8_ffn: quant X, then ONE kernel: up GEMM + GELU-tanh epilogue, per-token requant of "
-                 "the bf16 intermediate in L2, down GEMM + residual epilogue",
-         "four_launch_chain_ms": round(chain_ms, 4),
-         "four_launch_last_step_ms": {"quant_x": round(parts[0], 4), "up_gemm_gelu": round(parts[1], 4),
-                                      "requant_mid": round(parts[2], 4), "down_gemm_residual": round(parts[3], 4)},
-         "equals_four_launch_chain": same})
+        ffn_ms, ffn_flop, fp8_peak,
+        {"step": "vfb_fp8_ffn: quant X, up GEMM + GELU-tanh epilogue, per-token requant of the bf16 "
+                 "intermediate, down GEMM + residual epilogue (one C call, four launches)",
+         "last_step_ms": {"quant_x": round(parts[0], 4), "up_gemm_gelu": round(parts[1], 4),
+                          "requant_mid": round(parts[2], 4), "down_gemm_residual": round(parts[3], 4)},
+         "one_kernel_ms": round(one_kernel_ms, 4),
+         "one_kernel_tflops": round(ffn_flop / (one_kernel_ms * 1e-3) / 1e12, 1),
+         "equal_bits": same})
     del up, ups
 
     # c2 SwiGLU variant (the reference model's packed FFN input [2F, H]) through
@@ -650,8 +660,8 @@ def other_configs(device, flush, stream, cpu_seconds: float = 0.0) -> dict:
     ms = _timed(c2_swiglu, flush, stream)
     out["c2_fp8_ffn_swiglu"] = summary(
         ms, 2.0 * m * (2 * f) * h + 2.0 * m * f * h, fp8_peak,
-        {"step": "RowFP8Execution.ffn(activation='swiglu'): quant X, then one kernel: packed up GEMM [2F,H] "
-                 "with value * bf16(silu(gate)), requant in L2, down GEMM + residual"})
+        {"step": "RowFP8Execution.ffn(activation='swiglu'): quant X, packed up GEMM [2F,H] with "
+                 "value * bf16(silu(gate)), requant, down GEMM + residual"})
     del x, packed, packeds, down, downs
 
     # c3: NVFP4 linear, M = 32760, K = 4096, N in {4096, 16384}

@@ -225,17 +225,36 @@ VFB_API int vfb_bf16_gemm(const void *A, int64_t lda, const void *W, int64_t ldw
  *   -> down GEMM (w_down [H, F]; bias_down; RESIDUAL with residual [M, H]
  *      (row stride ldr) and optional gate [tokens, H] (row stride
  *      gate_token_stride), else STORE) into out [M, H] (row stride ldo).
- * The same bits as vfb_fp8_gemm / vfb_fp8_quant_rows called step by step.
- * When F % 256 == 0 (GELU) or F % 128 == 0 (SwiGLU) the three steps after
- * the input quantiser are one persistent kernel whose bf16 intermediate is
- * requantised in place in L2 and never round-trips HBM; other widths run
- * the three launches.  x: bf16 [M, H], row stride ldx; s_up [n_up], s_down
+ * The same bits as vfb_fp8_gemm / vfb_fp8_quant_rows called step by step,
+ * which is how it runs: three launches after the input quantiser, the
+ * fastest order measured on the B200 at the benchmark's size (see
+ * vfb_fp8_ffn_one_kernel).  x: bf16 [M, H], row stride ldx; s_up [n_up], s_down
  * [H] fp32.  H and F multiples of 32, at most 32768.  The intermediates live
  * in `workspace` (256-byte aligned, at least vfb_fp8_ffn_workspace_bytes(M,
  * H, F) bytes, F = intermediate width); the call allocates nothing.
  * vfb_fp8_ffn_workspace_bytes returns -1 for an invalid shape. */
 VFB_API int64_t vfb_fp8_ffn_workspace_bytes(int64_t M, int64_t H, int64_t F);
 VFB_API int vfb_fp8_ffn(const void *x, int64_t M, int64_t H, int64_t ldx,
+                const void *w_up, const float *s_up, int64_t n_up,
+                const void *w_down, const float *s_down, int32_t activation,
+                const void *bias_up, const void *bias_down,
+                const void *residual, int64_t ldr,
+                const void *gate, int64_t gate_token_stride, int64_t tokens,
+                void *out, int64_t ldo, void *workspace, int64_t workspace_bytes, void *stream);
+
+/* vfb_fp8_ffn with the up GEMM, the requantisation and the down GEMM in ONE
+ * persistent kernel (same arguments, same bits), for F % 256 == 0 (GELU) or
+ * F % 128 == 0 (SwiGLU); other widths run the three launches.  No reference
+ * counterpart: the reference runs the FFN's linears and its quantiser as
+ * separate launches.  CTA pairs take up and down tiles from one counter in
+ * row-block groups; each up tile's epilogue stores its bf16 tile (L2
+ * evict_last) and merges its rows' maxima, and once a row block's up tiles
+ * are all done the warps that stored it requantise it to e4m3 and drop the
+ * bf16 lines from L2; the row block's down tiles then read the codes.  The
+ * bf16 intermediate stays in L2 only while a group's intermediate fits next
+ * to the weight tiles in use: at the benchmark's FFN (M 32760, H 4096,
+ * F 16384) it does not, and this path is slower than vfb_fp8_ffn. */
+VFB_API int vfb_fp8_ffn_one_kernel(const void *x, int64_t M, int64_t H, int64_t ldx,
                 const void *w_up, const float *s_up, int64_t n_up,
                 const void *w_down, const float *s_down, int32_t activation,
                 const void *bias_up, const void *bias_down,

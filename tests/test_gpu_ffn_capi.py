@@ -1,14 +1,16 @@
-"""The fused FP8 FFN (vfb_fp8_ffn, RowFP8Execution.ffn) equals the step-by-step composition bit for bit.
+"""The FP8 FFN entry points equal the step-by-step composition bit for bit.
 
 The composition is the chain the reference runs for the block's FFN, each
 step through this library's own separately tested entry points: the
 per-token quantiser, the up GEMM with the activation epilogue (GELU-tanh or
 SwiGLU), the quantiser again on the bf16 intermediate, and the down GEMM
-with bias / gated residual.  The fused kernel (one launch; the intermediate
-is requantised in L2) must give the same bits: the same MMA tiles in the same
-K order, the same epilogue arithmetic and the same quotient per code.  Shapes
-cover several row-block groups of its schedule, ragged rows, partial down
-tiles, and widths the fused kernel does not tile (the three-launch path).
+with bias / gated residual.  vfb_fp8_ffn (RowFP8Execution.ffn) sequences
+those launches in one call; vfb_fp8_ffn_one_kernel runs the up GEMM, the
+requantisation and the down GEMM as one persistent kernel and must give the
+same bits: the same MMA tiles in the same K order, the same epilogue
+arithmetic and the same quotient per code.  Shapes cover several row-block
+groups of its schedule, ragged rows, partial down tiles, and widths the
+one-kernel path does not tile (it then runs the launches).
 """
 
 from __future__ import annotations
@@ -65,20 +67,22 @@ SHAPES = [
 @pytest.mark.parametrize("rows,hidden,width", SHAPES)
 @pytest.mark.parametrize("activation", ["gelu_tanh", "swiglu"])
 @pytest.mark.parametrize("with_residual", [False, True])
-def test_fused_ffn_equals_step_by_step_composition(rows, hidden, width, activation, with_residual):
+def test_ffn_entry_points_equal_step_by_step_composition(rows, hidden, width, activation, with_residual):
     c = case(rows, hidden, width, activation, with_residual)
     kind = _lib.EPI_SWIGLU if activation == "swiglu" else _lib.EPI_GELU_TANH
     codes, scales = quantize_fp8_rows(c["x"])
     want = composition(codes, scales, rows, c["up"], c["up_s"], c["down"], c["down_s"], kind, c["up_bias"],
                        c["down_bias"], c["residual"], c["gate"])
-    got = fp8_ffn(c["x"], c["up"], c["up_s"], c["down"], c["down_s"], activation=kind, up_bias=c["up_bias"],
-                  down_bias=c["down_bias"], residual=c["residual"], gate=c["gate"])
-    assert torch.equal(got, want)
-    ex = RowFP8Execution("w8a8")
-    via_api = ex.ffn(c["x"], c["up"], c["up_s"], c["down"], c["down_s"], activation=activation,
-                     up_bias=c["up_bias"], down_bias=c["down_bias"], residual=c["residual"], gate=c["gate"])
-    assert torch.equal(via_api, want)
-    assert ex.calls["w8a8"] == 2
+    for one_kernel in (False, True):
+        got = fp8_ffn(c["x"], c["up"], c["up_s"], c["down"], c["down_s"], activation=kind, up_bias=c["up_bias"],
+                      down_bias=c["down_bias"], residual=c["residual"], gate=c["gate"], one_kernel=one_kernel)
+        assert torch.equal(got, want), f"one_kernel={one_kernel}"
+        ex = RowFP8Execution("w8a8")
+        via_api = ex.ffn(c["x"], c["up"], c["up_s"], c["down"], c["down_s"], activation=activation,
+                         up_bias=c["up_bias"], down_bias=c["down_bias"], residual=c["residual"], gate=c["gate"],
+                         one_kernel=one_kernel)
+        assert torch.equal(via_api, want), f"one_kernel={one_kernel}"
+        assert ex.calls["w8a8"] == 2
     assert _lib.device_status(clear=True) == _lib.VFB_OK
 
 
@@ -99,12 +103,13 @@ def test_fused_ffn_after_the_norm_modulate_prologue(activation):
     assert torch.equal(got, want)
 
 
-def test_fused_ffn_repeats_bit_for_bit():
-    """The work order is dynamic (pairs take items from a counter); the results are not."""
+def test_one_kernel_ffn_repeats_bit_for_bit():
+    """The one-kernel path's work order is dynamic (pairs take items from a counter); the results are not."""
     c = case(3000, 512, 2048, "gelu_tanh", with_residual=True, seed=50)
-    runs = [fp8_ffn(c["x"], c["up"], c["up_s"], c["down"], c["down_s"], residual=c["residual"])
+    runs = [fp8_ffn(c["x"], c["up"], c["up_s"], c["down"], c["down_s"], residual=c["residual"], one_kernel=True)
             for _ in range(3)]
     assert torch.equal(runs[0], runs[1]) and torch.equal(runs[0], runs[2])
+    assert _lib.device_status(clear=True) == _lib.VFB_OK
 
 
 def test_c_entry_rejects_a_short_workspace():

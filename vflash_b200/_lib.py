@@ -93,6 +93,11 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         [_vp, _c_int64, _c_int64, _c_int64, _vp, _vp, _c_int64, _vp, _vp, ctypes.c_int32, _vp, _vp, _vp,
          _c_int64, _vp, _c_int64, _c_int64, _vp, _c_int64, _vp, _c_int64, _vp],
     ),
+    "vfb_fp8_ffn_one_kernel": (
+        ctypes.c_int,
+        [_vp, _c_int64, _c_int64, _c_int64, _vp, _vp, _c_int64, _vp, _vp, ctypes.c_int32, _vp, _vp, _vp,
+         _c_int64, _vp, _c_int64, _c_int64, _vp, _c_int64, _vp, _c_int64, _vp],
+    ),
     "vfb_fp8_ffn_quantized": (
         ctypes.c_int,
         [_vp, _vp, _c_int64, _c_int64, _vp, _vp, _c_int64, _vp, _vp, ctypes.c_int32, _vp, _vp, _vp,

@@ -1,13 +1,15 @@
-// The fused FP8 FFN as C entry points: per-token quantiser (vfb_fp8_ffn only),
-// then up GEMM + activation, per-token requantisation of the bf16
-// intermediate and down GEMM + bias / gated residual.
+// The fused FP8 FFN as C entry points: per-token quantiser (except
+// vfb_fp8_ffn_quantized), then up GEMM + activation, per-token requantisation
+// of the bf16 intermediate and down GEMM + bias / gated residual.
 //
-// When the intermediate width tiles the fused kernel (GELU: F % 256 == 0,
-// SwiGLU: F % 128 == 0) those three steps are ONE launch (ffn_fused.cu) whose
-// intermediate stays in L2; otherwise they are the three launches
-// RowFP8Execution.ffn used to issue (up GEMM with the activation epilogue,
-// vfb_fp8_quant_rows, down GEMM), with the same bits.  Intermediates live in a
-// caller-owned workspace (vfb_fp8_ffn_workspace_bytes): nothing is allocated.
+// vfb_fp8_ffn runs those three steps as three launches (up GEMM with the
+// activation epilogue, vfb_fp8_quant_rows, down GEMM with the residual
+// epilogue), the fastest order measured on the B200 at the benchmark's size.
+// vfb_fp8_ffn_one_kernel runs them as ONE persistent launch (ffn_fused.cu)
+// that requantises the intermediate in place, when the width tiles it (GELU:
+// F % 256 == 0, SwiGLU: F % 128 == 0).  Both give the same bits.
+// Intermediates live in a caller-owned workspace (vfb_fp8_ffn_workspace_bytes):
+// nothing is allocated.
 #include <cstdint>
 
 #include "common.cuh"
@@ -65,8 +67,8 @@ int ffn_body(const char *fn, const void *xc, const float *xs, int64_t M, int64_t
              const float *s_up, int64_t n_up, const void *w_down, const float *s_down, int32_t activation,
              const void *bias_up, const void *bias_down, const void *residual, int64_t ldr, const void *gate,
              int64_t gate_token_stride, int64_t tokens, void *out, int64_t ldo, uint8_t *ws,
-             const FfnWorkspace &lay, int64_t F, void *stream) {
-  if (ffn_fused_supported(activation, H, F)) {
+             const FfnWorkspace &lay, int64_t F, bool one_kernel, void *stream) {
+  if (one_kernel && ffn_fused_supported(activation, H, F)) {
     FfnFusedArgs a{};
     a.M = M;
     a.H = H;
@@ -162,19 +164,21 @@ extern "C" int64_t vfb_fp8_ffn_workspace_bytes(int64_t M, int64_t H, int64_t F) 
   return ffn_layout(M, H, F).total;
 }
 
-extern "C" int vfb_fp8_ffn(const void *x, int64_t M, int64_t H, int64_t ldx, const void *w_up, const float *s_up,
-                           int64_t n_up, const void *w_down, const float *s_down, int32_t activation,
-                           const void *bias_up, const void *bias_down, const void *residual, int64_t ldr,
-                           const void *gate, int64_t gate_token_stride, int64_t tokens, void *out, int64_t ldo,
-                           void *workspace, int64_t workspace_bytes, void *stream) {
-  using namespace vfb;
+namespace vfb {
+namespace {
+
+int ffn_entry(const char *fn, bool one_kernel, const void *x, int64_t M, int64_t H, int64_t ldx,
+              const void *w_up, const float *s_up, int64_t n_up, const void *w_down, const float *s_down,
+              int32_t activation, const void *bias_up, const void *bias_down, const void *residual, int64_t ldr,
+              const void *gate, int64_t gate_token_stride, int64_t tokens, void *out, int64_t ldo,
+              void *workspace, int64_t workspace_bytes, void *stream) {
   int64_t F = 0;
-  int rc = ffn_check("vfb_fp8_ffn", M, H, n_up, activation, w_up, s_up, w_down, s_down, bias_up, bias_down,
-                     residual, ldr, gate, gate_token_stride, tokens, out, ldo, &F);
+  int rc = ffn_check(fn, M, H, n_up, activation, w_up, s_up, w_down, s_down, bias_up, bias_down, residual, ldr,
+                     gate, gate_token_stride, tokens, out, ldo, &F);
   if (rc != VFB_OK) return rc;
   const FfnWorkspace lay = ffn_layout(M, H, F);
   if (workspace == nullptr || workspace_bytes < lay.total || reinterpret_cast<uintptr_t>(workspace) % kAlign)
-    return set_error(VFB_EINVAL, "vfb_fp8_ffn: workspace must be 256-byte aligned and hold %lld bytes",
+    return set_error(VFB_EINVAL, "%s: workspace must be 256-byte aligned and hold %lld bytes", fn,
                      (long long)lay.total);
   if (M == 0) return VFB_OK;
   uint8_t *ws = static_cast<uint8_t *>(workspace);
@@ -182,8 +186,32 @@ extern "C" int vfb_fp8_ffn(const void *x, int64_t M, int64_t H, int64_t ldx, con
   float *xs = reinterpret_cast<float *>(ws + lay.x_scales);
   rc = vfb_fp8_quant_rows(x, M, H, ldx, xc, xs, pad16(M), stream);
   if (rc != VFB_OK) return rc;
-  return ffn_body("vfb_fp8_ffn", xc, xs, M, H, w_up, s_up, n_up, w_down, s_down, activation, bias_up, bias_down,
-                  residual, ldr, gate, gate_token_stride, tokens, out, ldo, ws, lay, F, stream);
+  return ffn_body(fn, xc, xs, M, H, w_up, s_up, n_up, w_down, s_down, activation, bias_up, bias_down, residual,
+                  ldr, gate, gate_token_stride, tokens, out, ldo, ws, lay, F, one_kernel, stream);
+}
+
+}  // namespace
+}  // namespace vfb
+
+extern "C" int vfb_fp8_ffn(const void *x, int64_t M, int64_t H, int64_t ldx, const void *w_up, const float *s_up,
+                           int64_t n_up, const void *w_down, const float *s_down, int32_t activation,
+                           const void *bias_up, const void *bias_down, const void *residual, int64_t ldr,
+                           const void *gate, int64_t gate_token_stride, int64_t tokens, void *out, int64_t ldo,
+                           void *workspace, int64_t workspace_bytes, void *stream) {
+  return vfb::ffn_entry("vfb_fp8_ffn", false, x, M, H, ldx, w_up, s_up, n_up, w_down, s_down, activation, bias_up,
+                        bias_down, residual, ldr, gate, gate_token_stride, tokens, out, ldo, workspace,
+                        workspace_bytes, stream);
+}
+
+extern "C" int vfb_fp8_ffn_one_kernel(const void *x, int64_t M, int64_t H, int64_t ldx, const void *w_up,
+                                      const float *s_up, int64_t n_up, const void *w_down, const float *s_down,
+                                      int32_t activation, const void *bias_up, const void *bias_down,
+                                      const void *residual, int64_t ldr, const void *gate,
+                                      int64_t gate_token_stride, int64_t tokens, void *out, int64_t ldo,
+                                      void *workspace, int64_t workspace_bytes, void *stream) {
+  return vfb::ffn_entry("vfb_fp8_ffn_one_kernel", true, x, M, H, ldx, w_up, s_up, n_up, w_down, s_down,
+                        activation, bias_up, bias_down, residual, ldr, gate, gate_token_stride, tokens, out, ldo,
+                        workspace, workspace_bytes, stream);
 }
 
 extern "C" int vfb_fp8_ffn_quantized(const void *x_codes, const float *x_scales, int64_t M, int64_t H,
@@ -206,5 +234,5 @@ extern "C" int vfb_fp8_ffn_quantized(const void *x_codes, const float *x_scales,
     return set_error(VFB_EINVAL, "vfb_fp8_ffn_quantized: x codes need a 16-byte aligned [M, H] matrix");
   return ffn_body("vfb_fp8_ffn_quantized", x_codes, x_scales, M, H, w_up, s_up, n_up, w_down, s_down, activation,
                   bias_up, bias_down, residual, ldr, gate, gate_token_stride, tokens, out, ldo,
-                  static_cast<uint8_t *>(workspace), lay, F, stream);
+                  static_cast<uint8_t *>(workspace), lay, F, false, stream);
 }

@@ -350,6 +350,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
         if (rank == 0) {
           // every consumer of both CTAs has read the item this slot held
           if (!mbar_wait_cluster(&item_empty[slot], iph ^ 1, abort_flag, p.status)) break;
+          // an item is taken only when this pair can start it: an item taken
+          // ahead would hold up the row blocks whose conversions others wait for
           q = atomicAdd(p.queue, 1);
           if (q >= p.plan.total) q = -1;
           items[slot] = q;
@@ -644,14 +646,18 @@ int launch_ffn_fused(const FfnFusedArgs &a, void *stream) {
   pl.rows_blocks = static_cast<int>((a.M + 2 * BM - 1) / (2 * BM));
   pl.ju = static_cast<int>(swiglu ? a.F / BN_HALF : a.F / BN);
   pl.jd = static_cast<int>((a.H + BN - 1) / BN);
-  pl.group = a.group > 0 ? a.group : 4;
+  pl.group = a.group > 0 ? a.group : 8;
   pl.groups = (pl.rows_blocks + pl.group - 1) / pl.group;
   // half the GEMM's band budget for each weight: both bands, a group's
   // intermediate and its codes share L2
   pl.band_up = a.band_up > 0 ? a.band_up : band_width(pl.ju, 2 * a.H);
   pl.band_down = a.band_down > 0 ? a.band_down : band_width(pl.jd, 2 * a.F);
   const int pairs_max = sm_count / 2;
-  pl.lead = a.lead >= 0 ? a.lead : 2 * pairs_max;
+  // measured at config 2: interleaving down tiles with the next group's up
+  // tiles made them wait for conversions (lead 0: 7.1 ms, 148: 5.5 ms, a
+  // whole group: 4.3-4.5 ms), so by default a group's down tiles follow the
+  // next group's up tiles
+  pl.lead = a.lead >= 0 ? a.lead : 1 << 30;
   pl.lag = a.lag > 0 ? a.lag : 1;
   pl.total = pl.rows_blocks * (pl.ju + pl.jd);
   p.done_target = pl.ju * 2 * EPI_WARPS;

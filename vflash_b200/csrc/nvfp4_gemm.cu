@@ -343,6 +343,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
                 bf16r_x32(av);
 #pragma unroll
                 for (int j = 0; j < 32; ++j) v[j] = v[j] + av[j];
+                bf16r_x32(v);  // the merge's own rounding (the store packs exact bf16 values)
               }
             } else if constexpr (EPI == VFB_EPI_GELU_TANH) {
 #pragma unroll
@@ -364,7 +365,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 #pragma unroll
             for (int j = 0; j < 32; ++j) v[j] = 0.0f;
           }
-          store_box<EPI_BOXES>(warp_smem, box, &tmOut, v, lane, col, static_cast<int32_t>(row0), plane, any_row);
+          // STORE values are bf16 already (alpha_bias / the merge rounded them)
+          store_box<EPI_BOXES, false, EPI == VFB_EPI_STORE>(warp_smem, box, &tmOut, v, lane, col,
+                                                            static_cast<int32_t>(row0), plane, any_row);
         }
       }
     }

@@ -324,13 +324,14 @@ def _ffn_operands(rows, hidden, device, up, up_scales, down, down_scales, activa
 
 def fp8_ffn(x: torch.Tensor, up: torch.Tensor, up_scales: torch.Tensor, down: torch.Tensor,
             down_scales: torch.Tensor, *, activation: int = _lib.EPI_GELU_TANH, up_bias=None, down_bias=None,
-            residual=None, gate=None) -> torch.Tensor:
+            residual=None, gate=None, one_kernel: bool = False) -> torch.Tensor:
     """The whole FP8 FFN through ``vfb_fp8_ffn`` (one C call, workspace from torch's allocator).
 
     ``x`` bf16 ``[M, H]`` (unit column stride), ``up`` e4m3 ``[F or 2F, H]``,
     ``down`` e4m3 ``[H, F]``, scales fp32 ``[N, 1]``; ``residual`` bf16
     ``[M, H]`` and ``gate`` bf16 ``[tokens, H]`` as the down GEMM's RESIDUAL
-    epilogue.  Returns bf16 ``[M, H]``.
+    epilogue.  ``one_kernel`` selects ``vfb_fp8_ffn_one_kernel`` (the same
+    bits from one persistent launch).  Returns bf16 ``[M, H]``.
     """
     if x.dtype != BF16 or x.ndim != 2 or x.stride(1) != 1:
         raise KernelInputError("FP8 FFN input must be bf16 [M, H] with unit column stride")
@@ -339,10 +340,11 @@ def fp8_ffn(x: torch.Tensor, up: torch.Tensor, up_scales: torch.Tensor, down: to
     lib, need, workspace, base, tail = _ffn_operands(rows, hidden, device, up, up_scales, down, down_scales,
                                                      activation, up_bias, down_bias, residual, gate)
     out = torch.empty((rows, hidden), device=device, dtype=BF16)
+    entry = lib.vfb_fp8_ffn_one_kernel if one_kernel else lib.vfb_fp8_ffn
     with torch.cuda.device(device):
-        rc = lib.vfb_fp8_ffn(x.data_ptr(), rows, hidden, x.stride(0), *tail, out.data_ptr(), hidden, base, need,
-                             _lib.stream_handle(device))
-    _lib.check(rc, "vfb_fp8_ffn")
+        rc = entry(x.data_ptr(), rows, hidden, x.stride(0), *tail, out.data_ptr(), hidden, base, need,
+                   _lib.stream_handle(device))
+    _lib.check(rc, "vfb_fp8_ffn_one_kernel" if one_kernel else "vfb_fp8_ffn")
     return out
 
 

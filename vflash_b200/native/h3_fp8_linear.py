@@ -359,7 +359,8 @@ class RowFP8Execution:
         return out.reshape(*shape[:-1], n)
 
     def ffn(self, value, up_weight, up_scale, down_weight, down_scale, *, activation="gelu_tanh",
-            up_bias=None, down_bias=None, residual=None, gate=None, prologue: NormModulate | None = None):
+            up_bias=None, down_bias=None, residual=None, gate=None, prologue: NormModulate | None = None,
+            one_kernel: bool = False):
         """Fused FFN: up GEMM + activation -> per-token e4m3 requant -> down GEMM.
 
         ``activation`` is ``"gelu_tanh"`` (up weight ``[F, H]``) or ``"swiglu"``
@@ -369,8 +370,9 @@ class RowFP8Execution:
         the reference quantises the activation of the next linear
         (src/vflash/native/h3_fp8_activation.py:16-19).  One native call
         (``vfb_fp8_ffn``, or ``vfb_fp8_ffn_quantized`` after a fused
-        ``prologue``): the up GEMM, the requantisation and the down GEMM run
-        as one kernel whose bf16 intermediate stays in L2.
+        ``prologue``) that runs the up GEMM, the requantisation and the down
+        GEMM as three launches; ``one_kernel=True`` (no prologue) runs them as
+        one persistent kernel (``vfb_fp8_ffn_one_kernel``, same bits).
         """
         if (
             down_weight.ndim != 2
@@ -402,8 +404,10 @@ class RowFP8Execution:
         self.calls["w8a8"] += 1  # the FFN's second linear
         if prologue is None:
             with self.measure("linear.fp8_gemm"):
-                out = fp8_ffn(matrix, up_weight, up_scale, down_weight, down_scale, **args)
+                out = fp8_ffn(matrix, up_weight, up_scale, down_weight, down_scale, one_kernel=one_kernel, **args)
         else:
+            if one_kernel:
+                raise ValueError("the one-kernel FFN takes the unquantised input (no prologue)")
             codes, act_scale = self._quantize(matrix, prologue, shape)
             with self.measure("linear.fp8_gemm"):
                 out = fp8_ffn_quantized(codes, act_scale, rows, up_weight, up_scale, down_weight, down_scale,
