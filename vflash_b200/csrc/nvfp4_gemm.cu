@@ -292,20 +292,56 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       const bool odd = t & 1;
       const uint32_t t_row = tmem_base + (odd ? ACC1_COL : 0u) + (static_cast<uint32_t>(q * 32) << 16);
       // The 64 columns the two accumulators share are the last of an even
-      // tile and the first of an odd one: drain them first (even tiles in
-      // reverse chunk order), then release them to the next tile's MMAs.
-      // For SWIGLU they are gate chunks 2-3 (even) or value chunks 0-1 (odd).
+      // tile and the first of an odd one: both are read first, with one wait
+      // (even tiles go in reverse chunk order), and then released to the
+      // next tile's MMAs.  For SWIGLU they are gate chunks 2-3 (even) or
+      // value chunks 0-1 (odd).
+      uint32_t held[32];  // the second shared chunk, loaded together with the first
 #pragma unroll 1
       for (int i = 0; i < kChunks; ++i) {
         const int c = odd ? i : (kChunks - 1 - i);
         float v[32];
         if constexpr (kSwiglu) {
           float g[32];
-          tmem_ld_32x32b_x32(t_row + c * 32, v);
-          tmem_ld_32x32b_x32(t_row + BN_HALF + c * 32, g);
-          if (i == 1) {
+          uint32_t rv[32], rg[32];
+          if (i == 0) {
+            // this chunk's value and gate columns and the second shared chunk
+            // (gate c - 1 of an even tile, value 1 of an odd one), one wait
+            tmem_ld_32x32b_x32_issue(t_row + c * 32, rv);
+            tmem_ld_32x32b_x32_issue(t_row + BN_HALF + c * 32, rg);
+            tmem_ld_32x32b_x32_issue(odd ? t_row + 32 : t_row + BN_HALF + (c - 1) * 32, held);
+            tmem_ld_wait();
+            tmem_ld_fence(rv);
+            tmem_ld_fence(rg);
+            tmem_ld_fence(held);
             tc_fence_before();
             mbar_arrive_cluster(tfree_leader);
+          } else if (i == 1) {
+            // the shared half was loaded with chunk 0; load the other one
+            if (odd) {
+              tmem_ld_32x32b_x32_issue(t_row + BN_HALF + c * 32, rg);
+              tmem_ld_wait();
+              tmem_ld_fence(rg);
+#pragma unroll
+              for (int j = 0; j < 32; ++j) rv[j] = held[j];
+            } else {
+              tmem_ld_32x32b_x32_issue(t_row + c * 32, rv);
+              tmem_ld_wait();
+              tmem_ld_fence(rv);
+#pragma unroll
+              for (int j = 0; j < 32; ++j) rg[j] = held[j];
+            }
+          } else {
+            tmem_ld_32x32b_x32_issue(t_row + c * 32, rv);
+            tmem_ld_32x32b_x32_issue(t_row + BN_HALF + c * 32, rg);
+            tmem_ld_wait();
+            tmem_ld_fence(rv);
+            tmem_ld_fence(rg);
+          }
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            v[j] = __uint_as_float(rv[j]);
+            g[j] = __uint_as_float(rg[j]);
           }
           const int32_t f = n_tile * BN_HALF + c * 32;
           if (f >= p.F) continue;  // warp-uniform
@@ -320,11 +356,26 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           }
           store_box<EPI_BOXES>(warp_smem, box, &tmOut, v, lane, f, static_cast<int32_t>(row0), 0, any_row);
         } else {
-          tmem_ld_32x32b_x32(t_row + c * 32, v);
-          if (i == 1) {
+          uint32_t r[32];
+          if (i == 0) {
+            // both shared chunks with one wait, then release them
+            tmem_ld_32x32b_x32_issue(t_row + c * 32, r);
+            tmem_ld_32x32b_x32_issue(t_row + (odd ? 1 : kChunks - 2) * 32, held);
+            tmem_ld_wait();
+            tmem_ld_fence(r);
+            tmem_ld_fence(held);
             tc_fence_before();
             mbar_arrive_cluster(tfree_leader);
+          } else if (i == 1) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) r[j] = held[j];
+          } else {
+            tmem_ld_32x32b_x32_issue(t_row + c * 32, r);
+            tmem_ld_wait();
+            tmem_ld_fence(r);
           }
+#pragma unroll
+          for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
           const int32_t n = n_tile * BN + c * 32;
           if (n >= p.N) continue;  // warp-uniform
           const int32_t plane = n / p.plane_width;
