@@ -11,6 +11,7 @@ pytestmark = pytest.mark.gpu
 
 @pytest.mark.parametrize("argv", [
     ["fp8_gemm", "--rows", "300", "--repeats", "1"],
+    ["fp8_gemm_gelu", "--rows", "300", "--repeats", "1"],
     ["ffn", "--rows", "300", "--repeats", "1"],
     ["ffn", "--rows", "300", "--repeats", "1", "--swiglu", "--one-kernel"],
     ["nvfp4_gemm", "--rows", "300", "--n", "256", "--repeats", "1"],

@@ -158,7 +158,7 @@ __device__ __forceinline__ void store_value(float (&v)[32], float sa, const floa
 }
 
 
-__device__ __forceinline__ uint2 ld4(const __nv_bfloat16 *p) { return __ldg(reinterpret_cast<const uint2 *>(p)); }
+__device__ __forceinline__ uint4 ld8(const __nv_bfloat16 *p) { return __ldg(reinterpret_cast<const uint4 *>(p)); }
 
 __device__ __forceinline__ __nv_bfloat162 as_bf162(uint32_t u) { return *reinterpret_cast<__nv_bfloat162 *>(&u); }
 
@@ -174,20 +174,23 @@ __device__ __forceinline__ __nv_bfloat162 as_bf162(uint32_t u) { return *reinter
 __device__ __forceinline__ void qk_norm_rope_chunk(const uint32_t (&hp)[64], float rstd, int k,
                                                    const __nv_bfloat16 *w, const __nv_bfloat16 *cs,
                                                    const __nv_bfloat16 *sn, float (&out)[32]) {
-  const uint2 one = make_uint2(0x3f803f80u, 0x3f803f80u);
+  const uint4 one = make_uint4(0x3f803f80u, 0x3f803f80u, 0x3f803f80u, 0x3f803f80u);
   const int kp = k ^ 2;  // the partner chunk (64 columns away)
   const bool first = k < 2;
+  // eight columns per step: 16-byte loads of the norm weights and of this
+  // row's cos / sin (each lane reads its own token's row)
 #pragma unroll
-  for (int g = 0; g < 8; ++g) {
-    const int d = 32 * k + 4 * g;   // this chunk's columns d .. d+3
-    const int dp = 32 * kp + 4 * g;  // partner columns
-    const uint2 wv = w ? ld4(w + d) : one, wp = w ? ld4(w + dp) : one;
-    const uint2 cv = ld4(cs + d), sv = ld4(sn + d);
-    const uint32_t ww[2] = {wv.x, wv.y}, wpw[2] = {wp.x, wp.y}, cw[2] = {cv.x, cv.y}, sw[2] = {sv.x, sv.y};
+  for (int g = 0; g < 4; ++g) {
+    const int d = 32 * k + 8 * g;   // this chunk's columns d .. d+7
+    const int dp = 32 * kp + 8 * g;  // partner columns
+    const uint4 wv = w ? ld8(w + d) : one, wp = w ? ld8(w + dp) : one;
+    const uint4 cv = ld8(cs + d), sv = ld8(sn + d);
+    const uint32_t ww[4] = {wv.x, wv.y, wv.z, wv.w}, wpw[4] = {wp.x, wp.y, wp.z, wp.w};
+    const uint32_t cw[4] = {cv.x, cv.y, cv.z, cv.w}, sw[4] = {sv.x, sv.y, sv.z, sv.w};
 #pragma unroll
-    for (int h = 0; h < 2; ++h) {
-      const float2 x = __bfloat1622float2(as_bf162(hp[16 * k + 2 * g + h]));
-      const float2 xp = __bfloat1622float2(as_bf162(hp[16 * kp + 2 * g + h]));
+    for (int h = 0; h < 4; ++h) {
+      const float2 x = __bfloat1622float2(as_bf162(hp[16 * k + 4 * g + h]));
+      const float2 xp = __bfloat1622float2(as_bf162(hp[16 * kp + 4 * g + h]));
       const float2 fw = __bfloat1622float2(as_bf162(ww[h]));
       const float2 fwp = __bfloat1622float2(as_bf162(wpw[h]));
       const __nv_bfloat162 n = __floats2bfloat162_rn((x.x * rstd) * fw.x, (x.y * rstd) * fw.y);
@@ -195,8 +198,8 @@ __device__ __forceinline__ void qk_norm_rope_chunk(const uint32_t (&hp)[64], flo
       if (first) np = __hneg2(np);
       const float2 c = __bfloat1622float2(__hmul2(n, as_bf162(cw[h])));
       const float2 sp = __bfloat1622float2(__hmul2(np, as_bf162(sw[h])));
-      out[4 * g + 2 * h] = c.x + sp.x;
-      out[4 * g + 2 * h + 1] = c.y + sp.y;
+      out[8 * g + 2 * h] = c.x + sp.x;
+      out[8 * g + 2 * h + 1] = c.y + sp.y;
     }
   }
 }

@@ -7,12 +7,14 @@ with seeded synthetic inputs and exits non-zero when the library reports a
 device error or the output is not finite::
 
     python -m vflash_b200.profile_cases fp8_gemm --rows 4096
+    python -m vflash_b200.profile_cases fp8_gemm_gelu --rows 8192
     python -m vflash_b200.profile_cases ffn --rows 8192 [--swiglu] [--one-kernel]
     python -m vflash_b200.profile_cases nvfp4_gemm --rows 8192 --n 4096
 
 Shapes other than the row count are those of the benchmark configurations:
 the merged QKV projection (N = 12288, K = 4096), the FFN (H = 4096,
-F = 16384) and the NVFP4 linear (K = 4096).
+F = 16384; ``fp8_gemm_gelu`` is its up projection alone) and the NVFP4
+linear (K = 4096).
 """
 
 from __future__ import annotations
@@ -41,6 +43,13 @@ def run(case: str, rows: int, repeats: int, n: int = 4096, swiglu: bool = False,
         codes, scales = quantize_fp8_rows(x)
         for _ in range(repeats):
             y = fp8_gemm(codes, scales, rows, w, ws, Epilogue(bias=bias, planes=3))
+    elif case == "fp8_gemm_gelu":
+        # the FFN's up projection (F = 16384) with the GELU-tanh epilogue
+        x = _seeded(rows, 4096, 1, 1.0, device)
+        w, ws = quantize_fp8_rows(_seeded(16384, 4096, 2, 0.02, device), pad_to=1)
+        codes, scales = quantize_fp8_rows(x)
+        for _ in range(repeats):
+            y = fp8_gemm(codes, scales, rows, w, ws, Epilogue(kind=_lib.EPI_GELU_TANH))
     elif case == "ffn":
         h, f = 4096, 16384
         x = _seeded(rows, h, 1, 1.0, device)
@@ -68,7 +77,7 @@ def run(case: str, rows: int, repeats: int, n: int = 4096, swiglu: bool = False,
 
 def main(argv=None) -> int:
     parser = argparse.ArgumentParser(description=__doc__.split("\n\n")[0])
-    parser.add_argument("case", choices=["fp8_gemm", "ffn", "nvfp4_gemm"])
+    parser.add_argument("case", choices=["fp8_gemm", "fp8_gemm_gelu", "ffn", "nvfp4_gemm"])
     parser.add_argument("--rows", type=int, default=4096)
     parser.add_argument("--n", type=int, default=4096, help="NVFP4 output features")
     parser.add_argument("--repeats", type=int, default=3)
