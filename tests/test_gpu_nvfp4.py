@@ -267,6 +267,50 @@ def test_residual_epilogue_bit_exact_nvfp4(with_gate):
     np.testing.assert_array_equal(bits_of(fused), want)
 
 
+@pytest.mark.parametrize("kind", ["gelu", "swiglu", "residual", "merge"])
+def test_epilogues_over_many_tiles_per_pair(kind):
+    """Every CTA pair runs several tiles, so both accumulators (even and odd
+    tiles, which share 64 TMEM columns and hand them over differently) carry
+    each epilogue: 16 row blocks x 10 tiles of 256 columns = 160 tiles."""
+    m, n, k = 4096 - 37, 2560, 256
+    a_codes, a_sf, wp, ws, w_alpha, gsf, bias = nvfp4_case(m, n, k, 131)
+    alpha = (w_alpha / gsf).to(torch.float32)
+    base = nvfp4_gemm(a_codes, a_sf, wp, ws, alpha, bias)
+    gen = torch.Generator().manual_seed(29)
+    if kind == "gelu":
+        fused = nvfp4_gemm(a_codes, a_sf, wp, ws, alpha, epilogue=Epilogue(kind=_lib.EPI_GELU_TANH, bias=bias))
+        want = fp8.bf16_value(ep.gelu_tanh(bits_of(base)))
+        got = fp8.bf16_value(bits_of(fused))
+        np.testing.assert_allclose(got, want, rtol=2.0**-7, atol=1e-6)
+        assert (got != want).mean() < 1e-2
+    elif kind == "swiglu":
+        fused = nvfp4_gemm(a_codes, a_sf, wp, ws, alpha, epilogue=Epilogue(kind=_lib.EPI_SWIGLU, bias=bias))
+        assert fused.shape == (m, n // 2)
+        want = fp8.bf16_value(ep.silu_mul(bits_of(base)))
+        got = fp8.bf16_value(bits_of(fused))
+        np.testing.assert_allclose(got, want, rtol=2.0**-7, atol=1e-6)
+        assert (got != want).mean() < 1e-2
+    elif kind == "residual":
+        residual = torch.randn(m, n, generator=gen).to(torch.bfloat16).to(DEV)
+        fused = nvfp4_gemm(a_codes, a_sf, wp, ws, alpha,
+                           epilogue=Epilogue(kind=_lib.EPI_RESIDUAL, bias=bias, residual=residual))
+        want = fp8.bf16_bits(fp8.bf16_value(bits_of(residual)) + fp8.bf16_value(bits_of(base)))
+        np.testing.assert_array_equal(bits_of(fused), want)
+    else:
+        h = 896  # three planes: N = 2688 = 21 x 128, 11 tiles of 256 columns per row block
+        n3 = 3 * h
+        a3, s3, wp3, ws3, w3, g3, b3 = nvfp4_case(m, n3, k, 137)
+        alpha3 = (w3 / g3).to(torch.float32)
+        base3 = nvfp4_gemm(a3, s3, wp3, ws3, alpha3, b3)
+        adapters = tuple(torch.randn(m, h, generator=gen).to(torch.bfloat16).to(DEV) for _ in range(3))
+        scalings = (0.0625, 0.5, -1.25)
+        merged = nvfp4_gemm(a3, s3, wp3, ws3, alpha3,
+                            epilogue=Epilogue(bias=b3, planes=3, adapters=adapters, scalings=scalings))
+        want = ep.qkv_direct_merge(bits_of(base3), np.stack([bits_of(a) for a in adapters]), scalings)
+        for i in range(3):
+            np.testing.assert_array_equal(bits_of(merged[i]), want[:, i * h:(i + 1) * h])
+
+
 def test_execution_fused_entry_points_equal_linear_then_step():
     n, k = 384, 512
     _w, packed, scales, w_alpha = weight_case(n, k, 111)
