@@ -252,8 +252,10 @@ VFB_API int vfb_fp8_ffn(const void *x, int64_t M, int64_t H, int64_t ldx,
  * are all done the warps that stored it requantise it to e4m3 and drop the
  * bf16 lines from L2; the row block's down tiles then read the codes.  The
  * bf16 intermediate stays in L2 only while a group's intermediate fits next
- * to the weight tiles in use: at the benchmark's FFN (M 32760, H 4096,
- * F 16384) it does not, and this path is slower than vfb_fp8_ffn. */
+ * to the weight tiles in use.  Measured on the B200 at H 4096, F 16384
+ * (GELU), this path is slower than vfb_fp8_ffn at every M from 512 to 32760
+ * (1.4-1.7x at M <= 2048, 1.35x at 32760): the down tiles wait for their
+ * row blocks' conversion and the up epilogue carries the conversion work. */
 VFB_API int vfb_fp8_ffn_one_kernel(const void *x, int64_t M, int64_t H, int64_t ldx,
                 const void *w_up, const float *s_up, int64_t n_up,
                 const void *w_down, const float *s_down, int32_t activation,
