@@ -759,6 +759,38 @@ def other_configs(device, flush, stream, cpu_seconds: float = 0.0) -> dict:
         if n == 4096 and cpu_seconds > 0:
             ac, asf = nvfp4_quantize(x, gsf_x)
             out["c3_nvfp4_n4096"]["cpu_baseline"] = nvfp4_cpu_baseline(ac, asf, wp, wsc, alpha, cpu_seconds)
+    del x
+    # QAD-style NVFP4 FFN at config 2's shape (H 4096, F 16384, GELU-tanh):
+    # NVFP4Execution.ffn, whose up GEMM writes the intermediate as NVFP4 codes
+    # for the down linear, against the unfused linear(gelu_linear(...)) chain
+    from vflash_b200.native.h3_nvfp4_linear import NVFP4Execution, NVFP4Weight
+
+    m, h, f = 32760, 4096, 16384
+    x = seeded(m, h, 1004)
+
+    def nv_weight(rows, cols, seed, input_scale):
+        w = seeded(rows, cols, seed, std=0.02)
+        gw = (448.0 * 6.0 / w.float().abs().max()).reshape(())
+        packed, scales = nvfp4_quantize(w, gw)
+        return NVFP4Weight(packed, scales.view(rows, cols // 16).contiguous(), (1.0 / gw).to(torch.float32),
+                           input_scale.to(torch.float32))
+
+    engine = NVFP4Execution()
+    up = nv_weight(f, h, 2040, (448.0 * 6.0 / x.float().abs().max()).reshape(()))
+    mid = engine.gelu_linear(x, up)
+    down = nv_weight(h, f, 2041, (448.0 * 6.0 / mid.float().abs().max()).reshape(()))
+    del mid
+    fused_ms = statistics.median(_timed(lambda: engine.ffn(x, up, down), flush, stream))
+    unfused_ms = statistics.median(_timed(lambda: engine.linear(engine.gelu_linear(x, up), down), flush, stream))
+    same = bool(torch.equal(engine.ffn(x, up, down), engine.linear(engine.gelu_linear(x, up), down)))
+    ffn_flop = 4.0 * m * h * f
+    out["c2_shape_nvfp4_ffn_gelu"] = {
+        "ms": round(fused_ms, 4), "tflops": round(ffn_flop / (fused_ms * 1e-3) / 1e12, 1),
+        "frac_of_peak": round(ffn_flop / (fused_ms * 1e-3) / 1e12 / fp4_peak, 4),
+        "unfused_ms": round(unfused_ms, 4), "equal_bits": same,
+        "step": "NVFP4Execution.ffn (quantiser, up GEMM + GELU-tanh writing NVFP4 codes, down GEMM) vs "
+                "linear(gelu_linear(x, up), down) (the bf16 intermediate round-trips and is quantised again)"}
+    del x, up, down
     out["peak_note"] = ("fp8 peak = 2 x measured cuBLAS bf16 burst, fp4 peak = 4 x; nominal dense "
                         "fp8 4.5, fp4 9 PFLOP/s")
     return out

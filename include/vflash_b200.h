@@ -344,6 +344,23 @@ VFB_API int vfb_nvfp4_gemm_ex(const void *A, const void *sfa, const void *W, con
                               const float *alpha, const float *alpha_div, int64_t M, int64_t N, int64_t K,
                               const vfb_epilogue *ep, void *stream);
 
+/* vfb_nvfp4_gemm_ex whose result leaves the kernel quantised for the next
+ * NVFP4 linear instead of as bf16: the bf16 values the epilogue would store
+ * (VFB_EPI_STORE with one plane and no adapters, VFB_EPI_GELU_TANH or
+ * VFB_EPI_SWIGLU) are quantised as vfb_nvfp4_quant_rows(values,
+ * out_global_scale) would quantise them, bit for bit: out_codes e2m1
+ * [M, W/2] (contiguous) and out_sf 128x4 scales for ceil128(M) rows and W/16
+ * groups (padding rows 0), W = N (SWIGLU: N/2), W % 64 == 0.  ep->out, ldo,
+ * plane_width and plane_stride are not used.  No reference counterpart: the
+ * reference stores the bf16 activation output and the next
+ * NVFP4Execution.linear quantises it again (h3_nvfp4_linear.py:102), so the
+ * intermediate of a QAD FFN round-trips HBM in bf16 and costs a quantiser
+ * launch; here it stays as codes. */
+VFB_API int vfb_nvfp4_gemm_quant(const void *A, const void *sfa, const void *W, const void *sfw,
+                                 const float *alpha, const float *alpha_div, int64_t M, int64_t N,
+                                 int64_t K, const vfb_epilogue *ep, const float *out_global_scale,
+                                 void *out_codes, void *out_sf, void *stream);
+
 /* ---- strict-BF16 elementwise steps -----------------------------------------
  * Standalone versions of the epilogues above, for callers whose GEMM is not
  * this library's.  bf16 tensors; the last dimension is contiguous and its

@@ -311,6 +311,56 @@ def test_epilogues_over_many_tiles_per_pair(kind):
             np.testing.assert_array_equal(bits_of(merged[i]), want[:, i * h:(i + 1) * h])
 
 
+@pytest.mark.parametrize("kind", ["store", "gelu", "swiglu"])
+@pytest.mark.parametrize("m", [130, 4096 - 37])
+def test_quantised_output_equals_the_quantiser_of_the_bf16_output(kind, m):
+    """vfb_nvfp4_gemm_quant: codes and 128x4 scales (padding rows included)
+    equal nvfp4_quantize of the bf16 result the same epilogue stores."""
+    n, k = 2560, 256
+    a_codes, a_sf, wp, ws, w_alpha, gsf, bias = nvfp4_case(m, n, k, 151)
+    alpha = (w_alpha / gsf).to(torch.float32)
+    epi = {"store": _lib.EPI_STORE, "gelu": _lib.EPI_GELU_TANH, "swiglu": _lib.EPI_SWIGLU}[kind]
+    y = nvfp4_gemm(a_codes, a_sf, wp, ws, alpha, epilogue=Epilogue(kind=epi, bias=bias))
+    next_scale = global_scale(y)
+    want_codes, want_sf = nvfp4_quantize(y, next_scale)
+    codes, sf = nvfp4_gemm(a_codes, a_sf, wp, ws, alpha, epilogue=Epilogue(kind=epi, bias=bias),
+                           quantize_output=next_scale)
+    assert codes.shape == want_codes.shape and sf.shape == want_sf.shape
+    assert torch.equal(codes, want_codes)
+    assert torch.equal(sf, want_sf)
+
+
+@pytest.mark.parametrize("activation", ["gelu_tanh", "swiglu"])
+@pytest.mark.parametrize("with_residual", [False, True])
+def test_execution_ffn_equals_the_two_linears(activation, with_residual):
+    """NVFP4Execution.ffn: the intermediate never exists in bf16, and the
+    result is the unfused linear(gelu_linear(...)) / swiglu chain bit for bit."""
+    h, f, tokens = 512, 768, 150
+    n_up = 2 * f if activation == "swiglu" else f
+    _w, up_packed, up_scales, up_alpha = weight_case(n_up, h, 161)
+    _w, down_packed, down_scales, down_alpha = weight_case(h, f, 162)
+    x = outlier_activations(2 * tokens, h, 163).to(DEV).view(2, tokens, h)
+    up = NVFP4Weight(up_packed, up_scales, up_alpha.reshape(()), global_scale(x))
+    engine = NVFP4Execution()
+    first = engine.swiglu_linear if activation == "swiglu" else engine.gelu_linear
+    gen = torch.Generator().manual_seed(164)
+    up_bias = (torch.randn(n_up, generator=gen) * 0.01).to(torch.bfloat16).to(DEV)
+    down_bias = (torch.randn(h, generator=gen) * 0.01).to(torch.bfloat16).to(DEV)
+    mid = first(x, up, up_bias)
+    down = NVFP4Weight(down_packed, down_scales, down_alpha.reshape(()), global_scale(mid))
+    if with_residual:
+        residual = outlier_activations(2 * tokens, h, 165).to(DEV).view(2, tokens, h)
+        gate = outlier_activations(tokens, h, 166).to(DEV)
+        want = engine.gate_residual_linear(mid, down, residual, gate, down_bias)
+        got = engine.ffn(x, up, down, activation=activation, up_bias=up_bias, down_bias=down_bias,
+                         residual=residual, gate=gate)
+    else:
+        want = engine.linear(mid, down, down_bias)
+        got = engine.ffn(x, up, down, activation=activation, up_bias=up_bias, down_bias=down_bias)
+    assert got.shape == want.shape
+    assert torch.equal(got, want)
+
+
 def test_execution_fused_entry_points_equal_linear_then_step():
     n, k = 384, 512
     _w, packed, scales, w_alpha = weight_case(n, k, 111)

@@ -121,6 +121,11 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         ctypes.c_int,
         [_vp, _vp, _vp, _vp, _vp, _vp, _c_int64, _c_int64, _c_int64, ctypes.POINTER(Epilogue), _vp],
     ),
+    "vfb_nvfp4_gemm_quant": (
+        ctypes.c_int,
+        [_vp, _vp, _vp, _vp, _vp, _vp, _c_int64, _c_int64, _c_int64, ctypes.POINTER(Epilogue), _vp, _vp, _vp,
+         _vp],
+    ),
     "vfb_silu_mul": (ctypes.c_int, [_vp, _c_int64, _c_int64, _vp, _c_int64, _vp]),
     "vfb_ffn_adapter_silu": (
         ctypes.c_int, [_vp, _vp, _c_int64, _c_int64, ctypes.c_float, _vp, _c_int64, _vp]),

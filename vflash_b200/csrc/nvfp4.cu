@@ -1,24 +1,15 @@
 // NVFP4 (e2m1 with one ue4m3 scale per 16 elements) activation quantiser for
 // sm_100a.
 //
-// Quantiser — replaces FlashInfer nvfp4_quantize(x, global_scale,
-// sfLayout=128x4, do_shuffle=False) as called by NVFP4Execution.linear
-// (src/vflash/native/h3_nvfp4_linear.py:102).  Per group of 16 elements
-// (FlashInfer 0.6.18's default, non-TE-exact recipe, restated from its
-// published source quantization_utils.cuh:294-380):
-//   amax   = max |x|
-//   sf     = e4m3_rn_satfinite(gsf * (amax * rcp(6)))
-//   scale  = amax != 0 ? rcp(float(sf) * rcp(gsf)) : 0
-//   code_i = e2m1_rn_satfinite(x_i * scale)        (element 2i in the low nibble)
-// with rcp = rcp.approx.ftz.f32, so the codes and scales match that kernel bit
-// for bit.  Scales are written in the 128x4 layout: for row m and 16-element
-// group k, byte offset
-//   (m/128)*(kt*512) + (k/4)*512 + (m%32)*16 + ((m%128)/32)*4 + k%4,
-// kt = ceil(K/64); rows up to ceil128(M) and groups up to 4*kt exist, and the
-// padding entries are written as 0.  One thread handles one 16-element group
-// (two 16-byte loads, one 8-byte store of codes, one scale byte).  The
-// multiplies flush subnormals (mul.ftz), as the reference's fast-math build
-// does.
+// Replaces FlashInfer nvfp4_quantize(x, global_scale, sfLayout=128x4,
+// do_shuffle=False) as called by NVFP4Execution.linear
+// (src/vflash/native/h3_nvfp4_linear.py:102).  The arithmetic of a 16-element
+// group (FlashInfer's recipe, bit for bit) is nvfp4_group() in
+// nvfp4_quant.cuh, which the GEMM's quantising epilogue shares.  Scales are
+// written in the 128x4 layout for rows up to ceil128(M) and groups up to
+// 4*ceil(K/64); the padding entries are written as 0.  One thread handles one
+// 16-element group (two 16-byte loads, one 8-byte store of codes, one scale
+// byte).
 //
 // The block-scaled GEMM that consumes these codes is in nvfp4_gemm.cu.
 #include <cudaTypedefs.h>
@@ -26,6 +17,7 @@
 #include <mutex>
 
 #include "common.cuh"
+#include "nvfp4_quant.cuh"
 
 namespace vfb {
 namespace {
@@ -39,31 +31,6 @@ __device__ __forceinline__ float to_f32(uint16_t bits) {
   return __uint_as_float(static_cast<uint32_t>(bits) << 16);
 }
 
-// Multiplication with subnormal inputs and results flushed to zero, as the
-// reference quantiser's fast-math build performs it.
-__device__ __forceinline__ float mul_ftz(float a, float b) {
-  float r;
-  asm("mul.rn.ftz.f32 %0, %1, %2;" : "=f"(r) : "f"(a), "f"(b));
-  return r;
-}
-
-__device__ __forceinline__ uint32_t e4m3_byte(float x) {
-  uint16_t r;
-  asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(r) : "f"(0.0f), "f"(x));
-  return r & 0xFFu;
-}
-
-__device__ __forceinline__ float e4m3_value(uint32_t byte) {
-  // exact decode of a non-negative finite e4m3 byte
-  const uint32_t e = (byte >> 3) & 0xF, m = byte & 0x7;
-  if (e == 0) return static_cast<float>(m) * 0.001953125f;  // m * 2^-9
-  return __uint_as_float(((e + 120u) << 23) | (m << 20));
-}
-
-__device__ __forceinline__ int64_t sf_offset(int64_t m, int64_t k, int64_t ktiles) {
-  return (m >> 7) * (ktiles * 512) + (k >> 2) * 512 + (m & 31) * 16 + ((m & 127) >> 5) * 4 + (k & 3);
-}
-
 template <bool FP16, bool VEC>
 __global__ void __launch_bounds__(256) nvfp4_quant_kernel(const uint16_t *__restrict__ x, int64_t M,
                                                           int64_t K, int64_t ldx,
@@ -71,9 +38,7 @@ __global__ void __launch_bounds__(256) nvfp4_quant_kernel(const uint16_t *__rest
                                                           uint8_t *__restrict__ codes,
                                                           uint8_t *__restrict__ sf, int64_t rows_pad,
                                                           int64_t groups_pad) {
-  const float gsf = __ldg(gsf_ptr);
-  const float rcp6 = rcp_approx_ftz(6.0f);
-  const float rcp_gsf = rcp_approx_ftz(gsf);
+  const Nvfp4Consts consts = nvfp4_consts(__ldg(gsf_ptr));
   const int64_t groups = K / 16;
   const int64_t ktiles = groups_pad / 4;
   const int64_t total = rows_pad * groups_pad;
@@ -98,21 +63,8 @@ __global__ void __launch_bounds__(256) nvfp4_quant_kernel(const uint16_t *__rest
 #pragma unroll
         for (int j = 0; j < 16; ++j) v[j] = to_f32<FP16>(src[j]);
       }
-      float amax = 0.0f;
-#pragma unroll
-      for (int j = 0; j < 16; ++j) amax = fmaxf(amax, fabsf(v[j]));
-      const float sf_value = mul_ftz(gsf, mul_ftz(amax, rcp6));
-      sf_byte = e4m3_byte(sf_value);
-      // amax != 0 compared after flushing a subnormal amax to zero
-      const float scale =
-          mul_ftz(amax, 1.0f) != 0.0f ? rcp_approx_ftz(mul_ftz(e4m3_value(sf_byte), rcp_gsf)) : 0.0f;
-      float lo[8], hi[8];
-#pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        lo[j] = mul_ftz(v[j], scale);
-        hi[j] = mul_ftz(v[8 + j], scale);
-      }
-      uint2 packed = make_uint2(pack_e2m1x8(lo), pack_e2m1x8(hi));
+      uint2 packed;
+      sf_byte = nvfp4_group(v, consts, packed);
       *reinterpret_cast<uint2 *>(codes + m * (K / 2) + k * 8) = packed;
     }
     sf[sf_offset(m, k, ktiles)] = static_cast<uint8_t>(sf_byte);

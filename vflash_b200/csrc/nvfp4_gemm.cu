@@ -28,6 +28,7 @@
 
 #include "common.cuh"
 #include "epilogue.cuh"
+#include "nvfp4_quant.cuh"
 
 namespace vfb {
 namespace {
@@ -71,7 +72,34 @@ struct Params {
   int num_m_tiles, num_n_tiles, ktiles;  // ktiles = K / 64
   int band_n;                            // weight tiles per band of the tile order
   int *status;
+  // quantised output (vfb_nvfp4_gemm_quant): e2m1 codes [M, q_ld] and 128x4
+  // scales of the bf16 result, for the next NVFP4 linear
+  uint8_t *q_codes;
+  uint8_t *q_sf;
+  const float *q_gsf;
+  int64_t q_ld;        // code bytes per row (output width / 2)
+  int64_t q_rows_pad;  // ceil128(M): scale rows that exist
+  int64_t q_ktiles;    // output width / 64
 };
+
+// The bf16 values of 32 output columns of row m, quantised as the next
+// NVFP4 linear's quantiser would (nvfp4_group, the same arithmetic as
+// vfb_nvfp4_quant_rows): 16 code bytes and two scale bytes.  Rows past M
+// inside the padded scale rows get zero scales, as the quantiser writes them.
+__device__ __forceinline__ void store_nvfp4(const Params &p, float (&v)[32], int64_t m, bool live, int32_t col,
+                                            const Nvfp4Consts &c) {
+  if (m >= p.q_rows_pad) return;
+  uint32_t s0 = 0, s1 = 0;
+  if (live) {
+    bf16r_x32(v);  // the value a bf16 output would hold
+    uint2 c0, c1;
+    s0 = nvfp4_group(v, c, c0);
+    s1 = nvfp4_group(v + 16, c, c1);
+    *reinterpret_cast<uint4 *>(p.q_codes + m * p.q_ld + col / 2) = make_uint4(c0.x, c0.y, c1.x, c1.y);
+  }
+  // col % 32 == 0: groups k0 and k0 + 1 are adjacent bytes of the 128x4 layout
+  *reinterpret_cast<uint16_t *>(p.q_sf + sf_offset(m, col / 16, p.q_ktiles)) = static_cast<uint16_t>(s0 | (s1 << 8));
+}
 
 // y = bf16(alpha * acc) then bf16(y + bias): mm_fp4's output, then the
 // separate bias add of NVFP4Execution.linear (h3_nvfp4_linear.py:139).
@@ -88,7 +116,7 @@ __device__ __forceinline__ void alpha_bias(float (&v)[32], float alpha, const __
   }
 }
 
-template <int EPI>
+template <int EPI, bool QUANT = false>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     nvfp4_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                       const __grid_constant__ CUtensorMap tmB2, const __grid_constant__ CUtensorMap tmSFA,
@@ -276,6 +304,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     int box = 0;
     float alpha = __ldg(p.alpha);
     if (p.alpha_div != nullptr) alpha = __fdiv_rn(alpha, __ldg(p.alpha_div));
+    const Nvfp4Consts qc = nvfp4_consts(QUANT ? __ldg(p.q_gsf) : 1.0f);
     const uint32_t tfree_leader = map_to_rank(smem_u32(tfree_bar), 0);
     // chunks of 32 columns per tile; SWIGLU pairs value chunk c with gate chunk c + 4
     constexpr int kChunks = kSwiglu ? BN_HALF / 32 : BN / 32;
@@ -354,7 +383,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 #pragma unroll
             for (int j = 0; j < 32; ++j) v[j] = 0.0f;
           }
-          store_box<EPI_BOXES>(warp_smem, box, &tmOut, v, lane, f, static_cast<int32_t>(row0), 0, any_row);
+          if constexpr (QUANT)
+            store_nvfp4(p, v, m, live, f, qc);
+          else
+            store_box<EPI_BOXES>(warp_smem, box, &tmOut, v, lane, f, static_cast<int32_t>(row0), 0, any_row);
         } else {
           uint32_t r[32];
           if (i == 0) {
@@ -417,8 +449,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             for (int j = 0; j < 32; ++j) v[j] = 0.0f;
           }
           // STORE values are bf16 already (alpha_bias / the merge rounded them)
-          store_box<EPI_BOXES, false, EPI == VFB_EPI_STORE>(warp_smem, box, &tmOut, v, lane, col,
-                                                            static_cast<int32_t>(row0), plane, any_row);
+          if constexpr (QUANT)
+            store_nvfp4(p, v, m, live, col, qc);
+          else
+            store_box<EPI_BOXES, false, EPI == VFB_EPI_STORE>(warp_smem, box, &tmOut, v, lane, col,
+                                                              static_cast<int32_t>(row0), plane, any_row);
         }
       }
     }
@@ -452,10 +487,10 @@ int map_u8(CUtensorMap *map, const void *base, int64_t rows, int64_t row_bytes, 
 
 bool a16(const void *p) { return reinterpret_cast<uintptr_t>(p) % 16 == 0; }
 
-template <int EPI>
+template <int EPI, bool QUANT = false>
 int launch(const CUtensorMap &ta, const CUtensorMap &tb, const CUtensorMap &tb2, const CUtensorMap &tsa,
            const CUtensorMap &tsb, const CUtensorMap &to, const Params &p, int sms, cudaStream_t stream) {
-  auto kernel = nvfp4_gemm_kernel<EPI>;
+  auto kernel = nvfp4_gemm_kernel<EPI, QUANT>;
   // the shared-memory opt-in is a function attribute of the device's context: set it once per context
   static std::atomic<uint64_t> smem_set[kMaxAttrDevices];
   int rc = ensure_smem_optin(reinterpret_cast<const void *>(kernel), static_cast<int>(SMEM_BYTES), smem_set);
@@ -480,8 +515,11 @@ int launch(const CUtensorMap &ta, const CUtensorMap &tb, const CUtensorMap &tb2,
   return VFB_OK;
 }
 
+// quant: the result goes out as NVFP4 codes and scales (q_gsf its global
+// scale) instead of bf16 (ep->out, ldo and planes are not used).
 int nvfp4_impl(const char *fn, const void *A, const void *sfa, const void *W, const void *sfw, const float *alpha,
-               const float *alpha_div, int64_t M, int64_t N, int64_t K, const vfb_epilogue *ep, void *stream) {
+               const float *alpha_div, int64_t M, int64_t N, int64_t K, const vfb_epilogue *ep, void *stream,
+               bool quant = false, const float *q_gsf = nullptr, void *q_codes = nullptr, void *q_sf = nullptr) {
   if (ep == nullptr) return set_error(VFB_EINVAL, "%s: epilogue is NULL", fn);
   const int kind = ep->kind;
   if (kind != VFB_EPI_STORE && kind != VFB_EPI_GELU_TANH && kind != VFB_EPI_SWIGLU && kind != VFB_EPI_RESIDUAL)
@@ -490,10 +528,23 @@ int nvfp4_impl(const char *fn, const void *A, const void *sfa, const void *W, co
   if (M < 0 || N <= 0 || K <= 0 || K % 64 || N % 128 || K > (int64_t)1 << 20 || N > (int64_t)1 << 24)
     return set_error(VFB_EINVAL, "%s: need K %% 64 == 0 and N %% 128 == 0 (M=%lld N=%lld K=%lld)", fn,
                      (long long)M, (long long)N, (long long)K);
+  if (quant) {
+    const int64_t width = kind == VFB_EPI_SWIGLU ? N / 2 : N;
+    if (kind == VFB_EPI_RESIDUAL || width % 64 || (kind != VFB_EPI_SWIGLU && ep->plane_width != 0 &&
+                                                   ep->plane_width != N))
+      return set_error(VFB_EINVAL, "%s: the NVFP4 output needs a STORE, GELU_TANH or SWIGLU epilogue with one "
+                                   "plane whose width is a multiple of 64", fn);
+    for (int i = 0; i < 3; ++i)
+      if (ep->adapter[i] != nullptr) return set_error(VFB_EINVAL, "%s: no adapter merge for the NVFP4 output", fn);
+  }
   if (M == 0) return VFB_OK;
-  if (!A || !sfa || !W || !sfw || !alpha || !ep->out) return set_error(VFB_EINVAL, "%s: NULL operand", fn);
-  if (!a16(A) || !a16(W) || !a16(sfa) || !a16(sfw) || !a16(ep->out) || (ep->bias && !a16(ep->bias)) ||
-      ep->ldo % 8)
+  if (!A || !sfa || !W || !sfw || !alpha || (!quant && !ep->out))
+    return set_error(VFB_EINVAL, "%s: NULL operand", fn);
+  if (quant && (q_gsf == nullptr || q_codes == nullptr || q_sf == nullptr || !a16(q_codes) || !a16(q_sf)))
+    return set_error(VFB_EINVAL, "%s: the NVFP4 output needs its global scale and 16-byte aligned codes and "
+                                 "scales", fn);
+  if (!a16(A) || !a16(W) || !a16(sfa) || !a16(sfw) || (!quant && !a16(ep->out)) || (ep->bias && !a16(ep->bias)) ||
+      (!quant && ep->ldo % 8))
     return set_error(VFB_EINVAL, "%s: operands must be 16-byte aligned, ldo %% 8 == 0", fn);
   int sms = 0;
   int rc = check_device(&sms);
@@ -510,11 +561,11 @@ int nvfp4_impl(const char *fn, const void *A, const void *sfa, const void *W, co
   p.status = device_status_ptr();
   const int64_t a_blocks = (M + 127) / 128;  // 128-row scale blocks of the activation
   const int64_t w_blocks = N / 128;
-  CUtensorMap ta, tb, tb2, tsa, tsb, to;
+  CUtensorMap ta, tb, tb2, tsa, tsb, to{};  // `to` stays unused for the NVFP4 output
   if ((rc = map_u8(&ta, A, M, K / 2, BK_BYTES, BM, CU_TENSOR_MAP_SWIZZLE_128B)) != VFB_OK) return rc;
   if (kind == VFB_EPI_SWIGLU) {
     const int64_t F = N / 2;
-    if (F % 128 || ep->ldo < F)
+    if (F % 128 || (!quant && ep->ldo < F))
       return set_error(VFB_EINVAL, "%s: SWIGLU needs the packed N = 2F with F %% 128 == 0 and ldo >= F", fn);
     p.F = static_cast<int32_t>(F);
     p.plane_width = static_cast<int32_t>(F);
@@ -523,7 +574,12 @@ int nvfp4_impl(const char *fn, const void *A, const void *sfa, const void *W, co
     if ((rc = map_u8(&tb2, static_cast<const uint8_t *>(W) + F * (K / 2), F, K / 2, BK_BYTES, BN_HALF,
                      CU_TENSOR_MAP_SWIZZLE_128B)) != VFB_OK)
       return rc;
-    if ((rc = make_map_out(&to, ep->out, F, M, 1, ep->ldo, M * ep->ldo)) != VFB_OK) return rc;
+    if (!quant && (rc = make_map_out(&to, ep->out, F, M, 1, ep->ldo, M * ep->ldo)) != VFB_OK) return rc;
+  } else if (quant) {
+    p.plane_width = static_cast<int32_t>(N);
+    p.num_n_tiles = static_cast<int>((N + BN - 1) / BN);
+    if ((rc = map_u8(&tb, W, N, K / 2, BK_BYTES, BN_HALF, CU_TENSOR_MAP_SWIZZLE_128B)) != VFB_OK) return rc;
+    tb2 = tb;
   } else {
     if (ep->plane_width < 0 || (ep->plane_width > 0 && (ep->plane_width % 32 || N % ep->plane_width)))
       return set_error(VFB_EINVAL, "%s: plane_width must be 0 or a multiple of 32 dividing N", fn);
@@ -571,6 +627,23 @@ int nvfp4_impl(const char *fn, const void *A, const void *sfa, const void *W, co
                    CU_TENSOR_MAP_SWIZZLE_NONE)) != VFB_OK)
     return rc;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (quant) {
+    const int64_t width = kind == VFB_EPI_SWIGLU ? N / 2 : N;
+    p.q_codes = static_cast<uint8_t *>(q_codes);
+    p.q_sf = static_cast<uint8_t *>(q_sf);
+    p.q_gsf = q_gsf;
+    p.q_ld = width / 2;
+    p.q_rows_pad = (M + 127) / 128 * 128;
+    p.q_ktiles = width / 64;
+    switch (kind) {
+      case VFB_EPI_GELU_TANH:
+        return launch<VFB_EPI_GELU_TANH, true>(ta, tb, tb2, tsa, tsb, to, p, sms, s);
+      case VFB_EPI_SWIGLU:
+        return launch<VFB_EPI_SWIGLU, true>(ta, tb, tb2, tsa, tsb, to, p, sms, s);
+      default:
+        return launch<VFB_EPI_STORE, true>(ta, tb, tb2, tsa, tsb, to, p, sms, s);
+    }
+  }
   switch (kind) {
     case VFB_EPI_GELU_TANH:
       return launch<VFB_EPI_GELU_TANH>(ta, tb, tb2, tsa, tsb, to, p, sms, s);
@@ -606,4 +679,12 @@ extern "C" int vfb_nvfp4_gemm_ex(const void *A, const void *sfa, const void *W, 
                                  const float *alpha, const float *alpha_div, int64_t M, int64_t N, int64_t K,
                                  const vfb_epilogue *ep, void *stream) {
   return vfb::nvfp4_impl("vfb_nvfp4_gemm_ex", A, sfa, W, sfw, alpha, alpha_div, M, N, K, ep, stream);
+}
+
+extern "C" int vfb_nvfp4_gemm_quant(const void *A, const void *sfa, const void *W, const void *sfw,
+                                    const float *alpha, const float *alpha_div, int64_t M, int64_t N, int64_t K,
+                                    const vfb_epilogue *ep, const float *out_global_scale, void *out_codes,
+                                    void *out_sf, void *stream) {
+  return vfb::nvfp4_impl("vfb_nvfp4_gemm_quant", A, sfa, W, sfw, alpha, alpha_div, M, N, K, ep, stream, true,
+                         out_global_scale, out_codes, out_sf);
 }

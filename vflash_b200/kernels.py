@@ -438,7 +438,7 @@ def nvfp4_quantize(matrix: torch.Tensor, global_scale: torch.Tensor):
 def nvfp4_gemm(a_codes: torch.Tensor, a_sf: torch.Tensor, w_packed: torch.Tensor,
                w_scales: torch.Tensor, alpha: torch.Tensor, bias: torch.Tensor | None = None,
                planes: int = 1, *, alpha_div: torch.Tensor | None = None,
-               epilogue: Epilogue | None = None) -> torch.Tensor:
+               epilogue: Epilogue | None = None, quantize_output: torch.Tensor | None = None):
     """``bf16(alpha * A @ W^T)`` (+ bias, + epilogue) for NVFP4 operands in the 128x4 scale layout.
 
     ``alpha`` (and ``alpha_div``, when given: the GEMM uses ``alpha / alpha_div``
@@ -446,6 +446,11 @@ def nvfp4_gemm(a_codes: torch.Tensor, a_sf: torch.Tensor, w_packed: torch.Tensor
     fused step after the bias (``Epilogue`` kinds STORE with planes and LoRA
     adapters, GELU_TANH, SWIGLU over the packed ``[2F, K/2]`` weight, or
     RESIDUAL); ``bias`` / ``planes`` are the plain-store shorthand.
+
+    ``quantize_output`` (an fp32 scalar tensor, the next NVFP4 linear's input
+    scale) returns the result as ``nvfp4_quantize(result, quantize_output)``
+    would, bit for bit, without the bf16 tensor: ``(codes, scales)`` from
+    ``vfb_nvfp4_gemm_quant`` (STORE with one plane, GELU_TANH or SWIGLU).
     """
     rows, half_k = a_codes.shape
     n = w_packed.shape[0]
@@ -474,6 +479,8 @@ def nvfp4_gemm(a_codes: torch.Tensor, a_sf: torch.Tensor, w_packed: torch.Tensor
     for t in (a_sf, w_packed, w_scales, alpha, alpha_div):
         if t is not None and t.device != device:
             raise KernelInputError("NVFP4 GEMM operands must share one device")
+    if quantize_output is not None:
+        return _nvfp4_gemm_quant(a_codes, a_sf, w_packed, w_scales, alpha, alpha_div, ep, quantize_output)
     e, out = _build_epilogue(ep, rows, n, device, None)
     if rows == 0:
         return out
@@ -484,3 +491,35 @@ def nvfp4_gemm(a_codes: torch.Tensor, a_sf: torch.Tensor, w_packed: torch.Tensor
                                    k, ctypes.byref(e), _lib.stream_handle(device))
     _lib.check(rc, "vfb_nvfp4_gemm_ex")
     return out
+
+
+def _nvfp4_gemm_quant(a_codes, a_sf, w_packed, w_scales, alpha, alpha_div, ep: Epilogue, global_scale):
+    """``nvfp4_gemm`` whose result leaves the kernel as NVFP4 codes and 128x4 scales."""
+    rows, half_k = a_codes.shape
+    n = w_packed.shape[0]
+    device = a_codes.device
+    if ep.kind not in (_lib.EPI_STORE, _lib.EPI_GELU_TANH, _lib.EPI_SWIGLU) or ep.planes != 1 or ep.adapters:
+        raise KernelInputError("the NVFP4 output needs a STORE, GELU_TANH or SWIGLU epilogue with one plane")
+    width = n // 2 if ep.kind == _lib.EPI_SWIGLU else n
+    if width % 64:
+        raise KernelInputError("the NVFP4 output width must be a multiple of 64")
+    if (global_scale.dtype != torch.float32 or global_scale.numel() != 1 or global_scale.device != device):
+        raise KernelInputError("NVFP4 global scale must be an fp32 scalar on the GEMM's device")
+    e = _lib.Epilogue()
+    e.kind = ep.kind
+    if ep.bias is not None:
+        if ep.bias.dtype != BF16 or ep.bias.shape != (n,) or not ep.bias.is_contiguous():
+            raise KernelInputError("NVFP4 GEMM bias must be contiguous bf16 [N]")
+        e.bias = ep.bias.data_ptr()
+    codes = torch.empty((rows, width // 2), device=device, dtype=torch.uint8)
+    sf = torch.empty(nvfp4_sf_shape(rows, width), device=device, dtype=torch.uint8)
+    if rows == 0:
+        return codes, sf
+    lib = _lib.load()
+    with torch.cuda.device(device):
+        rc = lib.vfb_nvfp4_gemm_quant(a_codes.data_ptr(), a_sf.data_ptr(), w_packed.data_ptr(), w_scales.data_ptr(),
+                                      alpha.data_ptr(), None if alpha_div is None else alpha_div.data_ptr(), rows, n,
+                                      2 * half_k, ctypes.byref(e), global_scale.data_ptr(), codes.data_ptr(),
+                                      sf.data_ptr(), _lib.stream_handle(device))
+    _lib.check(rc, "vfb_nvfp4_gemm_quant")
+    return codes, sf

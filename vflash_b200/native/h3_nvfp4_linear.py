@@ -228,3 +228,63 @@ class NVFP4Execution:
             flat = tuple(None if a is None else a.reshape(-1, n // 3) for a in adapters)
         ep = Epilogue(bias=bias, planes=3, adapters=flat, scalings=tuple(scalings or (0.0, 0.0, 0.0)))
         return self._run(values, weight, bias, ep)
+
+    def ffn(self, values, up: NVFP4Weight, down: NVFP4Weight, *, activation="gelu_tanh", up_bias=None,
+            down_bias=None, residual=None, gate=None):
+        """The QAD FFN ``down(act(up(values)))``, optionally with a gated residual.
+
+        The same bits as ``linear(gelu_linear(values, up, up_bias), down, down_bias)``
+        (``swiglu_linear`` for ``activation="swiglu"`` over the packed ``[2F, K]``
+        up weight; ``gate_residual_linear`` when ``residual`` is given), but the
+        up GEMM's epilogue quantises its bf16 result with ``down.input_scale``
+        exactly as the down linear's quantiser would, so the intermediate never
+        exists in bf16: three launches (quantiser, up GEMM, down GEMM) and no
+        intermediate round trip through HBM.
+        """
+        if activation not in ("gelu_tanh", "swiglu"):
+            raise ValueError("NVFP4 FFN activation must be gelu_tanh or swiglu")
+        width = up.out_features // 2 if activation == "swiglu" else up.out_features
+        if activation == "swiglu" and up.out_features % 256:
+            raise ValueError("packed NVFP4 SwiGLU weight needs 2F rows with F % 128 == 0")
+        if down.in_features != width or width % 64:
+            raise ValueError("NVFP4 FFN weights differ: down.in_features must be the activation width")
+        if (values.ndim < 1 or values.shape[-1] != up.in_features
+                or values.dtype not in (torch.bfloat16, torch.float16, torch.float32)
+                or values.device != up.packed.device or down.packed.device != up.packed.device):
+            raise ValueError("NVFP4 input differs from its frozen matrix")
+        if torch.is_grad_enabled() and values.requires_grad:
+            raise ValueError("NVFP4 execution is inference-only")
+        _require_device(values.device)
+        self._check_bias(values, up_bias, up.out_features)
+        self._check_bias(values, down_bias, down.out_features)
+        n = down.out_features
+        if residual is not None and (residual.dtype != torch.bfloat16 or residual.shape != (*values.shape[:-1], n)
+                                     or residual.device != values.device):
+            raise ValueError("NVFP4 residual differs from the declared output")
+        if gate is not None and (residual is None or gate.dtype != torch.bfloat16 or gate.ndim != 2
+                                 or gate.shape[1] != n):
+            raise ValueError("NVFP4 gate must be bf16 [tokens, N] with a residual")
+        if self._ops is None:
+            self._ops = _operators()
+        if self._ops[2] is not _matmul:
+            raise ValueError("the fused NVFP4 FFN needs the native operators")
+        shape = values.shape
+        matrix = values.to(torch.bfloat16) if values.dtype == torch.float32 else values
+        matrix = matrix.reshape(-1, up.in_features)
+        if matrix.shape[0] == 0:
+            raise ValueError("NVFP4 input rows must be nonempty")
+        codes, scales = nvfp4_quantize(matrix, up.input_scale)
+        kind = _lib.EPI_SWIGLU if activation == "swiglu" else _lib.EPI_GELU_TANH
+        mid_codes, mid_scales = nvfp4_gemm(codes, scales, up.packed, up.scales, up.alpha, alpha_div=up.input_scale,
+                                           epilogue=Epilogue(kind=kind, bias=up_bias),
+                                           quantize_output=down.input_scale)
+        if residual is None:
+            ep = Epilogue(bias=down_bias)
+        else:
+            ep = Epilogue(kind=_lib.EPI_RESIDUAL, bias=down_bias, residual=residual.reshape(-1, n), gate=gate,
+                          tokens=0 if gate is None else gate.shape[0])
+        out = nvfp4_gemm(mid_codes, mid_scales, down.packed, down.scales, down.alpha, alpha_div=down.input_scale,
+                         epilogue=ep)
+        self.calls += 2
+        self.rows += 2 * matrix.shape[0]
+        return out.reshape(*shape[:-1], n)
