@@ -568,6 +568,28 @@ def other_configs(device, flush, stream, cpu_seconds: float = 0.0) -> dict:
         "unfused_ms": round(unfused_ms, 4),
         "step": "x [32760,4096] bf16, per-token scale/shift [32760,4096]: one pass (x, scale, shift "
                 "read, codes written) vs torch rms_norm + vfb_modulate + vfb_fp8_quant_rows"}
+    # the same prologue in front of an NVFP4 linear (codes 0.5 B and one
+    # scale byte per 16 elements written instead of e4m3 codes)
+    from vflash_b200.kernels import nvfp4_norm_modulate_quantize
+
+    gsf_p = torch.full((), 448.0 * 6.0 / 8.0, device=device, dtype=torch.float32)
+
+    def fused_prologue_nv():
+        nvfp4_norm_modulate_quantize(xp, nw, 1e-6, sc, sh, gsf_p)
+
+    def unfused_prologue_nv():
+        normed = torch.nn.functional.rms_norm(xp, (4096,), nw, 1e-6)
+        nvfp4_quantize(triton_strict_bf16_modulate(normed.view(1, m1, 4096), sc, sh).view(m1, 4096), gsf_p)
+
+    fused_ms = statistics.median(_timed(fused_prologue_nv, flush, stream))
+    unfused_ms = statistics.median(_timed(unfused_prologue_nv, flush, stream))
+    pbytes = m1 * 4096 * (2 + 2 + 2) + m1 * 4096 // 2 + m1 * 4096 // 16 + 4096 * 2
+    out["prologue_norm_modulate_nvfp4"] = {
+        "ms": round(fused_ms, 4), "gb_per_s": round(pbytes / (fused_ms * 1e-3) / 1e9, 1),
+        "frac_of_measured_hbm": round(pbytes / (fused_ms * 1e-3) / 1e9 / hbm, 4),
+        "unfused_ms": round(unfused_ms, 4),
+        "step": "as prologue_norm_modulate_quant, quantised to NVFP4 (vfb_nvfp4_norm_modulate_quant) vs torch "
+                "rms_norm + vfb_modulate + vfb_nvfp4_quant_rows"}
     del xp, nw, sc, sh
 
     # next-row epilogue at config 1's shape: QKV projection + per-head QK-norm +

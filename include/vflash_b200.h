@@ -313,6 +313,23 @@ VFB_API int vfb_fp8_ffn_noalloc(const void *x, int64_t M, int64_t H, int64_t ldx
 VFB_API int vfb_nvfp4_quant_rows(const void *x, int32_t dtype, int64_t M, int64_t K, int64_t ldx,
                                  const float *global_scale, void *codes, void *sf, void *stream);
 
+/* RMSNorm + AdaLN modulate + NVFP4 quantisation in one pass: the codes and
+ * scales vfb_nvfp4_quant_rows would give for the bf16 tensor
+ *   bf16(bf16(rms_norm(x) * bf16(1 + scale[t])) + shift[t]),  t = row % tokens,
+ * computed exactly as vfb_fp8_norm_modulate_quant computes it (rms_norm:
+ * src/vflash/native/h3_native_denoiser.py:231-243 with the norm weight
+ * norm_weight [K] or none; modulate: h3_fused_ops.py:52-122), so the block's
+ * norm and modulate before an NVFP4 linear cost one HBM pass.  x bf16 [M, K]
+ * (row stride ldx), scale / shift bf16 rows of K (token strides in
+ * elements, 0 for one row), global_scale the linear's input_scale (device
+ * fp32 scalar); codes [M, K/2], sf ceil128(M) * K/16 bytes (128x4, padding
+ * rows 0).  K % 64 == 0, K <= 32768; rows and weights 16-byte aligned. */
+VFB_API int vfb_nvfp4_norm_modulate_quant(const void *x, int64_t M, int64_t K, int64_t ldx,
+                                          const void *norm_weight, float eps, const void *scale,
+                                          int64_t scale_token_stride, const void *shift,
+                                          int64_t shift_token_stride, int64_t tokens,
+                                          const float *global_scale, void *codes, void *sf, void *stream);
+
 /* Block-scaled GEMM: replaces FlashInfer mm_fp4(codes, packed.T, scales,
  * weight_scales.T, alpha, bf16, backend="cutlass") and the bias add
  * (src/vflash/native/h3_nvfp4_linear.py:118-139):

@@ -114,6 +114,11 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     ),
     "vfb_nvfp4_quant_rows": (
         ctypes.c_int, [_vp, ctypes.c_int32, _c_int64, _c_int64, _c_int64, _vp, _vp, _vp, _vp]),
+    "vfb_nvfp4_norm_modulate_quant": (
+        ctypes.c_int,
+        [_vp, _c_int64, _c_int64, _c_int64, _vp, ctypes.c_float, _vp, _c_int64, _vp, _c_int64, _c_int64,
+         _vp, _vp, _vp, _vp],
+    ),
     "vfb_nvfp4_gemm": (
         ctypes.c_int,
         [_vp, _vp, _vp, _vp, _vp, _c_int64, _c_int64, _c_int64, _vp, _vp, _c_int64, _vp]),

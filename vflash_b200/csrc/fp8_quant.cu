@@ -21,6 +21,7 @@
 
 #include "common.cuh"
 #include "quant.cuh"
+#include "norm_modulate.cuh"
 
 namespace vfb {
 namespace {
@@ -171,21 +172,6 @@ __global__ void __launch_bounds__(kScalarThreads) fp8_quant_rows_scalar(
 // x stays in registers between the two row reductions (sum of squares, then
 // max |m|): 2 bytes read per element of x, scale and shift each, 1 written.
 // ---------------------------------------------------------------------------
-__device__ __forceinline__ float block_row_sum(float v, uint32_t *red_u32, int r_local, int t,
-                                               int warps_per_row) {
-#pragma unroll
-  for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
-  if (warps_per_row > 1) {
-    float *row_red = reinterpret_cast<float *>(red_u32) + r_local * warps_per_row;
-    if ((t & 31) == 0) row_red[t / 32] = v;
-    __syncthreads();
-    v = 0.0f;
-    for (int w = 0; w < warps_per_row; ++w) v += row_red[w];
-    __syncthreads();  // the buffer is reused by the maximum that follows
-  }
-  return v;
-}
-
 __global__ void __launch_bounds__(512) fp8_norm_modulate_quant_vec(
     const __nv_bfloat16 *__restrict__ x, int64_t M, int64_t K, int64_t ldx,
     const __nv_bfloat16 *__restrict__ norm_w, float eps, const __nv_bfloat16 *__restrict__ mod_scale,
@@ -210,21 +196,12 @@ __global__ void __launch_bounds__(512) fp8_norm_modulate_quant_vec(
       v[i] = c < nvec ? __ldcs(src + c) : make_uint4(0, 0, 0, 0);
     }
 #pragma unroll
-    for (int i = 0; i < kVecPerThread; ++i) {
-      const __nv_bfloat162 *h = reinterpret_cast<const __nv_bfloat162 *>(&v[i]);
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const float2 f = __bfloat1622float2(h[j]);
-        ss = fmaf(f.x, f.x, ss);
-        ss = fmaf(f.y, f.y, ss);
-      }
-    }
+    for (int i = 0; i < kVecPerThread; ++i) ss = sum_squares8(v[i], ss);
   }
   ss = block_row_sum(ss, red, r_local, t, warps_per_row);  // block-uniform call
   uint32_t bits = 0;
   if (live) {
-    const float mean_eps = __fadd_rn(__fdiv_rn(ss, static_cast<float>(K)), eps);
-    const float rstd = static_cast<float>(1.0 / sqrt(static_cast<double>(mean_eps)));
+    const float rstd = rms_rstd(ss, K, eps);
     const int64_t token = row % tokens;
     const uint4 *wq = reinterpret_cast<const uint4 *>(norm_w);
     const uint4 *scq = reinterpret_cast<const uint4 *>(mod_scale + token * scale_ts);
@@ -235,26 +212,7 @@ __global__ void __launch_bounds__(512) fp8_norm_modulate_quant_vec(
       if (c >= nvec) continue;
       const uint4 wv = norm_w != nullptr ? __ldg(wq + c) : make_uint4(0x3f803f80u, 0x3f803f80u,
                                                                        0x3f803f80u, 0x3f803f80u);
-      const uint4 scv = __ldg(scq + c);
-      const uint4 shv = __ldg(shq + c);
-      const __nv_bfloat162 *hx = reinterpret_cast<const __nv_bfloat162 *>(&v[i]);
-      const __nv_bfloat162 *hw = reinterpret_cast<const __nv_bfloat162 *>(&wv);
-      const __nv_bfloat162 *hs = reinterpret_cast<const __nv_bfloat162 *>(&scv);
-      const __nv_bfloat162 *hb = reinterpret_cast<const __nv_bfloat162 *>(&shv);
-      uint32_t out[4];
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const float2 fx = __bfloat1622float2(hx[j]);
-        const float2 fw = __bfloat1622float2(hw[j]);
-        const float2 fs = __bfloat1622float2(hs[j]);
-        const float2 fb = __bfloat1622float2(hb[j]);
-        const float n0 = bf16r((fx.x * rstd) * fw.x);
-        const float n1 = bf16r((fx.y * rstd) * fw.y);
-        const float m0 = bf16r(n0 * bf16r(1.0f + fs.x)) + fb.x;
-        const float m1 = bf16r(n1 * bf16r(1.0f + fs.y)) + fb.y;
-        out[j] = pack_bf16x2(m0, m1);
-      }
-      v[i] = make_uint4(out[0], out[1], out[2], out[3]);
+      v[i] = norm_modulate8(v[i], rstd, wv, __ldg(scq + c), __ldg(shq + c));
       bits = abs_bits_max8(v[i], bits);
     }
   }

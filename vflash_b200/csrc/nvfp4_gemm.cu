@@ -19,9 +19,11 @@
 // with tcgen05.cp.cta_group::2.32x128b.warpx4 and issues
 // tcgen05.mma.cta_group::2.kind::mxf4nvf4.block_scale.block16 (M = 256,
 // N = 256, K = 64).  TMEM per CTA: two 256-column accumulators overlapping by
-// 64 columns ([0,256) and [192,448)) and 48 columns of scales at [448,496);
-// the epilogue drains a tile's 64 shared columns first (reverse column order
-// for even tiles, forward for odd) and then lets the next tile's MMAs start.
+// 64 columns ([0,256) and [192,448)) and 48 columns of scales at [448,496).
+// Eight epilogue warps (two groups of four, each half of a tile's columns):
+// the group holding a tile's 64 shared columns reads them first (reverse
+// column order for even tiles, forward for odd) and then lets the next tile's
+// MMAs start.
 #include <cudaTypedefs.h>
 
 #include <atomic>
@@ -44,13 +46,18 @@ constexpr int B_STAGE = BN_HALF * BK_BYTES;            // 16 KB
 constexpr int SFA_STAGE = KB_PER_STAGE * 512;          // 2 KB: own 128 rows
 constexpr int SFB_STAGE = 2 * KB_PER_STAGE * 512;      // 4 KB: all 256 weight rows
 constexpr int STAGE_BYTES = A_STAGE + B_STAGE + SFA_STAGE + SFB_STAGE;
-constexpr int NUM_THREADS = 192;
+// Warps 0 (TMA) and 1 (MMA) plus the epilogue warps: one group of four (one
+// per TMEM lane quarter) per EPI_GROUPS, each group taking an equal share of
+// the tile's 32-column chunks.
+constexpr int EPI_GROUPS = 2;
+constexpr int EPI_WARPS = 4 * EPI_GROUPS;
+constexpr int NUM_THREADS = 64 + 32 * EPI_WARPS;
 constexpr int TMEM_COLS = 512;
 constexpr uint32_t ACC1_COL = 192;
 constexpr uint32_t SFA_COL = 448;          // 4 columns per K = 64 block
 constexpr uint32_t SFB_COL = 464;          // 8 columns per K = 64 block
 constexpr int EPI_BOXES = 2;
-constexpr int EPI_SMEM = 4 * EPI_BOXES * EPI_BOX_BYTES;
+constexpr int EPI_SMEM = EPI_WARPS * EPI_BOXES * EPI_BOX_BYTES;
 constexpr size_t SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + EPI_SMEM + 256;
 
 struct Params {
@@ -148,7 +155,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       mbar_init(&empty_bar[s], 1);
     }
     mbar_init(tfull_bar, 1);
-    mbar_init(tfree_bar, 2 * 128);
+    // every epilogue thread of both CTAs arrives once per tile: the group that
+    // holds the shared columns after reading them, the others at the tile's
+    // start (they are done with the previous tile by then)
+    mbar_init(tfree_bar, 2 * 32 * EPI_WARPS);
     mbar_init(drain_bar, 1);
     *abort_flag = 0;
     fence_mbar_init();
@@ -298,9 +308,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       __syncwarp();
     }
   } else {
-    // ---------------- epilogue (warps 2..5 of both CTAs) ----------------
-    const int q = warp & 3;
-    uint8_t *warp_smem = sEpi + q * EPI_BOXES * EPI_BOX_BYTES;
+    // ---------------- epilogue (warps 2.. of both CTAs) ----------------
+    const int q = warp & 3;              // TMEM lane quarter: this warp's 32 rows
+    const int group = (warp - 2) >> 2;   // which share of the tile's chunks
+    uint8_t *warp_smem = sEpi + (warp - 2) * EPI_BOXES * EPI_BOX_BYTES;
     int box = 0;
     float alpha = __ldg(p.alpha);
     if (p.alpha_div != nullptr) alpha = __fdiv_rn(alpha, __ldg(p.alpha_div));
@@ -308,6 +319,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     const uint32_t tfree_leader = map_to_rank(smem_u32(tfree_bar), 0);
     // chunks of 32 columns per tile; SWIGLU pairs value chunk c with gate chunk c + 4
     constexpr int kChunks = kSwiglu ? BN_HALF / 32 : BN / 32;
+    constexpr int kGroupChunks = kChunks / EPI_GROUPS;
+    static_assert(kGroupChunks >= 2, "the group holding the shared columns reads two chunks first");
     int t = 0;
     for (int tile = pair; tile < num_tiles; tile += num_pairs, ++t) {
       if (!mbar_wait(tfull_bar, t & 1, abort_flag, p.status)) break;
@@ -321,19 +334,26 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       const bool odd = t & 1;
       const uint32_t t_row = tmem_base + (odd ? ACC1_COL : 0u) + (static_cast<uint32_t>(q * 32) << 16);
       // The 64 columns the two accumulators share are the last of an even
-      // tile and the first of an odd one: both are read first, with one wait
-      // (even tiles go in reverse chunk order), and then released to the
-      // next tile's MMAs.  For SWIGLU they are gate chunks 2-3 (even) or
-      // value chunks 0-1 (odd).
+      // tile and the first of an odd one (for SWIGLU: gate chunks 2-3 or
+      // value chunks 0-1), in the last group's share or the first's.  That
+      // group reads both shared chunks first, with one wait (even tiles go in
+      // reverse chunk order), and then releases them to the next tile's MMAs;
+      // the other groups release at the tile's start.
+      const bool holder = group == (odd ? 0 : EPI_GROUPS - 1);
+      if (!holder) {
+        tc_fence_before();
+        mbar_arrive_cluster(tfree_leader);
+      }
       uint32_t held[32];  // the second shared chunk, loaded together with the first
 #pragma unroll 1
-      for (int i = 0; i < kChunks; ++i) {
-        const int c = odd ? i : (kChunks - 1 - i);
+      for (int i = 0; i < kGroupChunks; ++i) {
+        const int c = group * kGroupChunks + (odd ? i : (kGroupChunks - 1 - i));
+        const bool first_shared = holder && i == 0, second_shared = holder && i == 1;
         float v[32];
         if constexpr (kSwiglu) {
           float g[32];
           uint32_t rv[32], rg[32];
-          if (i == 0) {
+          if (first_shared) {
             // this chunk's value and gate columns and the second shared chunk
             // (gate c - 1 of an even tile, value 1 of an odd one), one wait
             tmem_ld_32x32b_x32_issue(t_row + c * 32, rv);
@@ -345,7 +365,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             tmem_ld_fence(held);
             tc_fence_before();
             mbar_arrive_cluster(tfree_leader);
-          } else if (i == 1) {
+          } else if (second_shared) {
             // the shared half was loaded with chunk 0; load the other one
             if (odd) {
               tmem_ld_32x32b_x32_issue(t_row + BN_HALF + c * 32, rg);
@@ -389,7 +409,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             store_box<EPI_BOXES>(warp_smem, box, &tmOut, v, lane, f, static_cast<int32_t>(row0), 0, any_row);
         } else {
           uint32_t r[32];
-          if (i == 0) {
+          if (first_shared) {
             // both shared chunks with one wait, then release them
             tmem_ld_32x32b_x32_issue(t_row + c * 32, r);
             tmem_ld_32x32b_x32_issue(t_row + (odd ? 1 : kChunks - 2) * 32, held);
@@ -398,7 +418,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             tmem_ld_fence(held);
             tc_fence_before();
             mbar_arrive_cluster(tfree_leader);
-          } else if (i == 1) {
+          } else if (second_shared) {
 #pragma unroll
             for (int j = 0; j < 32; ++j) r[j] = held[j];
           } else {

@@ -435,6 +435,44 @@ def nvfp4_quantize(matrix: torch.Tensor, global_scale: torch.Tensor):
     return codes, sf
 
 
+def nvfp4_norm_modulate_quantize(matrix: torch.Tensor, norm_weight: torch.Tensor | None, eps: float,
+                                 scale: torch.Tensor, shift: torch.Tensor, global_scale: torch.Tensor):
+    """RMSNorm + AdaLN modulate + NVFP4 quantisation of ``matrix`` in one pass.
+
+    The operands are those of ``quantize_fp8_norm_modulate``; ``global_scale``
+    is the NVFP4 linear's input scale.  Returns what
+    ``nvfp4_quantize(bf16(bf16(rms_norm(x) * bf16(1 + scale)) + shift),
+    global_scale)`` returns; K % 64 == 0.
+    """
+    rows, cols = _check_fp8_input(matrix)
+    device = matrix.device
+    if cols % 64:
+        raise KernelInputError("the NVFP4 prologue needs K % 64 == 0")
+    _check_modifier(scale, cols, device, "modulate scale")
+    _check_modifier(shift, cols, device, "modulate shift")
+    tokens = scale.shape[0]
+    if shift.shape[0] != tokens:
+        raise KernelInputError("modulate scale and shift cover different token counts")
+    if norm_weight is not None and (norm_weight.dtype != BF16 or norm_weight.shape != (cols,)
+                                    or not norm_weight.is_contiguous() or norm_weight.device != device):
+        raise KernelInputError("norm weight must be contiguous bf16 [K]")
+    if (global_scale.dtype != torch.float32 or global_scale.numel() != 1 or global_scale.device != device):
+        raise KernelInputError("NVFP4 global scale must be an fp32 scalar on the input's device")
+    codes = torch.empty((rows, cols // 2), device=device, dtype=torch.uint8)
+    sf = torch.empty(nvfp4_sf_shape(rows, cols), device=device, dtype=torch.uint8)
+    if rows == 0:
+        return codes, sf
+    lib = _lib.load()
+    with torch.cuda.device(device):
+        rc = lib.vfb_nvfp4_norm_modulate_quant(
+            matrix.data_ptr(), rows, cols, max(matrix.stride(0), cols),
+            None if norm_weight is None else norm_weight.data_ptr(), float(eps), scale.data_ptr(),
+            scale.stride(0) if tokens > 1 else 0, shift.data_ptr(), shift.stride(0) if tokens > 1 else 0,
+            tokens, global_scale.data_ptr(), codes.data_ptr(), sf.data_ptr(), _lib.stream_handle(device))
+    _lib.check(rc, "vfb_nvfp4_norm_modulate_quant")
+    return codes, sf
+
+
 def nvfp4_gemm(a_codes: torch.Tensor, a_sf: torch.Tensor, w_packed: torch.Tensor,
                w_scales: torch.Tensor, alpha: torch.Tensor, bias: torch.Tensor | None = None,
                planes: int = 1, *, alpha_div: torch.Tensor | None = None,

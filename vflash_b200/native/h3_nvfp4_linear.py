@@ -19,7 +19,8 @@ from functools import cache
 import torch
 
 from .. import _lib
-from ..kernels import Epilogue, nvfp4_gemm, nvfp4_quantize
+from ..kernels import Epilogue, nvfp4_gemm, nvfp4_norm_modulate_quantize, nvfp4_quantize
+from .h3_fp8_linear import NormModulate
 
 SF_LAYOUT_128x4 = "128x4"
 
@@ -97,7 +98,7 @@ class NVFP4Execution:
         self.rows = 0
         self._ops = None
 
-    def linear(self, values, weight: NVFP4Weight, bias=None):
+    def linear(self, values, weight: NVFP4Weight, bias=None, *, prologue: NormModulate | None = None):
         """``bf16(mm_fp4(nvfp4_quantize(values), W) * alpha / input_scale) + bias``.
 
         With the native operators the division of the two calibration scalars
@@ -105,10 +106,21 @@ class NVFP4Execution:
         and one GEMM launch per call); operators supplied through
         ``_operators`` (e.g. a test's fakes) get the reference's call
         sequence and arguments (h3_nvfp4_linear.py:100-139).
-        """
-        return self._run(values, weight, bias, Epilogue(bias=bias))
 
-    def _run(self, values, weight: NVFP4Weight, bias, epilogue: Epilogue, out_features=None):
+        ``prologue`` (native operators only): ``values`` is the block's
+        un-normalised hidden state, and the quantiser applies its RMSNorm and
+        AdaLN modulate first, in the same pass (``vfb_nvfp4_norm_modulate_quant``);
+        the result equals ``linear(modulated)`` bit for bit.
+        """
+        return self._run(values, weight, bias, Epilogue(bias=bias), prologue=prologue)
+
+    def _quantize_input(self, matrix, weight: NVFP4Weight, prologue):
+        if prologue is None:
+            return nvfp4_quantize(matrix, weight.input_scale)
+        return nvfp4_norm_modulate_quantize(matrix, prologue.norm_weight, prologue.eps, prologue.scale,
+                                            prologue.shift, weight.input_scale)
+
+    def _run(self, values, weight: NVFP4Weight, bias, epilogue: Epilogue, out_features=None, prologue=None):
         if (
             values.ndim < 1
             or values.shape[-1] != weight.in_features
@@ -133,7 +145,12 @@ class NVFP4Execution:
         matrix = matrix.reshape(-1, weight.in_features)
         if matrix.shape[0] == 0:
             raise ValueError("NVFP4 input rows must be nonempty")
-        codes, scales = quantize(matrix, weight.input_scale, sfLayout=layout, do_shuffle=False)
+        if prologue is not None:
+            if matmul is not _matmul or values.dtype != torch.bfloat16:
+                raise ValueError("the NVFP4 norm/modulate prologue needs the native operators and bf16 input")
+            codes, scales = self._quantize_input(matrix, weight, prologue)
+        else:
+            codes, scales = quantize(matrix, weight.input_scale, sfLayout=layout, do_shuffle=False)
         padded_rows = matrix.shape[0] + (-matrix.shape[0]) % 128
         padded_columns = (weight.in_features // 16 + 3) // 4 * 4
         if (
@@ -184,18 +201,18 @@ class NVFP4Execution:
                                  or bias.dtype != torch.bfloat16):
             raise ValueError("NVFP4 bias must match its BF16 output")
 
-    def gelu_linear(self, values, weight: NVFP4Weight, bias=None):
+    def gelu_linear(self, values, weight: NVFP4Weight, bias=None, *, prologue: NormModulate | None = None):
         """``F.gelu(linear(values, weight, bias), approximate="tanh")`` with the GELU in the epilogue."""
         self._check_bias(values, bias, weight.out_features)
-        return self._run(values, weight, bias, Epilogue(kind=_lib.EPI_GELU_TANH, bias=bias))
+        return self._run(values, weight, bias, Epilogue(kind=_lib.EPI_GELU_TANH, bias=bias), prologue=prologue)
 
-    def swiglu_linear(self, values, weight: NVFP4Weight, bias=None):
+    def swiglu_linear(self, values, weight: NVFP4Weight, bias=None, *, prologue: NormModulate | None = None):
         """Packed FFN input ``[2F, K]`` with ``value * bf16(silu(gate))`` fused (h3_fused_ops.py:185-224)."""
         if weight.out_features % 256:
             raise ValueError("packed NVFP4 SwiGLU weight needs 2F rows with F % 128 == 0")
         self._check_bias(values, bias, weight.out_features)
         return self._run(values, weight, bias, Epilogue(kind=_lib.EPI_SWIGLU, bias=bias),
-                         out_features=weight.out_features // 2)
+                         out_features=weight.out_features // 2, prologue=prologue)
 
     def gate_residual_linear(self, values, weight: NVFP4Weight, residual, gate=None, bias=None):
         """``residual + bf16(gate * linear(...))`` fused (h3_fused_ops.py:125-170); gate ``[tokens, N]``."""
@@ -210,7 +227,8 @@ class NVFP4Execution:
                       tokens=0 if gate is None else gate.shape[0])
         return self._run(values, weight, bias, ep)
 
-    def qkv_linear(self, values, weight: NVFP4Weight, bias=None, *, adapters=None, scalings=None):
+    def qkv_linear(self, values, weight: NVFP4Weight, bias=None, *, adapters=None, scalings=None,
+                   prologue: NormModulate | None = None):
         """Merged QKV: the Q, K, V planes of one GEMM, optionally each merged with its LoRA branch.
 
         ``adapters`` (three bf16 ``[..., N/3]`` tensors or None) and
@@ -227,10 +245,10 @@ class NVFP4Execution:
                 raise ValueError("QKV adapters need three branches and three scalings")
             flat = tuple(None if a is None else a.reshape(-1, n // 3) for a in adapters)
         ep = Epilogue(bias=bias, planes=3, adapters=flat, scalings=tuple(scalings or (0.0, 0.0, 0.0)))
-        return self._run(values, weight, bias, ep)
+        return self._run(values, weight, bias, ep, prologue=prologue)
 
     def ffn(self, values, up: NVFP4Weight, down: NVFP4Weight, *, activation="gelu_tanh", up_bias=None,
-            down_bias=None, residual=None, gate=None):
+            down_bias=None, residual=None, gate=None, prologue: NormModulate | None = None):
         """The QAD FFN ``down(act(up(values)))``, optionally with a gated residual.
 
         The same bits as ``linear(gelu_linear(values, up, up_bias), down, down_bias)``
@@ -239,7 +257,8 @@ class NVFP4Execution:
         up GEMM's epilogue quantises its bf16 result with ``down.input_scale``
         exactly as the down linear's quantiser would, so the intermediate never
         exists in bf16: three launches (quantiser, up GEMM, down GEMM) and no
-        intermediate round trip through HBM.
+        intermediate round trip through HBM.  ``prologue`` applies the block's
+        norm and modulate to ``values`` inside the first quantiser.
         """
         if activation not in ("gelu_tanh", "swiglu"):
             raise ValueError("NVFP4 FFN activation must be gelu_tanh or swiglu")
@@ -273,7 +292,9 @@ class NVFP4Execution:
         matrix = matrix.reshape(-1, up.in_features)
         if matrix.shape[0] == 0:
             raise ValueError("NVFP4 input rows must be nonempty")
-        codes, scales = nvfp4_quantize(matrix, up.input_scale)
+        if prologue is not None and values.dtype != torch.bfloat16:
+            raise ValueError("the NVFP4 norm/modulate prologue needs bf16 input")
+        codes, scales = self._quantize_input(matrix, up, prologue)
         kind = _lib.EPI_SWIGLU if activation == "swiglu" else _lib.EPI_GELU_TANH
         mid_codes, mid_scales = nvfp4_gemm(codes, scales, up.packed, up.scales, up.alpha, alpha_div=up.input_scale,
                                            epilogue=Epilogue(kind=kind, bias=up_bias),
