@@ -29,6 +29,7 @@ namespace {
 constexpr int kVecPerThread = 8;     // 16-byte vectors (8 bf16) per thread: 128 bytes in flight
 constexpr int kBlockThreads = 128;   // measured best with 8 vectors per thread (K = 4096 and 16384)
 constexpr int kScalarThreads = 256;  // unaligned rows: one block per row
+constexpr int kNormVecPerThread = 8; // the RMSNorm + modulate prologue: 16-byte vectors per thread
 
 // Vector path: x rows 16-byte aligned, K % 8 == 0.
 // amax_in != NULL: use these row maxima instead of reducing (a row split over
@@ -186,17 +187,17 @@ __global__ void __launch_bounds__(512) fp8_norm_modulate_quant_vec(
   const int64_t nvec = K / 8;
   const bool live = row < M;
 
-  uint4 v[kVecPerThread];
+  uint4 v[kNormVecPerThread];
   float ss = 0.0f;
   if (live) {
     const uint4 *src = reinterpret_cast<const uint4 *>(x + row * ldx);
 #pragma unroll
-    for (int i = 0; i < kVecPerThread; ++i) {
+    for (int i = 0; i < kNormVecPerThread; ++i) {
       const int64_t c = static_cast<int64_t>(i) * tpr + t;
       v[i] = c < nvec ? __ldcs(src + c) : make_uint4(0, 0, 0, 0);
     }
 #pragma unroll
-    for (int i = 0; i < kVecPerThread; ++i) ss = sum_squares8(v[i], ss);
+    for (int i = 0; i < kNormVecPerThread; ++i) ss = sum_squares8(v[i], ss);
   }
   ss = block_row_sum(ss, red, r_local, t, warps_per_row);  // block-uniform call
   uint32_t bits = 0;
@@ -207,7 +208,7 @@ __global__ void __launch_bounds__(512) fp8_norm_modulate_quant_vec(
     const uint4 *scq = reinterpret_cast<const uint4 *>(mod_scale + token * scale_ts);
     const uint4 *shq = reinterpret_cast<const uint4 *>(mod_shift + token * shift_ts);
 #pragma unroll
-    for (int i = 0; i < kVecPerThread; ++i) {
+    for (int i = 0; i < kNormVecPerThread; ++i) {
       const int64_t c = static_cast<int64_t>(i) * tpr + t;
       if (c >= nvec) continue;
       const uint4 wv = norm_w != nullptr ? __ldg(wq + c) : make_uint4(0x3f803f80u, 0x3f803f80u,
@@ -231,7 +232,7 @@ __global__ void __launch_bounds__(512) fp8_norm_modulate_quant_vec(
   const float recip = fast ? __frcp_rn(scale) : 0.0f;
   uint2 *dst = reinterpret_cast<uint2 *>(codes + row * K);
 #pragma unroll
-  for (int i = 0; i < kVecPerThread; ++i) {
+  for (int i = 0; i < kNormVecPerThread; ++i) {
     const int64_t c = static_cast<int64_t>(i) * tpr + t;
     if (c >= nvec) continue;
     uint2 q = make_uint2(0, 0);
@@ -326,7 +327,7 @@ extern "C" int vfb_fp8_norm_modulate_quant(const void *x, int64_t M, int64_t K, 
   int rc = check_device(nullptr);
   if (rc != VFB_OK) return rc;
   const int64_t nvec = K / 8;
-  int tpr = static_cast<int>((nvec + kVecPerThread - 1) / kVecPerThread);
+  int tpr = static_cast<int>((nvec + kNormVecPerThread - 1) / kNormVecPerThread);
   tpr = (tpr + 31) / 32 * 32;
   const int rows_per_block = tpr >= kBlockThreads ? 1 : kBlockThreads / tpr;
   const int threads = tpr * rows_per_block;
