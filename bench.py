@@ -25,10 +25,14 @@ over M=65520 tokens sharded across the ranks, weights streamed from the
 pinned host arena through the two-slot ring (and, for comparison, resident),
 milliseconds per denoising step as the max over ranks.
 
+``other_configs`` (2 and 3, the fused variants and
+the same-box library bars, with their own clock record) and the CPU
+baseline run at N=1 only.
+
 ``--impl reference`` times the reference's own CPU path for this layer
 (``RowFP8Execution("weight-only").linear``: dequantise to bf16, then
-``F.linear`` on the host cores) through the oracle's restatement, on a
-bounded row sample of the same workload.
+``F.linear`` on the host cores) through the oracle's restatement, over the
+same rows (``--reference-rows`` to sample fewer).
 """
 
 from __future__ import annotations
@@ -319,9 +323,11 @@ def run_gpu(args) -> None:
     # below runs dense GEMMs for tens of seconds, after which the same kernels
     # measure up to ~25 % slower under the power cap); they carry their own
     # clock record.
+    # They are single-GPU measurements: with several ranks they are skipped, so
+    # that no rank waits at a collective while rank 0 runs them alone.
     library = same_shape = None
     other = None
-    if rank == 0 and not (args.no_library_probe and args.no_other_configs):
+    if world == 1 and not (args.no_library_probe and args.no_other_configs):
         phase_clocks = ClockSampler(local_rank).start()
         time.sleep(0.5)
         phase_clocks.mark_start()
