@@ -20,7 +20,8 @@
 //               kind::f8f6f4 (M=256, N=256, K=32; four per stage), committing
 //               each stage to both CTAs' empty barriers and each finished tile to
 //               both CTAs' epilogues.
-//   warps 2-5   epilogue (2-9 for QKV_NORM_ROPE, one group of four per head):
+//   warps 2-5   epilogue (2-9 for QKV_NORM_ROPE, one group of four per head, and
+//               for SWIGLU and bf16 operands, one group per half of the tile):
 //               tcgen05.ld 32 columns at a time (warp w reads TMEM lanes
 //               32*(w%4)..+31 = tile rows), scales / bias / activation /
 //               residual / QK-norm + rotary in registers, 32 x 32 bf16 boxes
@@ -60,11 +61,16 @@ constexpr int B_STAGE_BYTES = BN_HALF * BK;  // 16 KB
 // Warps 0 (TMA) and 1 (MMA) plus the epilogue warps: four (one per TMEM lane
 // quarter) for the light epilogues, eight for QK-norm + rotary, where each
 // 256-column tile is two 128-column heads and each head gets its own four
-// warps, and eight for bf16 operands, whose products are mostly output writes
+// warps, eight for bf16 operands, whose products are mostly output writes
 // (each group of four stores one 128-column half of the tile, so two warps
-// per lane quarter hide each other's TMEM-load latency).
+// per lane quarter hide each other's TMEM-load latency), and eight for
+// SwiGLU, whose precise silu (expf and an IEEE divide per element) made the
+// four-warp epilogue the longer side of each tile (measured at the packed
+// FFN shape: 3.78 -> 3.28-3.33 ms for the up projection).
 template <int EPI, int OPS = OPS_E4M3>
-__host__ __device__ constexpr int epi_warps() { return EPI == VFB_EPI_QKV_NORM_ROPE || OPS == OPS_BF16 ? 8 : 4; }
+__host__ __device__ constexpr int epi_warps() {
+  return EPI == VFB_EPI_QKV_NORM_ROPE || OPS == OPS_BF16 || EPI == VFB_EPI_SWIGLU ? 8 : 4;
+}
 template <int EPI, int OPS = OPS_E4M3>
 __host__ __device__ constexpr int num_threads() { return 64 + 32 * epi_warps<EPI, OPS>(); }
 constexpr int TMEM_COLS = 512;
@@ -456,7 +462,8 @@ __global__ void __launch_bounds__(num_threads<EPI, OPS>(), 1)
       } else if (EPI == VFB_EPI_SWIGLU) {
         const int32_t F = ep.plane_width;
 #pragma unroll 1
-        for (int c = 0; c < BN_HALF / 32; ++c) {
+        for (int cc = 0; cc < BN_HALF / 64; ++cc) {
+          const int c = group * (BN_HALF / 64) + cc;  // each group of four: half of the value/gate chunk pairs
           const int32_t f = n_tile * BN_HALF + c * 32;
           if (f >= F) break;  // warp-uniform
           float v[32], g[32];
