@@ -331,12 +331,12 @@ def run_gpu(args) -> None:
         phase_clocks = ClockSampler(local_rank).start()
         time.sleep(0.5)
         phase_clocks.mark_start()
-        if not args.no_library_probe:
-            library = library_fp8_probe(device)
-            same_shape = library_same_shape(device, flush, stream)
         if not args.no_other_configs:
             other = other_configs(device, flush, stream,
                                   0.0 if args.no_cpu_baseline else min(args.cpu_seconds, 10.0))
+        if not args.no_library_probe:
+            library = library_fp8_probe(device)
+            same_shape = library_same_shape(device, flush, stream)
         phase_clocks.mark_end()
         phase_clocks.stop()
         if other is not None:
@@ -546,6 +546,133 @@ def other_configs(device, flush, stream, cpu_seconds: float = 0.0) -> dict:
                                         {"step": "quantiser + GEMM + bias"})
     del x, wc, ws, b
 
+    # c2: FFN, GELU-tanh, per-token requant of the intermediate, residual:
+    # vfb_fp8_ffn (quantiser, up GEMM + GELU, requantiser, down GEMM + residual;
+    # per-launch times from the same chain issued step by step) and, for
+    # comparison, vfb_fp8_ffn_one_kernel (the three steps after the quantiser
+    # in one persistent launch)
+    from vflash_b200.kernels import fp8_ffn
+
+    m, h, f = 32760, 4096, 16384
+    x = seeded(m, h, 1002)
+    up, ups = quantize_fp8_rows(seeded(f, h, 2020, std=0.02), pad_to=1)
+    down, downs = quantize_fp8_rows(seeded(h, f, 2021, std=0.02), pad_to=1)
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(5)]
+    ffn_flop = 2.0 * m * f * h * 2
+
+    def c2_ffn():
+        fp8_ffn(x, up, ups, down, downs, activation=_lib.EPI_GELU_TANH, residual=x)
+
+    def c2_one_kernel():
+        fp8_ffn(x, up, ups, down, downs, activation=_lib.EPI_GELU_TANH, residual=x, one_kernel=True)
+
+    def c2_chain():
+        ev[0].record(stream)
+        c, s = quantize_fp8_rows(x)
+        ev[1].record(stream)
+        mid = fp8_gemm(c, s, m, up, ups, Epilogue(kind=_lib.EPI_GELU_TANH))
+        ev[2].record(stream)
+        mc, ms_ = quantize_fp8_rows(mid)
+        ev[3].record(stream)
+        fp8_gemm(mc, ms_, m, down, downs, Epilogue(kind=_lib.EPI_RESIDUAL, residual=x))
+        ev[4].record(stream)
+
+    ffn_ms = _timed(c2_ffn, flush, stream)
+    one_kernel_ms = statistics.median(_timed(c2_one_kernel, flush, stream))
+    _timed(c2_chain, flush, stream, reps=10, warmup=3)
+    parts = [ev[i].elapsed_time(ev[i + 1]) for i in range(4)]
+    chain = _chain_output(x, up, ups, down, downs, m)
+    same = bool(torch.equal(fp8_ffn(x, up, ups, down, downs, activation=_lib.EPI_GELU_TANH, residual=x), chain)
+                and torch.equal(fp8_ffn(x, up, ups, down, downs, activation=_lib.EPI_GELU_TANH, residual=x,
+                                        one_kernel=True), chain))
+    del chain
+    out["c2_fp8_ffn_gelu"] = summary(
+        ffn_ms, ffn_flop, fp8_peak,
+        {"step": "vfb_fp8_ffn: quant X, up GEMM + GELU-tanh epilogue, per-token requant of the bf16 "
+                 "intermediate, down GEMM + residual epilogue (one C call, four launches)",
+         "last_step_ms": {"quant_x": round(parts[0], 4), "up_gemm_gelu": round(parts[1], 4),
+                          "requant_mid": round(parts[2], 4), "down_gemm_residual": round(parts[3], 4)},
+         "one_kernel_ms": round(one_kernel_ms, 4),
+         "one_kernel_tflops": round(ffn_flop / (one_kernel_ms * 1e-3) / 1e12, 1),
+         "equal_bits": same})
+    del up, ups
+
+    # c2 SwiGLU variant (the reference model's packed FFN input [2F, H]) through
+    # the public fused entry point RowFP8Execution.ffn
+    from vflash_b200.native.h3_fp8_linear import RowFP8Execution
+
+    packed, packeds = quantize_fp8_rows(seeded(2 * f, h, 2022, std=0.02), pad_to=1)
+    execution = RowFP8Execution("w8a8")
+
+    def c2_swiglu():
+        execution.ffn(x, packed, packeds, down, downs, activation="swiglu", residual=x)
+
+    ms = _timed(c2_swiglu, flush, stream)
+    out["c2_fp8_ffn_swiglu"] = summary(
+        ms, 2.0 * m * (2 * f) * h + 2.0 * m * f * h, fp8_peak,
+        {"step": "RowFP8Execution.ffn(activation='swiglu'): quant X, packed up GEMM [2F,H] with "
+                 "value * bf16(silu(gate)), requant, down GEMM + residual"})
+    del x, packed, packeds, down, downs
+
+    # c3: NVFP4 linear, M = 32760, K = 4096, N in {4096, 16384}
+    x = seeded(32760, 4096, 1003)
+    gsf_x = (448.0 * 6.0 / x.float().abs().max()).reshape(())
+    for n in (4096, 16384):
+        w = seeded(n, 4096, 2030 + n, std=0.02)
+        gsf_w = (448.0 * 6.0 / w.float().abs().max()).reshape(())
+        wp, wsc = nvfp4_quantize(w, gsf_w)
+        wsc = wsc.view(n, 4096 // 16)
+        alpha = ((1.0 / gsf_w) / gsf_x).to(torch.float32)
+
+        # the GEMM's share is read from the same timed calls (and clocks) as the step
+        ms, gemm_part = _timed_split(lambda: nvfp4_quantize(x, gsf_x),
+                                     lambda q: nvfp4_gemm(q[0], q[1], wp, wsc, alpha), flush, stream)
+        gemm_ms = statistics.median(gemm_part)
+        flop = 2.0 * 32760 * n * 4096
+        out[f"c3_nvfp4_n{n}"] = summary(ms, flop, fp4_peak, {
+            "step": "NVFP4 quantiser + block-scaled GEMM",
+            "gemm_only_ms": round(gemm_ms, 4),
+            "gemm_only_tflops": round(flop / (gemm_ms * 1e-3) / 1e12, 1),
+            "gemm_frac_of_peak": round(flop / (gemm_ms * 1e-3) / 1e12 / fp4_peak, 4)})
+        out[f"c3_nvfp4_n{n}"]["library_flashinfer"] = flashinfer_nvfp4(x, gsf_x, wp, wsc, alpha, flop, fp4_peak,
+                                                                       flush, stream)
+        if n == 4096 and cpu_seconds > 0:
+            ac, asf = nvfp4_quantize(x, gsf_x)
+            out["c3_nvfp4_n4096"]["cpu_baseline"] = nvfp4_cpu_baseline(ac, asf, wp, wsc, alpha, cpu_seconds)
+    del x
+    # QAD-style NVFP4 FFN at config 2's shape (H 4096, F 16384, GELU-tanh):
+    # NVFP4Execution.ffn, whose up GEMM writes the intermediate as NVFP4 codes
+    # for the down linear, against the unfused linear(gelu_linear(...)) chain
+    from vflash_b200.native.h3_nvfp4_linear import NVFP4Execution, NVFP4Weight
+
+    m, h, f = 32760, 4096, 16384
+    x = seeded(m, h, 1004)
+
+    def nv_weight(rows, cols, seed, input_scale):
+        w = seeded(rows, cols, seed, std=0.02)
+        gw = (448.0 * 6.0 / w.float().abs().max()).reshape(())
+        packed, scales = nvfp4_quantize(w, gw)
+        return NVFP4Weight(packed, scales.view(rows, cols // 16).contiguous(), (1.0 / gw).to(torch.float32),
+                           input_scale.to(torch.float32))
+
+    engine = NVFP4Execution()
+    up = nv_weight(f, h, 2040, (448.0 * 6.0 / x.float().abs().max()).reshape(()))
+    mid = engine.gelu_linear(x, up)
+    down = nv_weight(h, f, 2041, (448.0 * 6.0 / mid.float().abs().max()).reshape(()))
+    del mid
+    fused_ms = statistics.median(_timed(lambda: engine.ffn(x, up, down), flush, stream))
+    unfused_ms = statistics.median(_timed(lambda: engine.linear(engine.gelu_linear(x, up), down), flush, stream))
+    same = bool(torch.equal(engine.ffn(x, up, down), engine.linear(engine.gelu_linear(x, up), down)))
+    ffn_flop = 4.0 * m * h * f
+    out["c2_shape_nvfp4_ffn_gelu"] = {
+        "ms": round(fused_ms, 4), "tflops": round(ffn_flop / (fused_ms * 1e-3) / 1e12, 1),
+        "frac_of_peak": round(ffn_flop / (fused_ms * 1e-3) / 1e12 / fp4_peak, 4),
+        "unfused_ms": round(unfused_ms, 4), "equal_bits": same,
+        "step": "NVFP4Execution.ffn (quantiser, up GEMM + GELU-tanh writing NVFP4 codes, down GEMM) vs "
+                "linear(gelu_linear(x, up), down) (the bf16 intermediate round-trips and is quantised again)"}
+    del x, up, down
+    # --- the next-row fusions, after the BASELINE configurations (which run
+    # first, in the GPU state closest to the headline's) ---
     # next-row prologue at config 1's shape: RMSNorm + AdaLN modulate (per-token
     # scale / shift) + per-token e4m3 quantisation, fused vs the three launches
     from vflash_b200.kernels import quantize_fp8_norm_modulate
@@ -694,131 +821,6 @@ def other_configs(device, flush, stream, cpu_seconds: float = 0.0) -> dict:
                 "QKV epilogue; vs planar QKV then per branch cuBLAS linear(linear(x, down), up) * s + add"}
     del xq, wq, wqs, rc, rs, ang, residuals
 
-    # c2: FFN, GELU-tanh, per-token requant of the intermediate, residual:
-    # vfb_fp8_ffn (quantiser, up GEMM + GELU, requantiser, down GEMM + residual;
-    # per-launch times from the same chain issued step by step) and, for
-    # comparison, vfb_fp8_ffn_one_kernel (the three steps after the quantiser
-    # in one persistent launch)
-    from vflash_b200.kernels import fp8_ffn
-
-    m, h, f = 32760, 4096, 16384
-    x = seeded(m, h, 1002)
-    up, ups = quantize_fp8_rows(seeded(f, h, 2020, std=0.02), pad_to=1)
-    down, downs = quantize_fp8_rows(seeded(h, f, 2021, std=0.02), pad_to=1)
-    ev = [torch.cuda.Event(enable_timing=True) for _ in range(5)]
-    ffn_flop = 2.0 * m * f * h * 2
-
-    def c2_ffn():
-        fp8_ffn(x, up, ups, down, downs, activation=_lib.EPI_GELU_TANH, residual=x)
-
-    def c2_one_kernel():
-        fp8_ffn(x, up, ups, down, downs, activation=_lib.EPI_GELU_TANH, residual=x, one_kernel=True)
-
-    def c2_chain():
-        ev[0].record(stream)
-        c, s = quantize_fp8_rows(x)
-        ev[1].record(stream)
-        mid = fp8_gemm(c, s, m, up, ups, Epilogue(kind=_lib.EPI_GELU_TANH))
-        ev[2].record(stream)
-        mc, ms_ = quantize_fp8_rows(mid)
-        ev[3].record(stream)
-        fp8_gemm(mc, ms_, m, down, downs, Epilogue(kind=_lib.EPI_RESIDUAL, residual=x))
-        ev[4].record(stream)
-
-    ffn_ms = _timed(c2_ffn, flush, stream)
-    one_kernel_ms = statistics.median(_timed(c2_one_kernel, flush, stream))
-    _timed(c2_chain, flush, stream, reps=10, warmup=3)
-    parts = [ev[i].elapsed_time(ev[i + 1]) for i in range(4)]
-    chain = _chain_output(x, up, ups, down, downs, m)
-    same = bool(torch.equal(fp8_ffn(x, up, ups, down, downs, activation=_lib.EPI_GELU_TANH, residual=x), chain)
-                and torch.equal(fp8_ffn(x, up, ups, down, downs, activation=_lib.EPI_GELU_TANH, residual=x,
-                                        one_kernel=True), chain))
-    del chain
-    out["c2_fp8_ffn_gelu"] = summary(
-        ffn_ms, ffn_flop, fp8_peak,
-        {"step": "vfb_fp8_ffn: quant X, up GEMM + GELU-tanh epilogue, per-token requant of the bf16 "
-                 "intermediate, down GEMM + residual epilogue (one C call, four launches)",
-         "last_step_ms": {"quant_x": round(parts[0], 4), "up_gemm_gelu": round(parts[1], 4),
-                          "requant_mid": round(parts[2], 4), "down_gemm_residual": round(parts[3], 4)},
-         "one_kernel_ms": round(one_kernel_ms, 4),
-         "one_kernel_tflops": round(ffn_flop / (one_kernel_ms * 1e-3) / 1e12, 1),
-         "equal_bits": same})
-    del up, ups
-
-    # c2 SwiGLU variant (the reference model's packed FFN input [2F, H]) through
-    # the public fused entry point RowFP8Execution.ffn
-    from vflash_b200.native.h3_fp8_linear import RowFP8Execution
-
-    packed, packeds = quantize_fp8_rows(seeded(2 * f, h, 2022, std=0.02), pad_to=1)
-    execution = RowFP8Execution("w8a8")
-
-    def c2_swiglu():
-        execution.ffn(x, packed, packeds, down, downs, activation="swiglu", residual=x)
-
-    ms = _timed(c2_swiglu, flush, stream)
-    out["c2_fp8_ffn_swiglu"] = summary(
-        ms, 2.0 * m * (2 * f) * h + 2.0 * m * f * h, fp8_peak,
-        {"step": "RowFP8Execution.ffn(activation='swiglu'): quant X, packed up GEMM [2F,H] with "
-                 "value * bf16(silu(gate)), requant, down GEMM + residual"})
-    del x, packed, packeds, down, downs
-
-    # c3: NVFP4 linear, M = 32760, K = 4096, N in {4096, 16384}
-    x = seeded(32760, 4096, 1003)
-    gsf_x = (448.0 * 6.0 / x.float().abs().max()).reshape(())
-    for n in (4096, 16384):
-        w = seeded(n, 4096, 2030 + n, std=0.02)
-        gsf_w = (448.0 * 6.0 / w.float().abs().max()).reshape(())
-        wp, wsc = nvfp4_quantize(w, gsf_w)
-        wsc = wsc.view(n, 4096 // 16)
-        alpha = ((1.0 / gsf_w) / gsf_x).to(torch.float32)
-
-        # the GEMM's share is read from the same timed calls (and clocks) as the step
-        ms, gemm_part = _timed_split(lambda: nvfp4_quantize(x, gsf_x),
-                                     lambda q: nvfp4_gemm(q[0], q[1], wp, wsc, alpha), flush, stream)
-        gemm_ms = statistics.median(gemm_part)
-        flop = 2.0 * 32760 * n * 4096
-        out[f"c3_nvfp4_n{n}"] = summary(ms, flop, fp4_peak, {
-            "step": "NVFP4 quantiser + block-scaled GEMM",
-            "gemm_only_ms": round(gemm_ms, 4),
-            "gemm_only_tflops": round(flop / (gemm_ms * 1e-3) / 1e12, 1),
-            "gemm_frac_of_peak": round(flop / (gemm_ms * 1e-3) / 1e12 / fp4_peak, 4)})
-        out[f"c3_nvfp4_n{n}"]["library_flashinfer"] = flashinfer_nvfp4(x, gsf_x, wp, wsc, alpha, flop, fp4_peak,
-                                                                       flush, stream)
-        if n == 4096 and cpu_seconds > 0:
-            ac, asf = nvfp4_quantize(x, gsf_x)
-            out["c3_nvfp4_n4096"]["cpu_baseline"] = nvfp4_cpu_baseline(ac, asf, wp, wsc, alpha, cpu_seconds)
-    del x
-    # QAD-style NVFP4 FFN at config 2's shape (H 4096, F 16384, GELU-tanh):
-    # NVFP4Execution.ffn, whose up GEMM writes the intermediate as NVFP4 codes
-    # for the down linear, against the unfused linear(gelu_linear(...)) chain
-    from vflash_b200.native.h3_nvfp4_linear import NVFP4Execution, NVFP4Weight
-
-    m, h, f = 32760, 4096, 16384
-    x = seeded(m, h, 1004)
-
-    def nv_weight(rows, cols, seed, input_scale):
-        w = seeded(rows, cols, seed, std=0.02)
-        gw = (448.0 * 6.0 / w.float().abs().max()).reshape(())
-        packed, scales = nvfp4_quantize(w, gw)
-        return NVFP4Weight(packed, scales.view(rows, cols // 16).contiguous(), (1.0 / gw).to(torch.float32),
-                           input_scale.to(torch.float32))
-
-    engine = NVFP4Execution()
-    up = nv_weight(f, h, 2040, (448.0 * 6.0 / x.float().abs().max()).reshape(()))
-    mid = engine.gelu_linear(x, up)
-    down = nv_weight(h, f, 2041, (448.0 * 6.0 / mid.float().abs().max()).reshape(()))
-    del mid
-    fused_ms = statistics.median(_timed(lambda: engine.ffn(x, up, down), flush, stream))
-    unfused_ms = statistics.median(_timed(lambda: engine.linear(engine.gelu_linear(x, up), down), flush, stream))
-    same = bool(torch.equal(engine.ffn(x, up, down), engine.linear(engine.gelu_linear(x, up), down)))
-    ffn_flop = 4.0 * m * h * f
-    out["c2_shape_nvfp4_ffn_gelu"] = {
-        "ms": round(fused_ms, 4), "tflops": round(ffn_flop / (fused_ms * 1e-3) / 1e12, 1),
-        "frac_of_peak": round(ffn_flop / (fused_ms * 1e-3) / 1e12 / fp4_peak, 4),
-        "unfused_ms": round(unfused_ms, 4), "equal_bits": same,
-        "step": "NVFP4Execution.ffn (quantiser, up GEMM + GELU-tanh writing NVFP4 codes, down GEMM) vs "
-                "linear(gelu_linear(x, up), down) (the bf16 intermediate round-trips and is quantised again)"}
-    del x, up, down
     out["peak_note"] = ("fp8 peak = 2 x measured cuBLAS bf16 burst, fp4 peak = 4 x; nominal dense "
                         "fp8 4.5, fp4 9 PFLOP/s")
     return out
