@@ -21,7 +21,8 @@
 //               each stage to both CTAs' empty barriers and each finished tile to
 //               both CTAs' epilogues.
 //   warps 2-5   epilogue (2-9 for QKV_NORM_ROPE, one group of four per head, and
-//               for SWIGLU and bf16 operands, one group per half of the tile):
+//               for SWIGLU, one group per half of the tile; 2-17 for bf16
+//               operands, one group per quarter):
 //               tcgen05.ld 32 columns at a time (warp w reads TMEM lanes
 //               32*(w%4)..+31 = tile rows), scales / bias / activation /
 //               residual / QK-norm + rotary in registers, 32 x 32 bf16 boxes
@@ -61,28 +62,33 @@ constexpr int B_STAGE_BYTES = BN_HALF * BK;  // 16 KB
 // Warps 0 (TMA) and 1 (MMA) plus the epilogue warps: four (one per TMEM lane
 // quarter) for the light epilogues, eight for QK-norm + rotary, where each
 // 256-column tile is two 128-column heads and each head gets its own four
-// warps, eight for bf16 operands, whose products are mostly output writes
-// (each group of four stores one 128-column half of the tile, so two warps
-// per lane quarter hide each other's TMEM-load latency), and eight for
+// warps, sixteen for bf16 operands, whose products are mostly output writes
+// (each group of four stores one 64-column quarter of the tile, so four warps
+// per lane quarter hide each other's TMEM-load and store latency; eight gave
+// 0.292 ms and sixteen 0.261 ms for three rank-32 up products at config 1's
+// shape), and eight for
 // SwiGLU, whose precise silu (expf and an IEEE divide per element) made the
 // four-warp epilogue the longer side of each tile (measured at the packed
 // FFN shape: 3.78 -> 3.28-3.33 ms for the up projection).
 template <int EPI, int OPS = OPS_E4M3>
 __host__ __device__ constexpr int epi_warps() {
-  return EPI == VFB_EPI_QKV_NORM_ROPE || OPS == OPS_BF16 || EPI == VFB_EPI_SWIGLU ? 8 : 4;
+  return OPS == OPS_BF16 ? 16 : EPI == VFB_EPI_QKV_NORM_ROPE || EPI == VFB_EPI_SWIGLU ? 8 : 4;
 }
 template <int EPI, int OPS = OPS_E4M3>
 __host__ __device__ constexpr int num_threads() { return 64 + 32 * epi_warps<EPI, OPS>(); }
 constexpr int TMEM_COLS = 512;
 // Epilogue staging: per epilogue warp a ring of EPI_BOXES 32 x 32 bf16 boxes
 // (2 KB each), so TMA stores drain while the warp fills the next boxes.
-constexpr int EPI_BOXES = 4;  // with four epilogue warps; two with eight (same shared memory)
+constexpr int EPI_BOXES = 4;  // with four epilogue warps; two with eight or sixteen
 template <int EPI, int OPS = OPS_E4M3>
-__host__ __device__ constexpr int epi_boxes() { return 16 / epi_warps<EPI, OPS>(); }
-constexpr int EPI_SMEM_BYTES = 4 * EPI_BOXES * EPI_BOX_BYTES;
-static_assert(8 * 2 * EPI_BOX_BYTES == EPI_SMEM_BYTES, "eight-warp epilogue staging must fit");
-constexpr size_t SMEM_BYTES =
-    1024 + STAGES * (A_STAGE_BYTES + B_STAGE_BYTES) + EPI_SMEM_BYTES + 256;
+__host__ __device__ constexpr int epi_boxes() { return epi_warps<EPI, OPS>() > 8 ? 2 : 16 / epi_warps<EPI, OPS>(); }
+template <int EPI, int OPS = OPS_E4M3>
+__host__ __device__ constexpr int epi_smem_bytes() { return epi_warps<EPI, OPS>() * epi_boxes<EPI, OPS>() * EPI_BOX_BYTES; }
+template <int EPI, int OPS = OPS_E4M3>
+__host__ __device__ constexpr size_t smem_bytes() {
+  return 1024 + STAGES * (A_STAGE_BYTES + B_STAGE_BYTES) + epi_smem_bytes<EPI, OPS>() + 256;
+}
+static_assert(smem_bytes<VFB_EPI_STORE, OPS_BF16>() <= 227 * 1024, "the widest epilogue staging must fit");
 
 struct EpiParams {
   int32_t plane_width;  // columns per output plane (N when there is one plane)
@@ -221,7 +227,7 @@ __global__ void __launch_bounds__(num_threads<EPI, OPS>(), 1)
   uint8_t *sA = smem;
   uint8_t *sB = smem + STAGES * A_STAGE_BYTES;
   uint8_t *sEpi = sB + STAGES * B_STAGE_BYTES;
-  uint64_t *full_bar = reinterpret_cast<uint64_t *>(sEpi + EPI_SMEM_BYTES);
+  uint64_t *full_bar = reinterpret_cast<uint64_t *>(sEpi + epi_smem_bytes<EPI, OPS>());
   uint64_t *empty_bar = full_bar + STAGES;
   uint64_t *tfull_bar = empty_bar + STAGES;
   uint64_t *tempty_bar = tfull_bar + 2;
@@ -370,10 +376,11 @@ __global__ void __launch_bounds__(num_threads<EPI, OPS>(), 1)
     const int q = warp & 3;  // TMEM lane quarter this warp may access
     const EpiParams &ep = p.ep;
     constexpr int kBoxes = epi_boxes<EPI, OPS>();
-    // eight warps: the 128-column half of the tile (QKV_NORM_ROPE: the head) this warp handles
+    // which group of four warps: its share of the tile's chunks (QKV_NORM_ROPE: its head)
     const int group = (warp - 2) >> 2;
-    constexpr bool kHalves = EPI != VFB_EPI_QKV_NORM_ROPE && epi_warps<EPI, OPS>() == 8;
-    constexpr int kChunks = kHalves ? BN / 64 : BN / 32;  // 32-column chunks per warp and tile
+    // groups of four warps that split the tile's chunks (QK-norm + rotary splits by head instead)
+    constexpr int kGroups = EPI == VFB_EPI_QKV_NORM_ROPE ? 1 : epi_warps<EPI, OPS>() / 4;
+    constexpr int kChunks = BN / 32 / kGroups;  // 32-column chunks per warp and tile
     uint8_t *warp_smem = sEpi + (q + 4 * group) * kBoxes * EPI_BOX_BYTES;
     int box = 0;
     int t = 0;
@@ -483,7 +490,7 @@ __global__ void __launch_bounds__(num_threads<EPI, OPS>(), 1)
       } else {
 #pragma unroll 1
         for (int cc = 0; cc < kChunks; ++cc) {
-          const int c = kHalves ? group * kChunks + cc : cc;
+          const int c = group * kChunks + cc;
           const int32_t n = n_tile * BN + c * 32;
           if (n >= p.N) break;  // warp-uniform
           float v[32];
@@ -547,7 +554,8 @@ int launch(const CUtensorMap &a, const CUtensorMap &b, const CUtensorMap &b2, co
   auto kernel = fp8_gemm_kernel<EPI, OPS>;
   // the shared-memory opt-in is a function attribute of the device's context: set it once per context
   static std::atomic<uint64_t> smem_set[kMaxAttrDevices];
-  int rc = ensure_smem_optin(reinterpret_cast<const void *>(kernel), static_cast<int>(SMEM_BYTES), smem_set);
+  int rc = ensure_smem_optin(reinterpret_cast<const void *>(kernel), static_cast<int>(smem_bytes<EPI, OPS>()),
+                             smem_set);
   if (rc != VFB_OK) return rc;
   // Persistent grid of CTA pairs, one CTA per SM.
   const int tiles = p.num_m_tiles * p.num_n_tiles;
@@ -556,7 +564,7 @@ int launch(const CUtensorMap &a, const CUtensorMap &b, const CUtensorMap &b2, co
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(2 * pairs, 1, 1);
   cfg.blockDim = dim3(num_threads<EPI, OPS>(), 1, 1);
-  cfg.dynamicSmemBytes = SMEM_BYTES;
+  cfg.dynamicSmemBytes = smem_bytes<EPI, OPS>();
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeClusterDimension;
