@@ -195,3 +195,63 @@ def test_noalloc_row_limit_at_the_h3_ffn_shape():
     rc = lib.vfb_fp8_ffn_noalloc(None, 1383, 5376, 5376, None, None, 14336, None, None, _lib.EPI_RESIDUAL, None,
                                  None, None, 0, None, 0, 0, None, 5376, None)
     assert rc == _lib.VFB_EINVAL and "activation" in _lib.last_error()
+
+
+def test_nvfp4_output_and_prologue_entry_points_reject_bad_arguments_before_any_launch():
+    lib = _lib.load()
+    buf = ctypes.create_string_buffer(256)
+    ptr = (ctypes.addressof(buf) + 15) // 16 * 16
+    alpha = ctypes.c_float(1.0)
+    gsf = ctypes.c_float(1.0)
+
+    def quant(ep, codes=ptr, sf=ptr, n=128):
+        return lib.vfb_nvfp4_gemm_quant(ptr, ptr, ptr, ptr, ctypes.byref(alpha), None, 4, n, 64,
+                                        ctypes.byref(ep), ctypes.byref(gsf), codes, sf, None)
+
+    # the NVFP4 output: no RESIDUAL epilogue, one plane, no adapter merge
+    ep = _lib.Epilogue()
+    ep.kind = _lib.EPI_RESIDUAL
+    assert quant(ep) == _lib.VFB_EINVAL and "NVFP4 output" in _lib.last_error()
+    ep = _lib.Epilogue()
+    ep.kind, ep.plane_width = _lib.EPI_STORE, 64
+    assert quant(ep) == _lib.VFB_EINVAL and "one plane" in _lib.last_error()
+    ep = _lib.Epilogue()
+    ep.kind = _lib.EPI_GELU_TANH
+    ep.adapter[0] = ptr
+    assert quant(ep) == _lib.VFB_EINVAL and "adapter" in _lib.last_error()
+    # codes and scales present and 16-byte aligned; N % 128
+    ep = _lib.Epilogue()
+    ep.kind = _lib.EPI_GELU_TANH
+    assert quant(ep, codes=None) == _lib.VFB_EINVAL and "global scale" in _lib.last_error()
+    assert quant(ep, sf=ptr + 8) == _lib.VFB_EINVAL
+    assert quant(ep, n=192) == _lib.VFB_EINVAL and "vfb_nvfp4_gemm_quant" in _lib.last_error()
+    ep.kind = _lib.EPI_SWIGLU
+    assert quant(ep, n=128) == _lib.VFB_EINVAL and "SWIGLU" in _lib.last_error()
+
+    # norm + modulate + NVFP4 quantise: K % 64, tokens, eps, alignment
+    def prologue(k=64, ldx=64, tokens=1, eps=1e-6, x=ptr, codes=ptr):
+        return lib.vfb_nvfp4_norm_modulate_quant(x, 4, k, ldx, None, eps, ptr, 0, ptr, 0, tokens,
+                                                 ctypes.byref(gsf), codes, ptr, None)
+
+    assert prologue(k=96, ldx=96) == _lib.VFB_EINVAL and "K %" in _lib.last_error()
+    assert prologue(ldx=32) == _lib.VFB_EINVAL
+    assert prologue(tokens=0) == _lib.VFB_EINVAL
+    assert prologue(eps=-1.0) == _lib.VFB_EINVAL
+    assert prologue(x=ptr + 2) == _lib.VFB_EINVAL and "aligned" in _lib.last_error()
+    assert prologue(codes=ptr + 4) == _lib.VFB_EINVAL
+    assert prologue(x=None) == _lib.VFB_EINVAL and "NULL" in _lib.last_error()
+
+
+def test_fp8_swiglu_width_checks_come_before_the_device_probe():
+    lib = _lib.load()
+    buf = ctypes.create_string_buffer(256)
+    ptr = (ctypes.addressof(buf) + 15) // 16 * 16
+    ep = _lib.Epilogue()
+    ep.kind, ep.out, ep.ldo = _lib.EPI_SWIGLU, ptr, 64
+    # packed width 2F with F % 32: N = 96 is refused
+    assert lib.vfb_fp8_gemm(ptr, 64, ptr, ptr, 64, ptr, 4, 96, 64, ctypes.byref(ep), None) == _lib.VFB_EINVAL
+    assert "SWIGLU" in _lib.last_error()
+    # ldo below F = 64
+    ep.ldo = 32
+    assert lib.vfb_fp8_gemm(ptr, 64, ptr, ptr, 64, ptr, 4, 128, 64, ctypes.byref(ep), None) == _lib.VFB_EINVAL
+    assert "ldo" in _lib.last_error()

@@ -614,6 +614,9 @@ int gemm_impl(const char *fn, int ops, const void *A, int64_t lda, const float *
       (ep->wire_chunks > 0 && kind != VFB_EPI_STORE && kind != VFB_EPI_QKV_NORM_ROPE))
     return set_error(VFB_EINVAL, "%s: wire_chunks must be 0..1024, and 0 unless the epilogue is "
                                  "STORE or QKV_NORM_ROPE", fn);
+  if (kind == VFB_EPI_SWIGLU && N % 64)
+    return set_error(VFB_EINVAL, "%s: SWIGLU needs the packed width N = 2F, F %% 32 == 0", fn);
+  if (kind == VFB_EPI_SWIGLU && ep->ldo < N / 2) return set_error(VFB_EINVAL, "%s: SWIGLU output ldo < F", fn);
 
   int sm_count = 0;
   int rc = check_device(&sm_count);
@@ -636,10 +639,7 @@ int gemm_impl(const char *fn, int ops, const void *A, int64_t lda, const float *
   if (rc != VFB_OK) return rc;
 
   if (kind == VFB_EPI_SWIGLU) {
-    if (N % 64)
-      return set_error(VFB_EINVAL, "%s: SWIGLU needs the packed width N = 2F, F %% 32 == 0", fn);
     const int64_t F = N / 2;
-    if (ep->ldo < F) return set_error(VFB_EINVAL, "%s: SWIGLU output ldo < F", fn);
     e.plane_width = static_cast<int32_t>(F);
     p.num_n_tiles = static_cast<int>((F + BN_HALF - 1) / BN_HALF);
     if ((rc = make_map_out(&to, ep->out, F, M, 1, ep->ldo, M * ep->ldo)) != VFB_OK) return rc;

@@ -548,6 +548,8 @@ int nvfp4_impl(const char *fn, const void *A, const void *sfa, const void *W, co
   if (M < 0 || N <= 0 || K <= 0 || K % 64 || N % 128 || K > (int64_t)1 << 20 || N > (int64_t)1 << 24)
     return set_error(VFB_EINVAL, "%s: need K %% 64 == 0 and N %% 128 == 0 (M=%lld N=%lld K=%lld)", fn,
                      (long long)M, (long long)N, (long long)K);
+  if (kind == VFB_EPI_SWIGLU && ((N / 2) % 128 || (!quant && ep->ldo < N / 2)))
+    return set_error(VFB_EINVAL, "%s: SWIGLU needs the packed N = 2F with F %% 128 == 0 and ldo >= F", fn);
   if (quant) {
     const int64_t width = kind == VFB_EPI_SWIGLU ? N / 2 : N;
     if (kind == VFB_EPI_RESIDUAL || width % 64 || (kind != VFB_EPI_SWIGLU && ep->plane_width != 0 &&
@@ -585,8 +587,6 @@ int nvfp4_impl(const char *fn, const void *A, const void *sfa, const void *W, co
   if ((rc = map_u8(&ta, A, M, K / 2, BK_BYTES, BM, CU_TENSOR_MAP_SWIZZLE_128B)) != VFB_OK) return rc;
   if (kind == VFB_EPI_SWIGLU) {
     const int64_t F = N / 2;
-    if (F % 128 || (!quant && ep->ldo < F))
-      return set_error(VFB_EINVAL, "%s: SWIGLU needs the packed N = 2F with F %% 128 == 0 and ldo >= F", fn);
     p.F = static_cast<int32_t>(F);
     p.plane_width = static_cast<int32_t>(F);
     p.num_n_tiles = static_cast<int>(F / BN_HALF);
