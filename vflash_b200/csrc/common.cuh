@@ -153,6 +153,24 @@ __device__ __forceinline__ void st_shared_cluster_u32(uint32_t cluster_addr, uin
   asm volatile("st.shared::cluster.u32 [%0], %1;" ::"r"(cluster_addr), "r"(v) : "memory");
 }
 
+// ---- programmatic dependent launch ----------------------------------------
+// The GEMMs are launched with programmatic stream serialisation: one may be
+// scheduled while the kernel before it in the stream (the quantiser that wrote
+// its A operand and row scales) is still running, set up its barriers and
+// TMEM, and then wait here.  The wait returns once every prerequisite grid has
+// completed and its memory operations are visible to this grid; for a kernel
+// launched without the attribute it returns at once.  Every thread waits
+// before it touches global memory that an earlier kernel may write or read.
+__device__ __forceinline__ void grid_dependency_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+// Lets the next kernel in the stream be scheduled once every block of this
+// grid has issued it (or exited).  Only a kernel launched with programmatic
+// serialisation is affected, and it still waits in grid_dependency_wait() for
+// this grid to complete, so a block may issue it before writing anything.
+__device__ __forceinline__ void grid_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // ---- TMA ------------------------------------------------------------------
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap *map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");

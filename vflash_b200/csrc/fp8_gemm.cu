@@ -269,6 +269,7 @@ __global__ void __launch_bounds__(num_threads<EPI, OPS>(), 1)
   cluster_sync();  // the peer's barriers are initialised before any remote arrival
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  grid_dependency_wait();  // the previous kernel's outputs (A, its scales) are complete
 
   const int num_tiles = p.num_m_tiles * p.num_n_tiles;
 
@@ -566,13 +567,16 @@ int launch(const CUtensorMap &a, const CUtensorMap &b, const CUtensorMap &b2, co
   cfg.blockDim = dim3(num_threads<EPI, OPS>(), 1, 1);
   cfg.dynamicSmemBytes = smem_bytes<EPI, OPS>();
   cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = 2;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
+  // scheduled while the previous kernel (the quantiser) finishes; waits in the kernel for its results
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = 2;
   cudaError_t err = cudaLaunchKernelEx(&cfg, kernel, a, b, b2, o, p);
   if (err != cudaSuccess)
     return set_error(VFB_ECUDA, "vfb_fp8_gemm launch: %s", cudaGetErrorString(err));

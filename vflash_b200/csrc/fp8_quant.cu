@@ -39,6 +39,7 @@ __global__ void __launch_bounds__(512) fp8_quant_rows_vec(
     const __nv_bfloat16 *__restrict__ x, int64_t M, int64_t K, int64_t ldx,
     uint8_t *__restrict__ codes, float *__restrict__ scales, int64_t M_pad, int tpr,
     const float *__restrict__ amax_in, float *__restrict__ amax_out) {
+  grid_launch_dependents();  // the GEMM reading this output may be scheduled now
   extern __shared__ uint32_t red[];  // [rows per block][warps per row] maxima (bit patterns)
   const int rows_per_block = blockDim.x / tpr;
   const int r_local = threadIdx.x / tpr;
@@ -103,6 +104,7 @@ __global__ void __launch_bounds__(kScalarThreads) fp8_quant_rows_scalar(
     const __nv_bfloat16 *__restrict__ x, int64_t M, int64_t K, int64_t ldx,
     uint8_t *__restrict__ codes, float *__restrict__ scales, int64_t M_pad,
     const float *__restrict__ amax_in, float *__restrict__ amax_out) {
+  grid_launch_dependents();  // the GEMM reading this output may be scheduled now
   __shared__ float red[kScalarThreads / 32 * 2];
   const int64_t row = blockIdx.x;
   const bool live = row < M;
@@ -178,6 +180,7 @@ __global__ void __launch_bounds__(512) fp8_norm_modulate_quant_vec(
     const __nv_bfloat16 *__restrict__ norm_w, float eps, const __nv_bfloat16 *__restrict__ mod_scale,
     int64_t scale_ts, const __nv_bfloat16 *__restrict__ mod_shift, int64_t shift_ts, int64_t tokens,
     uint8_t *__restrict__ codes, float *__restrict__ scales, int64_t M_pad, int tpr) {
+  grid_launch_dependents();  // the GEMM reading this output may be scheduled now
   extern __shared__ uint32_t red[];
   const int rows_per_block = blockDim.x / tpr;
   const int r_local = threadIdx.x / tpr;

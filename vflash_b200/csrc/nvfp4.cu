@@ -39,6 +39,7 @@ __global__ void __launch_bounds__(256) nvfp4_quant_kernel(const uint16_t *__rest
                                                           uint8_t *__restrict__ codes,
                                                           uint8_t *__restrict__ sf, int64_t rows_pad,
                                                           int64_t groups_pad) {
+  grid_launch_dependents();  // the GEMM reading this output may be scheduled now
   const Nvfp4Consts consts = nvfp4_consts(__ldg(gsf_ptr));
   const int64_t groups = K / 16;
   const int64_t ktiles = groups_pad / 4;
@@ -92,6 +93,7 @@ __global__ void __launch_bounds__(512) nvfp4_norm_modulate_quant_kernel(
     int64_t scale_ts, const __nv_bfloat16 *__restrict__ mod_shift, int64_t shift_ts, int64_t tokens,
     const float *__restrict__ gsf_ptr, uint8_t *__restrict__ codes, uint8_t *__restrict__ sf, int64_t rows_pad,
     int tpr) {
+  grid_launch_dependents();  // the GEMM reading this output may be scheduled now
   extern __shared__ uint32_t red[];
   const int rows_per_block = blockDim.x / tpr;
   const int r_local = threadIdx.x / tpr;

@@ -180,6 +180,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   cluster_sync();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  grid_dependency_wait();  // the previous kernel's outputs (A, its scales) are complete
   const int num_tiles = p.num_m_tiles * p.num_n_tiles;
   const int kstages = (p.ktiles + KB_PER_STAGE - 1) / KB_PER_STAGE;
 
@@ -523,13 +524,16 @@ int launch(const CUtensorMap &ta, const CUtensorMap &tb, const CUtensorMap &tb2,
   cfg.blockDim = dim3(NUM_THREADS, 1, 1);
   cfg.dynamicSmemBytes = SMEM_BYTES;
   cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = 2;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
+  // scheduled while the previous kernel (the quantiser) finishes; waits in the kernel for its results
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = 2;
   cudaError_t err = cudaLaunchKernelEx(&cfg, kernel, ta, tb, tb2, tsa, tsb, to, p);
   if (err != cudaSuccess) return set_error(VFB_ECUDA, "vfb_nvfp4_gemm launch: %s", cudaGetErrorString(err));
   return VFB_OK;
