@@ -15,6 +15,7 @@ pytestmark = pytest.mark.gpu
     ["ffn", "--rows", "300", "--repeats", "1"],
     ["ffn", "--rows", "300", "--repeats", "1", "--swiglu", "--one-kernel"],
     ["nvfp4_gemm", "--rows", "300", "--n", "256", "--repeats", "1"],
+    ["bf16_up", "--rows", "300", "--repeats", "1"],
 ])
 def test_profile_case_runs(argv):
     assert profile_cases.main(argv) == 0

@@ -65,7 +65,7 @@ constexpr int B_STAGE_BYTES = BN_HALF * BK;  // 16 KB
 // warps, sixteen for bf16 operands, whose products are mostly output writes
 // (each group of four stores one 64-column quarter of the tile, so four warps
 // per lane quarter hide each other's TMEM-load and store latency; eight gave
-// 0.292 ms and sixteen 0.261 ms for three rank-32 up products at config 1's
+// 0.292 ms and sixteen 0.261 ms -- 0.222 ms with one proxy fence per two boxes -- for three rank-32 up products at config 1's
 // shape), and eight for
 // SwiGLU, whose precise silu (expf and an IEEE divide per element) made the
 // four-warp epilogue the longer side of each tile (measured at the packed
@@ -487,6 +487,49 @@ __global__ void __launch_bounds__(num_threads<EPI, OPS>(), 1)
             for (int j = 0; j < 32; ++j) v[j] = 0.0f;
           }
           store_box<kBoxes>(warp_smem, box, &tmOut, v, lane, f, static_cast<int32_t>(row0), 0, any_row);
+        }
+      } else if constexpr (OPS == OPS_BF16) {
+        // Plain bf16 store (the low-rank products, bound by their output writes):
+        // this warp's two adjacent chunks are staged one after the other in its
+        // two boxes, then ONE proxy fence covers both box stores (a fence per
+        // box made the fence the kernel's main stall).
+        static_assert(kChunks == 2 && kBoxes == 2, "two chunks per warp, one box each");
+        const int c0 = group * kChunks;
+        const int32_t n = n_tile * BN + c0 * 32;
+        if (n < p.N) {  // warp-uniform
+          if (lane == 0) bulk_wait_group_read<0>();  // both boxes read by the previous tile's stores
+          __syncwarp();
+          const int sw = (lane >> 1) & 3;  // 64-byte swizzle of the 64-byte box rows
+#pragma unroll
+          for (int cc = 0; cc < 2; ++cc) {
+            float v[32];
+            tmem_ld_32x32b_x32(t_row + (c0 + cc) * 32, v);
+            if (live) {
+              bf16r_x32(v);
+            } else {
+#pragma unroll
+              for (int j = 0; j < 32; ++j) v[j] = 0.0f;
+            }
+            uint4 *r = reinterpret_cast<uint4 *>(warp_smem + cc * EPI_BOX_BYTES + lane * 64);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              uint4 w;
+              w.x = pack_exact_bf16x2(v[8 * j + 0], v[8 * j + 1]);
+              w.y = pack_exact_bf16x2(v[8 * j + 2], v[8 * j + 3]);
+              w.z = pack_exact_bf16x2(v[8 * j + 4], v[8 * j + 5]);
+              w.w = pack_exact_bf16x2(v[8 * j + 6], v[8 * j + 7]);
+              r[j ^ sw] = w;
+            }
+          }
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0 && any_row) {
+            const uint64_t policy = l2_policy_evict_first();  // final outputs, as store_box
+            tma_store_3d_hint(&tmOut, warp_smem, n, static_cast<int32_t>(row0), 0, policy);
+            if (n + 32 < p.N)
+              tma_store_3d_hint(&tmOut, warp_smem + EPI_BOX_BYTES, n + 32, static_cast<int32_t>(row0), 0, policy);
+            bulk_commit_group();
+          }
         }
       } else {
 #pragma unroll 1

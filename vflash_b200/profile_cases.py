@@ -10,11 +10,13 @@ device error or the output is not finite::
     python -m vflash_b200.profile_cases fp8_gemm_gelu --rows 8192
     python -m vflash_b200.profile_cases ffn --rows 8192 [--swiglu] [--one-kernel]
     python -m vflash_b200.profile_cases nvfp4_gemm --rows 8192 --n 4096
+    python -m vflash_b200.profile_cases bf16_up --rows 32760
 
 Shapes other than the row count are those of the benchmark configurations:
 the merged QKV projection (N = 12288, K = 4096), the FFN (H = 4096,
-F = 16384; ``fp8_gemm_gelu`` is its up projection alone) and the NVFP4
-linear (K = 4096).
+F = 16384; ``fp8_gemm_gelu`` is its up projection alone), the NVFP4
+linear (K = 4096) and a rank-32 low-rank up product (bf16, K = 32,
+N = 4096).
 """
 
 from __future__ import annotations
@@ -25,7 +27,7 @@ import sys
 import torch
 
 from . import _lib
-from .kernels import Epilogue, fp8_ffn, fp8_gemm, nvfp4_gemm, nvfp4_quantize, quantize_fp8_rows
+from .kernels import Epilogue, bf16_gemm, fp8_ffn, fp8_gemm, nvfp4_gemm, nvfp4_quantize, quantize_fp8_rows
 
 
 def _seeded(rows: int, cols: int, seed: int, std: float, device) -> torch.Tensor:
@@ -69,6 +71,12 @@ def run(case: str, rows: int, repeats: int, n: int = 4096, swiglu: bool = False,
         ac, asf = nvfp4_quantize(x, gsf_x)
         for _ in range(repeats):
             y = nvfp4_gemm(ac, asf, wp, wsc.view(n, 4096 // 16), alpha)
+    elif case == "bf16_up":
+        # a low-rank adapter's up product: [rows, 32] x [4096, 32]^T, bound by its output writes
+        lo = _seeded(rows, 32, 1, 1.0, device)
+        up = _seeded(4096, 32, 2, 0.02, device)
+        for _ in range(repeats):
+            y = bf16_gemm(lo, up)
     else:
         raise ValueError(f"unknown case {case!r}")
     torch.cuda.synchronize(device)
@@ -77,7 +85,7 @@ def run(case: str, rows: int, repeats: int, n: int = 4096, swiglu: bool = False,
 
 def main(argv=None) -> int:
     parser = argparse.ArgumentParser(description=__doc__.split("\n\n")[0])
-    parser.add_argument("case", choices=["fp8_gemm", "fp8_gemm_gelu", "ffn", "nvfp4_gemm"])
+    parser.add_argument("case", choices=["fp8_gemm", "fp8_gemm_gelu", "ffn", "nvfp4_gemm", "bf16_up"])
     parser.add_argument("--rows", type=int, default=4096)
     parser.add_argument("--n", type=int, default=4096, help="NVFP4 output features")
     parser.add_argument("--repeats", type=int, default=3)
