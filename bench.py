@@ -1,6 +1,6 @@
 """Benchmark of the B200 FP8 linear hot path (one JSON line on rank 0).
 
-Workload (N=1 and per rank at N>1): BASELINE config 1, the merged QKV FP8
+Workload (N=1 and per rank at N>1): benchmark config 1, the merged QKV FP8
 projection of one H3-style block — X bf16 [32760, 4096] (N(0,1) with 0.1 %
 x20 outliers), W_qkv e4m3 [12288, 4096] (N(0,0.02), per-output-row scales),
 bias bf16 [12288], output Q, K, V bf16 [32760, 32, 128].  One step = the
@@ -20,12 +20,12 @@ region: ``HostRowPipeline`` around ``RowFP8Execution("w8a8").qkv_linear``
 (row chunks whose copies in, compute and copies out overlap); the
 ``unpipelined`` entry is one whole-tensor copy in, the linear, one copy out.
 
-``stack_c4`` is BASELINE config 4 on every rank: 48 blocks of FP8 linears
+``stack_c4`` is benchmark config 4 on every rank: 48 blocks of FP8 linears
 over M=65520 tokens sharded across the ranks, weights streamed from the
 pinned host arena through the two-slot ring (and, for comparison, resident),
 milliseconds per denoising step as the max over ranks.
 
-``other_configs`` (2 and 3, the fused variants and
+``other_configs`` (benchmark configs 0, 2 and 3, the fused variants and
 the same-box library bars, with their own clock record) and the CPU
 baseline run at N=1 only.
 
@@ -151,7 +151,7 @@ class ClockSampler:
 
 
 def synthetic_workload(device: torch.device, rank: int, M: int):
-    """Seeded inputs of BASELINE config 1 (seeds X 1001, W 2010, bias 3001; offset by rank)."""
+    """Seeded inputs of benchmark config 1 (seeds X 1001, W 2010, bias 3001; offset by rank)."""
     gen = torch.Generator().manual_seed(1001 + 97 * rank)
     x = torch.randn(M, K, generator=gen)
     count = round(0.001 * M * K)
@@ -507,7 +507,7 @@ def nvfp4_cpu_baseline(ac, asf, wp, wsc, alpha, seconds: float) -> dict:
 
 
 def other_configs(device, flush, stream, cpu_seconds: float = 0.0) -> dict:
-    """BASELINE configs 0, 2 and 3 on one GPU: seeded synthetic inputs, 10 warm-up calls, median of 50
+    """benchmark configs 0, 2 and 3 on one GPU: seeded synthetic inputs, 10 warm-up calls, median of 50
     timed calls with L2 flushed before each."""
     from vflash_b200 import _lib
     from vflash_b200.kernels import Epilogue, fp8_gemm, nvfp4_gemm, nvfp4_quantize, quantize_fp8_rows
@@ -671,7 +671,7 @@ def other_configs(device, flush, stream, cpu_seconds: float = 0.0) -> dict:
         "step": "NVFP4Execution.ffn (quantiser, up GEMM + GELU-tanh writing NVFP4 codes, down GEMM) vs "
                 "linear(gelu_linear(x, up), down) (the bf16 intermediate round-trips and is quantised again)"}
     del x, up, down
-    # --- the next-row fusions, after the BASELINE configurations (which run
+    # --- the next-row fusions, after the benchmark configurations (which run
     # first, in the GPU state closest to the headline's) ---
     # next-row prologue at config 1's shape: RMSNorm + AdaLN modulate (per-token
     # scale / shift) + per-token e4m3 quantisation, fused vs the three launches
@@ -1153,9 +1153,9 @@ def main() -> None:
     parser.add_argument("--stack-blocks", type=int, default=STACK_BLOCKS)
     parser.add_argument("--stack-steps", type=int, default=2)
     parser.add_argument("--no-other-configs", action="store_true",
-                        help="skip the extra BASELINE config 0/2/3 measurements")
+                        help="skip the extra benchmark config 0/2/3 measurements")
     parser.add_argument("--rows", type=int, default=M,
-                        help="token rows M (default 32760 = BASELINE config 1; smaller only for profiling)")
+                        help="token rows M (default 32760 = benchmark config 1; smaller only for profiling)")
     args = parser.parse_args()
     args.warmup = max(3, args.warmup)  # the timing rules require >= 3 warm-up steps
     if args.impl == "reference":
