@@ -35,6 +35,9 @@
 // same time share one A row-block, and each band's weights are fetched from
 // DRAM once instead of once per row-block.
 // No TMA multicast is used: every CTA loads its own operands.
+// Launched with programmatic stream serialisation: setup (barriers, TMEM,
+// descriptor prefetch) may overlap the previous kernel (the quantiser), and
+// every thread waits in grid_dependency_wait() before touching global memory.
 #include <cudaTypedefs.h>
 
 #include <atomic>

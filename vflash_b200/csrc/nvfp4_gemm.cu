@@ -24,6 +24,8 @@
 // the group holding a tile's 64 shared columns reads them first (reverse
 // column order for even tiles, forward for odd) and then lets the next tile's
 // MMAs start.
+// Launched as a programmatic dependent of the previous kernel (the quantiser):
+// setup overlaps its last wave; grid_dependency_wait() precedes every global access.
 #include <cudaTypedefs.h>
 
 #include <atomic>
