@@ -9,7 +9,8 @@ It imports the reference's own CPU code and freezes its outputs:
 * ``_quantize_activation_torch`` (src/vflash/native/h3_fp8_linear.py:18-31) on
   seeded inputs, including the padding / zero-row / bf16.tiny / strided-view
   cases of the reference test tests/test_fp8_linear.py:99-120, rounding ties
-  and bf16 subnormals -> e4m3 codes and fp32 scales (bit-exact fixtures);
+  and bf16 subnormals, non-finite and signed-zero rows -> e4m3 codes and fp32
+  scales (bit-exact fixtures);
 * ``RowFP8Execution("weight-only").linear`` (h3_fp8_linear.py:88-91) on the
   reference test's fixture weights (tests/test_fp8_linear.py:13-16) and on a
   seeded mid-size case;
@@ -62,6 +63,7 @@ def outlier_matrix(rows, cols, seed):
 def main() -> None:
     parser = argparse.ArgumentParser()
     parser.add_argument("--reference-src", required=True, help="the src/ directory of a vflash checkout")
+    parser.add_argument("--out", default=str(HERE / "fp8_golden.npz"), help="where to write the fixture")
     args = parser.parse_args()
     sys.path.insert(0, args.reference_src)
     import torch
@@ -104,6 +106,19 @@ def main() -> None:
                        dtype=torch.float32).to(torch.bfloat16).reshape(2, 8)
     quant_case("subnormal", sub)
     quant_case("zeros", torch.zeros(3, 32, dtype=torch.bfloat16))
+    # non-finite and signed-zero rows: an inf makes the row's scale inf (finite values -> 0,
+    # infinities -> NaN), a NaN makes amax NaN and the scale 1, an all -0 row keeps -0 codes;
+    # the largest bf16 magnitudes give a finite scale
+    inf, nan = float("inf"), float("nan")
+    specials = torch.tensor(
+        [[1.0, inf, -2.0, 0.5] * 4,
+         [-inf, 3.0, -0.0, 1e-3] * 4,
+         [nan, 1.0, -448.0, 2.5] * 4,
+         [inf, -inf, nan, 0.0] * 4,
+         [3.3e38, -1.0, -0.0, 1e-38] * 4,
+         [-0.0] * 16],
+        dtype=torch.float32).to(torch.bfloat16)
+    quant_case("specials", specials)
 
     # weight-only linear, reference fixture weights
     codes = torch.arange(128).reshape(16, 8).to(torch.float8_e4m3fn)
@@ -166,8 +181,8 @@ def main() -> None:
         out[f"pack{chunks}_qkv"] = np.stack([bits(t) for t in qkv])
         out[f"pack{chunks}_out"] = bits(pack_qkv_reference(*qkv, chunks=chunks))
 
-    np.savez_compressed(HERE / "fp8_golden.npz", **out)
-    print(f"wrote {HERE / 'fp8_golden.npz'} with {len(out)} arrays")
+    np.savez_compressed(args.out, **out)
+    print(f"wrote {args.out} with {len(out)} arrays")
 
 
 if __name__ == "__main__":

@@ -75,6 +75,25 @@ def test_every_bf16_value_at_unit_scale_bit_exact():
     check_against_oracle(to_bf16_tensor(fp8.bf16_bits(grid), DEV))
 
 
+def test_non_finite_rows_against_the_reference(golden):
+    # Rows holding +-inf (scale inf: finite values -> signed zero codes, infinities -> NaN),
+    # NaN (scale 1) and -0, frozen from the reference's CPU quantiser.  Scales and every non-NaN
+    # code are bit-exact.  A NaN code's sign bit is the platform's: x86 arithmetic returns a
+    # negative default NaN for inf / inf and keeps a NaN operand's sign, CUDA arithmetic returns
+    # the canonical positive NaN, so the reference itself gives 0xff on the CPU where a CUDA
+    # run of the same expression gives 0x7f.  Both bytes decode to NaN; here they must sit at
+    # the same places.  A row holding both a NaN and an infinity has scale 1, and its +-inf
+    # must clamp to +-448 as in the reference (not turn into NaN).
+    x = to_bf16_tensor(golden["q_specials_x"], DEV)
+    codes, scales = quantize_fp8_rows(x)
+    got, want = codes_of(codes), golden["q_specials_codes"]
+    np.testing.assert_array_equal(scales.cpu().numpy().view(np.uint32), golden["q_specials_scales"].view(np.uint32))
+    got_nan, want_nan = (got & 0x7F) == 0x7F, (want & 0x7F) == 0x7F
+    np.testing.assert_array_equal(got_nan, want_nan)
+    np.testing.assert_array_equal(got[~got_nan], want[~want_nan])
+    assert want_nan.any()
+
+
 def test_nan_row_gets_unit_scale_like_torch():
     x = outlier_activations(4, 64, 3)
     x[2, 5] = float("nan")

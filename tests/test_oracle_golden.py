@@ -14,7 +14,7 @@ import pytest
 from oracle import epilogues as ep
 from oracle import fp8
 
-QUANT_CASES = ["outliers", "wide", "k16", "k24", "k40", "ties", "subnormal", "zeros"]
+QUANT_CASES = ["outliers", "wide", "k16", "k24", "k40", "ties", "subnormal", "zeros", "specials"]
 
 
 @pytest.mark.parametrize("name", QUANT_CASES)

@@ -173,7 +173,7 @@ struct Ffn {
         const int64_t m = base + (i0 + i) * RPI;
         if (m < p.M) {
           const float scale = row_scale_from_bits(bits[i]);
-          const bool fast = isfinite(scale);
+          const bool fast = markstein_ok(scale);
           const uint2 out = fast ? quantize8(v[i], scale, __frcp_rn(scale)) : quantize8_ieee(v[i], scale);
           *reinterpret_cast<uint2 *>(p.mid_codes + m * p.F + col0 + part * 8) = out;
         }

@@ -84,7 +84,7 @@ __global__ void __launch_bounds__(512) fp8_quant_rows_vec(
   }
   if (row >= M_pad) return;
   const float scale = live ? row_scale(amax, nan) : 1.0f;
-  const bool fast = isfinite(scale);
+  const bool fast = markstein_ok(scale);
   const float recip = fast ? __frcp_rn(scale) : 0.0f;
   uint2 *dst = reinterpret_cast<uint2 *>(codes + row * K);
 #pragma unroll
@@ -142,7 +142,7 @@ __global__ void __launch_bounds__(kScalarThreads) fp8_quant_rows_scalar(
     return;
   }
   const float scale = live ? row_scale(amax, any_nan != 0.0f) : 1.0f;
-  const bool fast = isfinite(scale);
+  const bool fast = markstein_ok(scale);
   const float recip = fast ? __frcp_rn(scale) : 0.0f;
   for (int64_t c = threadIdx.x; c < K; c += blockDim.x) {
     uint8_t q = 0;
@@ -231,7 +231,7 @@ __global__ void __launch_bounds__(512) fp8_norm_modulate_quant_vec(
   if (row >= M_pad) return;
   const float amax = __uint_as_float(m << 16);
   const float scale = live ? row_scale(amax, m > kBf16Inf) : 1.0f;
-  const bool fast = isfinite(scale);
+  const bool fast = markstein_ok(scale);
   const float recip = fast ? __frcp_rn(scale) : 0.0f;
   uint2 *dst = reinterpret_cast<uint2 *>(codes + row * K);
 #pragma unroll

@@ -37,6 +37,13 @@ __device__ __forceinline__ float div_rn_by_scale(float x, float scale, float rec
   return fmaf(-rem_neg, recip, q);
 }
 
+// Whether a row may use div_rn_by_scale.  Its remainder is inf - inf for an
+// infinite x, and a row holds an infinity only when its scale is inf (amax =
+// inf) or 1 (a NaN in the row makes amax NaN, and the reference clamps the
+// row's +-inf to +-448).  Such rows take the IEEE division, which for a scale
+// of 1 is x itself; a row of finite values gets the same bits either way.
+__device__ __forceinline__ bool markstein_ok(float scale) { return isfinite(scale) && scale != 1.0f; }
+
 // Quotient used for the codes: exact division routine for non-finite scales.
 __device__ __forceinline__ float quotient(float x, float scale, float recip, bool fast) {
   return fast ? div_rn_by_scale(x, scale, recip) : __fdiv_rn(x, scale);
